@@ -1,0 +1,155 @@
+// Shared device helpers for the ArcLLM-B200 kernels (sm_100a only).
+//
+// * mbarrier + cp.async.bulk (TMA bulk copy) wrappers used by the streaming
+//   matvec pipelines;
+// * bounded waits: every spin in these kernels gives up after
+//   kWaitLimitNs nanoseconds of %globaltimer, records ARC_DEV_ERR_TIMEOUT in
+//   the device error word and lets the kernel return, so a lost copy can
+//   never wedge the GPU;
+// * the fp16 decode used by the bit-exact dequant paths.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "arcllm_b200 kernels are written for sm_100a (B200) only"
+#endif
+
+namespace arc {
+
+// device error word bits (read and cleared by arcllm_cuda_device_error)
+enum : uint32_t {
+    ARC_DEV_ERR_TIMEOUT = 1u,      // a bounded mbarrier / flag wait gave up
+    ARC_DEV_ERR_BOUNDS = 2u,       // a kernel rejected an out-of-range index
+};
+
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// `err` is the device error word (arcllm_cuda_device_error reads it); kernels
+// receive its address as a parameter.
+__device__ __forceinline__ void raise_error(unsigned int* err, uint32_t bits) {
+    if (err) atomicOr(err, bits);
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete; false (and the device error
+// word set) if it did not within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            raise_error(err, ARC_DEV_ERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// L2 policy for weight streams: every weight byte is read once per token, so
+// let it leave L2 first and keep activations / KV resident.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// 1-D TMA bulk copy global -> this CTA's shared memory, completing `bytes`
+// transactions on `bar`.  dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Bit-level fp16 -> fp32 (normal, subnormal, inf and NaN payload preserved),
+// so dequantised values match the reference's half_to_float bit for bit.
+__device__ __forceinline__ float half_bits_to_float(uint32_t h) {
+    const uint32_t sign = (h & 0x8000u) << 16;
+    const uint32_t exp = (h >> 10) & 0x1fu;
+    uint32_t mant = h & 0x3ffu;
+    uint32_t out;
+    if (exp == 0u) {
+        if (mant == 0u) {
+            out = sign;
+        } else {
+            // subnormal: normalise (the leading one is at bit 9 - (clz - 22))
+            const int lz = __clz(mant) - 21;  // shifts to bring bit 10 set
+            mant = (mant << lz) & 0x3ffu;
+            out = sign | (uint32_t(127 - 14 - lz) << 23) | (mant << 13);
+        }
+    } else if (exp == 31u) {
+        out = sign | 0x7f800000u | (mant << 13);
+    } else {
+        out = sign | ((exp + 112u) << 23) | (mant << 13);
+    }
+    return __uint_as_float(out);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace arc

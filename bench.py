@@ -1,0 +1,492 @@
+"""ArcLLM-B200 benchmark: Q4_K/Q6_K dequant-matvec HBM throughput on B200.
+
+Headline workload (N=1 and every N): the Q6_K LM-head matvec, 152064 x 3584
+(447,068,160 weight bytes), fp32 x ~ N(0,1).  One step = one pass of the LM
+head over one activation vector.  At N>1 the rows are sharded over the ranks
+(152064/N contiguous rows each) and the fp32 logits are all-gathered with
+NCCL, so every rank ends the step with the full logits (strong scaling).
+
+Timing: W untimed warm-up steps, then K steps between barrier +
+cuda.synchronize on both sides, CUDA events on the launching stream, max
+over ranks.  The weights (447 MB) are larger than the 126 MB L2, so
+consecutive steps read them from HBM; the smaller extra configs rotate
+enough weight copies to exceed 3x L2.
+
+Printed (rank 0, one JSON line): the contract keys plus `roofline` (dominant
+kernel = the matvec; achieved = algorithmic bytes / mean kernel time vs the
+measured HBM copy bandwidth), `cpu_baseline` (the reference's own CPU
+matmul_q6_cpu timed on this host), `e2e` (the C-ABI host-IO call:
+x host->device, matvec, logits device->host, every step), `clocks`, and
+`extra` (configs 0, 1b, 2 at N=1).
+
+`--impl reference` times the reference's CPU implementation of the same
+workload (oracle/_ref, compiled from the reference sources; the restated
+oracle where that library is absent) on all host cores, and prints the
+same line with "impl": "reference".
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4_K/Q6_K matvec HBM GB/s (% of B200 peak); decode tok/s, Qwen2.5-7B shape"
+LM_ROWS, HIDDEN, FFN = 152064, 3584, 18944
+Q4B, Q6B = 144, 210
+L2_BYTES = 126 * 1024 * 1024
+
+
+def q_bytes(fmt, rows, k):
+    return rows * (k // 256) * (Q4B if fmt == "q4k" else Q6B)
+
+
+def matvec_alg_bytes(fmt, rows, k):
+    """weights + x (fp32) + y (fp32): the algorithmic bytes of one matvec"""
+    return q_bytes(fmt, rows, k) + 4 * k + 4 * rows
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def committed_traffic(name):
+    """dram bytes per launch from a committed ncu summary (profiles/*.json)"""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    return json.load(open(p)).get(name)
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            cmd = ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "50"]
+            if self.gpu_id is not None:
+                cmd += ["-i", str(self.gpu_id)]
+            self.proc = subprocess.Popen(cmd, stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.06)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [l.strip().split(",") for l in self.f.read().splitlines() if l.strip()]
+        os.unlink(self.f.name)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+                power.append(float(r[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+def gpu_smi_id(torch, local_rank):
+    try:
+        p = torch.cuda.get_device_properties(local_rank)
+        return "%08x:%02x:%02x.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            return vis.split(",")[local_rank]
+        return local_rank
+
+
+# --------------------------------------------------------------- cpu baseline
+def cpu_baseline(seconds=10.0):
+    """The reference's own matmul_q6_cpu (oracle/_ref) on a bounded sample of
+    the LM head, 1 thread (the reference's form); the restated oracle is used
+    only where the reference library is absent."""
+    import numpy as np
+
+    import oracle as O
+    rows = 8192
+    w = O.fill_q6k(rows, HIDDEN, 0x1A4D)
+    x = O.normal_f32(HIDDEN, 0x1A4E)
+    y = np.empty(rows, np.float32)
+    kind = "reference" if O.ref is not None else "port"
+    done, t0 = 0, time.perf_counter()
+    while True:
+        if O.ref is not None:
+            O.ref.ref_matmul_q6(w, HIDDEN, rows, 1, x, None, y)
+        else:
+            O.orc.orc_matmul_q6(w, HIDDEN, rows, 1, x, None, y, 1)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= 400:
+            break
+    gbs = done * matvec_alg_bytes("q6k", rows, HIDDEN) / el / 1e9
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
+            "sample": "%d passes over an 8192-row slice (%.1f MB) of the 152064x3584 Q6_K LM head, "
+                      "x fp32, 1 thread, %.1f s" % (done, q_bytes("q6k", rows, HIDDEN) / 1e6, el)}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path on all host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    import oracle as O
+    cores = os.cpu_count() or 1
+    rows = 19008  # 1/8 of the LM head per step (bounded sample)
+    w = O.fill_q6k(rows, HIDDEN, 0x2B5E)
+    x = O.normal_f32(HIDDEN, 0x2B5F)
+    y = np.empty(rows, np.float32)
+    kind = "reference" if O.ref is not None else "port"
+    rb = q_bytes("q6k", 1, HIDDEN)
+    bounds = [rows * t // cores for t in range(cores + 1)]
+
+    def part(t):
+        r0, r1 = bounds[t], bounds[t + 1]
+        if r1 <= r0:
+            return
+        wv = w[r0 * rb:r1 * rb]
+        yv = np.empty(r1 - r0, np.float32)
+        if O.ref is not None:
+            O.ref.ref_matmul_q6(wv, HIDDEN, r1 - r0, 1, x, None, yv)
+        else:
+            O.orc.orc_matmul_q6(wv, HIDDEN, r1 - r0, 1, x, None, yv, 1)
+        y[r0:r1] = yv
+
+    def step():
+        ts = [threading.Thread(target=part, args=(t,)) for t in range(cores)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    gbs = args.steps * matvec_alg_bytes("q6k", rows, HIDDEN) / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config1: Q6_K LM-head matvec 152064x3584, fp32 x; reference CPU path on a "
+                               "19008-row (1/8) sample per step", "parallelism": "%d host threads" % cores},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": "19008 rows x 3584 (55.9 MB) of the LM head per step, rows split over "
+                                   "%d threads, reference matmul_q6_cpu per row" % cores},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU arm
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extra", action="store_true", help="skip the extra configs")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args(argv)
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import numpy as np
+    import torch
+
+    import arcllm_b200 as A
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    L = A.lib()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- headline: LM head (rows sharded over ranks) ----
+    rows_per = LM_ROWS // world
+    r0 = rank * rows_per
+    rb = q_bytes("q6k", 1, HIDDEN)
+    w = torch.empty(rows_per * rb + 16, dtype=torch.uint8, device=dev)
+    A.call("arcllm_cuda_fill_q6k", C.c_void_p(w.data_ptr()), r0 * (HIDDEN // 256), rows_per * (HIDDEN // 256),
+           0x1A4D, sp)
+    # x ~ N(0,1) generated with the library's fixture stream (same as the oracle's)
+    x = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(x.data_ptr()), 0, HIDDEN, 0x1A4E, C.c_float(0.0),
+           C.c_float(1.0), sp)
+    y = torch.empty(rows_per, dtype=torch.float32, device=dev)
+    logits = torch.empty(LM_ROWS, dtype=torch.float32, device=dev)
+    wp, xp, yp = C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr())
+
+    def step():
+        st = L.arcllm_cuda_matvec(A.GGML_Q6_K, wp, rows_per, HIDDEN, xp, None, C.c_float(0.0), None, None, yp, sp)
+        if st:
+            A.check(st, "matvec")
+        if dist is not None:
+            dist.all_gather_into_tensor(logits, y)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clk = ClockSampler(gpu_smi_id(torch, local_rank))
+    clk.start()
+    time.sleep(0.1)
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for i in range(args.steps):
+        ev[i][0].record()
+        st = L.arcllm_cuda_matvec(A.GGML_Q6_K, wp, rows_per, HIDDEN, xp, None, C.c_float(0.0), None, None, yp, sp)
+        if st:
+            A.check(st, "matvec")
+        ev[i][1].record()
+        if dist is not None:
+            dist.all_gather_into_tensor(logits, y)
+    t_end.record()
+    barrier()
+    clocks = clk.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    kern_ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    bits = C.c_uint32(0)
+    A.check(L.arcllm_cuda_device_error(sp, C.byref(bits)), "device_error")
+    if dist is not None:
+        tt = torch.tensor([total_ms, kern_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms, kern_ms = float(tt[0]), float(tt[1])
+    ms_per_step = total_ms / args.steps
+    alg_total = matvec_alg_bytes("q6k", LM_ROWS, HIDDEN)
+    value = alg_total / (ms_per_step * 1e-3) / 1e9
+    alg_shard = matvec_alg_bytes("q6k", rows_per, HIDDEN)
+    achieved = alg_shard / (kern_ms * 1e-3) / 1e9
+    hbm_peak, _, peak_src = measured_peaks()
+    traffic = committed_traffic("lmhead_q6k_%d" % world)
+
+    # ---- e2e through the C-ABI host-IO entry point (rank-local shard + all-gather) ----
+    xh = torch.empty(HIDDEN, dtype=torch.float32).pin_memory()
+    xh.copy_(x.cpu())
+    yh = torch.empty(rows_per, dtype=torch.float32).pin_memory()
+    xd = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    lh = torch.empty(LM_ROWS, dtype=torch.float32).pin_memory()
+    e2e_steps = max(10, min(args.steps, 500))
+
+    def e2e_step():
+        A.check(L.arcllm_cuda_matvec_hostio(A.GGML_Q6_K, wp, rows_per, HIDDEN, C.c_void_p(xh.data_ptr()),
+                                            C.c_void_p(xd.data_ptr()), yp, C.c_void_p(yh.data_ptr()), sp),
+                "matvec_hostio")
+        if dist is not None:
+            dist.all_gather_into_tensor(logits, y)
+            lh.copy_(logits, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if dist is not None:
+        tt = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt[0])
+    e2e_val = alg_total / (e2e_ms * 1e-3) / 1e9
+    d2h = 4 * (LM_ROWS if dist is not None else rows_per)
+
+    extra = {}
+    if world == 1 and not args.no_extra:
+        extra = run_extra(A, L, torch, dev, sp, hbm_peak)
+
+    if rank == 0:
+        cpu = None if args.no_cpu or world > 1 else cpu_baseline()
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": {
+                "workload": "config1: Q6_K LM-head matvec 152064x3584 (447.07 MB packed weights), fp32 x ~ N(0,1)"
+                            + ("; rows sharded over %d GPUs + NCCL all-gather of fp32 logits" % world
+                               if world > 1 else ""),
+                "l2": "weights larger than L2 (447 MB vs 126 MB): no flush needed between steps",
+                "parallelism": "row-shard%d" % world,
+                "algorithmic_bytes_per_step": alg_total,
+            },
+            "roofline": {
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                "kernel": "matvec_stream_kernel<14,8,false> (Q6_K, 8-row groups)",
+                "kernel_ms": round(kern_ms, 5), "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+            },
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * HIDDEN,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
+                    "api": "arcllm_cuda_matvec_hostio (pinned host x in, logits out, stream sync)"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        if extra:
+            line["extra"] = extra
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_extra(A, L, torch, dev, sp, hbm_peak):
+    """Configs 0, 1b and 2 at N=1 (each timed over rotating weight copies whose
+    total exceeds 3x L2, CUDA events, 200 launches after 10 warm-ups)."""
+    out = {}
+
+    def timed(launch, n_iter=200, warm=10):
+        for i in range(warm):
+            launch(i)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(n_iter):
+            launch(i)
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n_iter
+
+    def copies(nbytes):
+        return max(2, -(-3 * L2_BYTES // nbytes))
+
+    def make_w(fmt, rows, k, n, seed):
+        nb = k // 256
+        ws = []
+        for c in range(n):
+            t = torch.empty(q_bytes(fmt, rows, k) + 16, dtype=torch.uint8, device=dev)
+            A.call("arcllm_cuda_fill_" + fmt, C.c_void_p(t.data_ptr()), 0, rows * nb, seed + c, sp)
+            ws.append(t)
+        return ws
+
+    x18 = torch.empty(FFN, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(x18.data_ptr()), 0, FFN, 0x77, C.c_float(0), C.c_float(1), sp)
+    x35 = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(x35.data_ptr()), 0, HIDDEN, 0x78, C.c_float(0), C.c_float(1), sp)
+    y18 = torch.empty(FFN, dtype=torch.float32, device=dev)
+    y35 = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+
+    for name, fmt, rows, k, xv, yv in (("config0_q4k_18944x3584", "q4k", FFN, HIDDEN, x35, y18),
+                                       ("config1b_q6k_3584x18944", "q6k", HIDDEN, FFN, x18, y35),
+                                       ("q4k_3584x18944", "q4k", HIDDEN, FFN, x18, y35)):
+        n = copies(q_bytes(fmt, rows, k))
+        ws = make_w(fmt, rows, k, n, 0x100)
+        ty = A.GGML_Q4_K if fmt == "q4k" else A.GGML_Q6_K
+
+        def launch(i, ws=ws, ty=ty, rows=rows, k=k, xv=xv, yv=yv):
+            st = L.arcllm_cuda_matvec(ty, C.c_void_p(ws[i % len(ws)].data_ptr()), rows, k, C.c_void_p(xv.data_ptr()),
+                                      None, C.c_float(0), None, None, C.c_void_p(yv.data_ptr()), sp)
+            if st:
+                A.check(st, name)
+
+        ms = timed(launch)
+        gbs = matvec_alg_bytes(fmt, rows, k) / (ms * 1e-3) / 1e9
+        out[name] = {"GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 4), "us": round(ms * 1e3, 2),
+                     "weight_copies": n}
+        del ws
+        torch.cuda.empty_cache()
+
+    # config 2: one FFN block (RMSNorm -> fused gate/up + SiLU -> down + residual), all Q4_K
+    n = copies(3 * q_bytes("q4k", FFN, HIDDEN))
+    wg = make_w("q4k", FFN, HIDDEN, n, 0x200)
+    wu = make_w("q4k", FFN, HIDDEN, n, 0x300)
+    wd = make_w("q4k", HIDDEN, FFN, n, 0x400)
+    gamma = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(gamma.data_ptr()), 0, HIDDEN, 0x79, C.c_float(1), C.c_float(0.1),
+           sp)
+    s = torch.empty(FFN, dtype=torch.float32, device=dev)
+    h = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+
+    def ffn(i):
+        c = i % n
+        A.check(L.arcllm_cuda_gateup_silu_q4k(C.c_void_p(wg[c].data_ptr()), C.c_void_p(wu[c].data_ptr()), FFN, HIDDEN,
+                                              C.c_void_p(x35.data_ptr()), C.c_void_p(gamma.data_ptr()),
+                                              C.c_float(1e-6), C.c_void_p(s.data_ptr()), sp), "gateup")
+        A.check(L.arcllm_cuda_matvec(A.GGML_Q4_K, C.c_void_p(wd[c].data_ptr()), HIDDEN, FFN, C.c_void_p(s.data_ptr()),
+                                     None, C.c_float(0), None, C.c_void_p(x35.data_ptr()), C.c_void_p(h.data_ptr()),
+                                     sp), "down")
+
+    ms = timed(ffn, n_iter=100)
+    alg = 3 * q_bytes("q4k", FFN, HIDDEN) + 4 * (HIDDEN * 3 + FFN * 2)
+    out["config2_ffn_block_q4k"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
+                                    "frac_of_hbm": round(alg / (ms * 1e-3) / 1e9 / hbm_peak, 4),
+                                    "us": round(ms * 1e3, 2), "launches": 2}
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,72 @@
+"""Build recipe for the oracle (TEST INFRASTRUCTURE ONLY).
+
+Two libraries:
+
+* ``oracle/lib/liborc.so`` -- the C restatement in ``oracle/orc.c``.  It needs
+  only gcc and is rebuilt wherever it is missing (also on a GPU box).
+* ``oracle/_ref/libref_cpu.so`` -- the reference's OWN CPU code, compiled in
+  place from an ArcLLM checkout (``--reference``, default ``/root/reference``)
+  through ``oracle/ref_wrap.cpp``.  Nothing is copied out of the reference
+  tree.  Built only where that checkout exists; the golden fixtures under
+  ``tests/golden/`` carry its outputs elsewhere.
+
+Both use ``-ffp-contract=off`` so fp32 expressions are rounded op by op, as
+the reference's arithmetic is.
+"""
+import argparse
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORC_SO = os.path.join(HERE, "lib", "liborc.so")
+REF_SO = os.path.join(HERE, "_ref", "libref_cpu.so")
+DEFAULT_REFERENCE = "/root/reference"
+
+
+def _run(cmd):
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("oracle build failed:\n%s\n%s%s" % (" ".join(cmd), r.stdout, r.stderr))
+
+
+def build_orc(force=False):
+    src = os.path.join(HERE, "orc.c")
+    if not force and os.path.exists(ORC_SO) and os.path.getmtime(ORC_SO) >= os.path.getmtime(src):
+        return ORC_SO
+    os.makedirs(os.path.dirname(ORC_SO), exist_ok=True)
+    tmp = ORC_SO + ".tmp%d" % os.getpid()
+    _run(["gcc", "-std=c11", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
+          "-pthread", src, "-o", tmp, "-lm"])
+    os.replace(tmp, ORC_SO)
+    return ORC_SO
+
+
+def build_ref(reference=DEFAULT_REFERENCE, force=False):
+    """Compile the reference's CPU functions in place; returns the .so path or
+    None when no reference checkout is present."""
+    src_dir = os.path.join(reference, "src")
+    if not os.path.isfile(os.path.join(src_dir, "p8c_segmented_access_correctness.cpp")):
+        return None
+    wrap = os.path.join(HERE, "ref_wrap.cpp")
+    if not force and os.path.exists(REF_SO) and os.path.getmtime(REF_SO) >= os.path.getmtime(wrap):
+        return REF_SO
+    os.makedirs(os.path.dirname(REF_SO), exist_ok=True)
+    tmp = REF_SO + ".tmp%d" % os.getpid()
+    _run(["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
+          "-w", "-I", os.path.join(HERE, "ref_shim"), "-I", src_dir, wrap, "-o", tmp])
+    os.replace(tmp, REF_SO)
+    return REF_SO
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=DEFAULT_REFERENCE)
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args(argv)
+    print("orc:", build_orc(a.force))
+    print("ref:", build_ref(a.reference, a.force))
+
+
+if __name__ == "__main__":
+    sys.exit(main())
