@@ -37,6 +37,29 @@ SIGNATURES = {
     "arcllm_cuda_fill_q6k": [_vp, _u64, _u64, _u64, _vp],
     "arcllm_cuda_fill_normal_f32": [_vp, _u64, _u64, _u64, _f32, _f32, _vp],
     "arcllm_cuda_fill_normal_f16": [_vp, _u64, _u64, _u64, _f32, _f32, _vp],
+    "arcllm_cuda_rope_table": [_vp, _u32, _u32, _f32],
+    "arcllm_cuda_rope_kv_store": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp],
+    "arcllm_cuda_attention_decode": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp],
+    "arcllm_cuda_embed": [_i32, _vp, _vp, _u32, _u32, _vp, _vp],
+    "arcllm_cuda_argmax": [_vp, _u32, _vp, C.POINTER(_u32), C.POINTER(_i32), _vp],
+    "arcllm_cuda_set_device": [_i32],
+    "arcllm_cuda_malloc": [_u64, C.POINTER(_vp)],
+    "arcllm_cuda_free": [_vp],
+    "arcllm_cuda_memcpy_h2d": [_vp, _vp, _u64, _vp],
+    "arcllm_cuda_memcpy_d2h": [_vp, _vp, _u64, _vp],
+    "arcllm_cuda_stream_create": [C.POINTER(_vp)],
+    "arcllm_cuda_stream_destroy": [_vp],
+    "arcllm_cuda_stream_synchronize": [_vp],
+    "arcllm_cuda_model_create": [_vp, C.POINTER(_vp)],
+    "arcllm_cuda_model_destroy": [_vp],
+    "arcllm_cuda_model_set_layer": [_vp, _u32, _vp],
+    "arcllm_cuda_model_set_endpoints": [_vp, _vp, _i32, _vp, _vp, _i32],
+    "arcllm_cuda_model_generate": [_vp, _vp, _u32, _u32, _vp, _vp, _vp],
+    "arcllm_cuda_model_begin": [_vp, _vp, _u32, _u32, _vp],
+    "arcllm_cuda_model_step": [_vp, _i32, _i32, _vp],
+    "arcllm_cuda_model_logits": [_vp, C.POINTER(_vp)],
+    "arcllm_cuda_model_kv_cache": [_vp, C.POINTER(_vp), C.POINTER(_vp)],
+    "arcllm_cuda_model_shard_lm_head": [_vp, _u32, _u32],
 }
 _RESTYPE = {
     "arcllm_cuda_status_string": C.c_char_p,
@@ -84,6 +107,25 @@ def check(status, what=""):
 def call(name, *args):
     """Invoke an entry point and raise ArcError on a non-zero status."""
     return check(getattr(lib(), name)(*args), name)
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [("n_layers", _u32), ("hidden", _u32), ("n_heads", _u32), ("n_kv_heads", _u32),
+                ("head_dim", _u32), ("ffn", _u32), ("vocab", _u32), ("max_ctx", _u32),
+                ("rms_eps", _f32), ("rope_theta", _f32)]
+
+
+class Layer(C.Structure):
+    _fields_ = [("attn_norm", _vp), ("wq", _vp), ("bq", _vp), ("type_q", _i32),
+                ("wk", _vp), ("bk", _vp), ("type_k", _i32), ("wv", _vp), ("bv", _vp), ("type_v", _i32),
+                ("wo", _vp), ("type_o", _i32), ("ffn_norm", _vp), ("w_gate", _vp), ("w_up", _vp),
+                ("type_gate_up", _i32), ("w_down", _vp), ("type_down", _i32)]
+
+
+class GenStats(C.Structure):
+    _fields_ = [("prefill_launches", _u32), ("prefill_graph_launches", _u32),
+                ("decode_launches_per_step", _u32), ("decode_graph_launches_per_step", _u32),
+                ("decode_steps", _u32), ("prefill_ms", _f32), ("decode_ms", _f32), ("finite", _i32)]
 
 
 def row_bytes(ggml_type, k):

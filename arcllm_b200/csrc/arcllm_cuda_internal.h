@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "../../include/arcllm_cuda.h"
 
@@ -20,13 +21,33 @@ unsigned int* dev_error_word();
 struct MatvecPlan {
     int fmt = 0;
     bool dual = false;
+    bool xreg = false;  // x held in registers (one 32-weight unit per consumer thread)
+    uint32_t nwc = 0;   // consumer warps per CTA
     uint32_t rows = 0, k = 0, nb = 0, rb = 0;
     uint32_t G = 0, gmax = 0, n_groups = 0, stages = 0, stage_smem = 0, x_floats = 0;
     uint32_t smem = 0, grid = 0;
 };
 
+// Load and configure every matvec kernel on the current device (idempotent);
+// call before capturing launches into a CUDA graph.
+int matvec_prepare();
 int matvec_plan(int fmt, bool dual, uint32_t rows, uint32_t k, MatvecPlan* out);
 int matvec_launch(const MatvecPlan& pl, const void* w0, const void* w1, const float* x, const float* gamma,
                   float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
+
+std::vector<float> rope_table(uint32_t max_ctx, uint32_t head_dim, float theta);
+int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out);
+int model_destroy(arcllm_cuda_model* m);
+int model_set_layer(arcllm_cuda_model* m, uint32_t layer, const arcllm_cuda_layer* L);
+int model_set_endpoints(arcllm_cuda_model* m, const void* tok_embd, int tok_embd_type, const float* out_norm,
+                        const void* out_w, int out_type);
+int model_shard_lm_head(arcllm_cuda_model* m, uint32_t row0, uint32_t rows);
+int model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
+                cudaStream_t st);
+int model_step(arcllm_cuda_model* m, int with_head, int use_graph, cudaStream_t st);
+int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
+                   uint32_t* out_host, arcllm_cuda_gen_stats* stats, cudaStream_t st);
+int model_logits(arcllm_cuda_model* m, const float** out);
+int model_kv_cache(arcllm_cuda_model* m, const uint16_t** k, const uint16_t** v);
 
 }  // namespace arc

@@ -1,11 +1,13 @@
 // extern "C" entry points of libarcllm_cuda.so (declared in include/arcllm_cuda.h).
 // Each one validates its arguments, maps failures to a status code and never
 // lets a C++ exception or a CUDA error escape the ABI.
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
+#include "decode_ops.h"
 
 namespace arc {
 
@@ -178,6 +180,186 @@ int arcllm_cuda_fill_normal_f16(uint16_t* y, uint64_t begin, uint64_t n, uint64_
                                 void* stream) {
     ARC_GUARD_BEGIN
     return arc::fill_normal(true, y, begin, n, seed, mu, sigma, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_rope_table(float* table, uint32_t max_ctx, uint32_t head_dim, float theta) {
+    ARC_GUARD_BEGIN
+    if (!table || max_ctx == 0 || head_dim == 0 || (head_dim & 1u))
+        return set_error(ARC_E_INVALID_ARGUMENT, "rope_table: bad arguments");
+    std::vector<float> t = arc::rope_table(max_ctx, head_dim, theta);
+    const cudaError_t e = cudaMemcpy(table, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "rope_table");
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_rope_kv_store(float* q, float* k, const float* v, const float* table, const uint32_t* pos_dev,
+                              uint16_t* k_cache, uint16_t* v_cache, uint32_t q_heads, uint32_t kv_heads,
+                              uint32_t head_dim, uint32_t max_ctx, uint32_t layer, void* stream) {
+    ARC_GUARD_BEGIN
+    if (!q || !k || !v || !table || !pos_dev || !k_cache || !v_cache)
+        return set_error(ARC_E_INVALID_ARGUMENT, "rope_kv_store: null pointer");
+    if (head_dim == 0 || (head_dim & 1u) || q_heads == 0 || kv_heads == 0 || max_ctx == 0)
+        return set_error(ARC_E_INVALID_ARGUMENT, "rope_kv_store: bad shape");
+    arc::RopeKvShape s{q_heads, kv_heads, head_dim, max_ctx, layer};
+    return arc::launch_rope_kv_store(q, k, v, reinterpret_cast<const float2*>(table), pos_dev, k_cache, v_cache, s,
+                                     static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_attention_decode(const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                 const uint32_t* pos_dev, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                                 uint32_t max_ctx, uint32_t layer, uint32_t n_splits, float* scratch, float* out,
+                                 void* stream) {
+    ARC_GUARD_BEGIN
+    if (!q || !k_cache || !v_cache || !pos_dev || !scratch || !out)
+        return set_error(ARC_E_INVALID_ARGUMENT, "attention: null pointer");
+    if (n_splits == 0 || n_splits > 65535u || kv_heads == 0 || max_ctx == 0)
+        return set_error(ARC_E_INVALID_ARGUMENT, "attention: bad shape");
+    arc::AttnShape s{q_heads, kv_heads, head_dim, max_ctx, layer, n_splits, 1.0f / std::sqrt((float)head_dim)};
+    return arc::launch_attention(q, k_cache, v_cache, pos_dev, s, scratch, out, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_embed(int type, const void* table, const uint32_t* token_dev, uint32_t hidden, uint32_t vocab,
+                      float* out, void* stream) {
+    ARC_GUARD_BEGIN
+    if (!table || !token_dev || !out || hidden == 0) return set_error(ARC_E_INVALID_ARGUMENT, "embed: bad arguments");
+    if (type == ARC_GGML_Q4_K && (hidden % 256u)) return set_error(ARC_E_INVALID_ARGUMENT, "embed: Q4_K rows need hidden % 256 == 0");
+    return arc::launch_embed(type, table, token_dev, hidden, vocab, out, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_argmax(const float* logits, uint32_t n, void* scratch_dev, uint32_t* index_host, int* finite_host,
+                       void* stream) {
+    ARC_GUARD_BEGIN
+    if (!logits || !scratch_dev || !index_host || n == 0)
+        return set_error(ARC_E_INVALID_ARGUMENT, "argmax: bad arguments");
+    if (reinterpret_cast<uintptr_t>(scratch_dev) & 7u) return set_error(ARC_E_ALIGNMENT, "argmax: scratch 8-byte alignment");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned long long* key = static_cast<unsigned long long*>(scratch_dev);
+    uint32_t* flag = reinterpret_cast<uint32_t*>(key + 1);
+    cudaError_t e = cudaMemsetAsync(scratch_dev, 0, 16, s);
+    if (e != cudaSuccess) return arc::set_cuda_error(e, "argmax clear");
+    int st = arc::launch_argmax(logits, n, key, flag, s);
+    if (st != ARC_OK) return st;
+    unsigned long long hk[2] = {0, 0};
+    e = cudaMemcpyAsync(hk, scratch_dev, 16, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return arc::set_cuda_error(e, "argmax read");
+    const uint32_t nonfinite = (uint32_t)(hk[1] & 0xffffffffull);
+    *index_host = hk[0] ? ~(uint32_t)(hk[0] & 0xffffffffull) : 0u;
+    if (finite_host) *finite_host = (nonfinite == 0 && hk[0] != 0) ? 1 : 0;
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_set_device(int device) {
+    const cudaError_t e = cudaSetDevice(device);
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "set_device");
+}
+
+int arcllm_cuda_malloc(uint64_t bytes, void** out) {
+    if (!out) return set_error(ARC_E_INVALID_ARGUMENT, "malloc: null out");
+    const cudaError_t e = cudaMalloc(out, bytes);
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "malloc");
+}
+
+int arcllm_cuda_free(void* p) {
+    const cudaError_t e = cudaFree(p);
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "free");
+}
+
+int arcllm_cuda_memcpy_h2d(void* dst, const void* src_host, uint64_t bytes, void* stream) {
+    const cudaError_t e = cudaMemcpyAsync(dst, src_host, bytes, cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "memcpy_h2d");
+}
+
+int arcllm_cuda_memcpy_d2h(void* dst_host, const void* src, uint64_t bytes, void* stream) {
+    const cudaError_t e = cudaMemcpyAsync(dst_host, src, bytes, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "memcpy_d2h");
+}
+
+int arcllm_cuda_stream_create(void** out) {
+    if (!out) return set_error(ARC_E_INVALID_ARGUMENT, "stream_create: null out");
+    cudaStream_t s;
+    const cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return arc::set_cuda_error(e, "stream_create");
+    *out = s;
+    return ARC_OK;
+}
+
+int arcllm_cuda_stream_destroy(void* stream) {
+    const cudaError_t e = cudaStreamDestroy(static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "stream_destroy");
+}
+
+int arcllm_cuda_stream_synchronize(void* stream) {
+    const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "stream_synchronize");
+}
+
+int arcllm_cuda_model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
+    ARC_GUARD_BEGIN
+    return arc::model_create(cfg, out);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_destroy(arcllm_cuda_model* m) {
+    ARC_GUARD_BEGIN
+    return arc::model_destroy(m);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_set_layer(arcllm_cuda_model* m, uint32_t layer, const arcllm_cuda_layer* w) {
+    ARC_GUARD_BEGIN
+    return arc::model_set_layer(m, layer, w);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_set_endpoints(arcllm_cuda_model* m, const void* tok_embd, int tok_embd_type,
+                                    const float* output_norm, const void* output, int output_type) {
+    ARC_GUARD_BEGIN
+    return arc::model_set_endpoints(m, tok_embd, tok_embd_type, output_norm, output, output_type);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
+                               uint32_t* out_tokens_host, arcllm_cuda_gen_stats* stats, void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::model_generate(m, prompt_host, n_prompt, max_new, out_tokens_host, stats,
+                               static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
+                            void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::model_begin(m, prompt_host, n_prompt, max_new, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_step(arcllm_cuda_model* m, int with_head, int use_graph, void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::model_step(m, with_head, use_graph, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_logits(arcllm_cuda_model* m, const float** out) {
+    ARC_GUARD_BEGIN
+    return arc::model_logits(m, out);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_kv_cache(arcllm_cuda_model* m, const uint16_t** k, const uint16_t** v) {
+    ARC_GUARD_BEGIN
+    return arc::model_kv_cache(m, k, v);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_shard_lm_head(arcllm_cuda_model* m, uint32_t row0, uint32_t rows) {
+    ARC_GUARD_BEGIN
+    return arc::model_shard_lm_head(m, row0, rows);
     ARC_GUARD_END
 }
 

@@ -1,0 +1,379 @@
+// Greedy decode runtime for one Qwen2-family model on one GPU, behind the C ABI.
+//
+// This is the device half of the reference's generate()
+// (src/arcllm_v1_runtime.cpp:149-536): its per-token Vulkan chain of 469
+// dispatches with a fence wait and a host top-2 per token (:371-421, 461-505)
+// becomes one CUDA-graph launch per token whose kernels read the position and
+// token from device memory and write the next token back on the device
+// (greedy argmax included), so consecutive tokens need no host round trip.
+//
+// Per layer (decode_step): RMSNorm fused into the Q/K/V matvecs (+bias),
+// RoPE + fp16 KV store, split-KV GQA attention, O projection + residual,
+// RMSNorm fused into the dual gate/up matvec with silu(g)*u, down projection
+// + residual.  Then output RMSNorm fused into the LM head, argmax, finalize.
+// The prompt is consumed token by token through the same layer chain without
+// the LM head (the prefill graph).
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "arcllm_cuda_internal.h"
+#include "decode_ops.h"
+
+struct arcllm_cuda_model {
+    int device = 0;
+    arcllm_cuda_model_config cfg{};
+    std::vector<arcllm_cuda_layer> layers;
+    std::vector<uint8_t> layer_set;
+    const void* tok_embd = nullptr;
+    int tok_embd_type = 0;
+    const float* out_norm = nullptr;
+    const void* out_w = nullptr;
+    int out_type = 0;
+    bool endpoints_set = false;
+    // row shard of the LM head computed here (all rows unless sharded)
+    uint32_t lm_row0 = 0, lm_rows = 0;
+
+    // device memory (one allocation)
+    void* arena = nullptr;
+    float *h0 = nullptr, *h1 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *s = nullptr,
+          *logits = nullptr, *part = nullptr;
+    uint16_t *kc = nullptr, *vc = nullptr;
+    float2* rope = nullptr;
+    arc::GreedyState* state = nullptr;
+    uint32_t* prompt = nullptr;
+    uint32_t* out_tokens = nullptr;
+    uint32_t attn_splits = 16;
+
+    cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
+    uint32_t launches_prefill_step = 0, launches_decode_step = 0;
+};
+
+namespace arc {
+namespace {
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+bool quant_ok(int t) { return t == ARC_GGML_Q4_K || t == ARC_GGML_Q6_K; }
+
+int check_layer(const arcllm_cuda_model_config& c, const arcllm_cuda_layer& L) {
+    if (!L.attn_norm || !L.ffn_norm || !L.wq || !L.wk || !L.wv || !L.wo || !L.w_gate || !L.w_up || !L.w_down)
+        return set_error(ARC_E_INVALID_ARGUMENT, "model_set_layer: null tensor pointer");
+    if (!quant_ok(L.type_q) || !quant_ok(L.type_k) || !quant_ok(L.type_v) || !quant_ok(L.type_o) ||
+        !quant_ok(L.type_down) || L.type_gate_up != ARC_GGML_Q4_K)
+        return set_error(ARC_E_UNSUPPORTED_SHAPE,
+                         "model_set_layer: projections must be Q4_K/Q6_K and gate/up Q4_K "
+                         "(reference contract: src/arcllm_v1_runtime.cpp:194-211)");
+    (void)c;
+    return ARC_OK;
+}
+
+// Launch one matvec with a freshly computed plan (host-only arithmetic).
+int mv(int type, const void* w, uint32_t rows, uint32_t k, const float* x, const float* gamma, float eps,
+       const float* bias, const float* residual, float* y, cudaStream_t st) {
+    MatvecPlan pl;
+    int r = matvec_plan(type, false, rows, k, &pl);
+    if (r != ARC_OK) return r;
+    return matvec_launch(pl, w, nullptr, x, gamma, eps, bias, residual, y, st);
+}
+
+#define ARC_TRY(expr)          \
+    do {                       \
+        int _st = (expr);      \
+        if (_st != ARC_OK) return _st; \
+    } while (0)
+
+// Enqueue one token step; `with_head` adds output norm + LM head + argmax.
+int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t* n_launch) {
+    const arcllm_cuda_model_config& c = m->cfg;
+    const uint32_t H = c.hidden, KV = c.n_kv_heads * c.head_dim;
+    uint32_t n = 0;
+    ARC_TRY(launch_embed(m->tok_embd_type, m->tok_embd, &m->state->token, H, c.vocab, m->h0, st));
+    ++n;
+    float* hc = m->h0;
+    float* hm = m->h1;
+    for (uint32_t l = 0; l < c.n_layers; ++l) {
+        const arcllm_cuda_layer& L = m->layers[l];
+        ARC_TRY(mv(L.type_q, L.wq, H, H, hc, L.attn_norm, c.rms_eps, L.bq, nullptr, m->q, st));
+        ARC_TRY(mv(L.type_k, L.wk, KV, H, hc, L.attn_norm, c.rms_eps, L.bk, nullptr, m->k, st));
+        ARC_TRY(mv(L.type_v, L.wv, KV, H, hc, L.attn_norm, c.rms_eps, L.bv, nullptr, m->v, st));
+        RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
+        ARC_TRY(launch_rope_kv_store(m->q, m->k, m->v, m->rope, &m->state->pos, m->kc, m->vc, rs, st));
+        AttnShape as{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l, m->attn_splits,
+                     1.0f / std::sqrt((float)c.head_dim)};
+        ARC_TRY(launch_attention(m->q, m->kc, m->vc, &m->state->pos, as, m->part, m->attn, st));
+        ARC_TRY(mv(L.type_o, L.wo, H, H, m->attn, nullptr, 0.f, nullptr, hc, hm, st));
+        {
+            MatvecPlan pl;
+            ARC_TRY(matvec_plan(ARC_GGML_Q4_K, true, c.ffn, H, &pl));
+            ARC_TRY(matvec_launch(pl, L.w_gate, L.w_up, hm, L.ffn_norm, c.rms_eps, nullptr, nullptr, m->s, st));
+        }
+        ARC_TRY(mv(L.type_down, L.w_down, H, c.ffn, m->s, nullptr, 0.f, nullptr, hm, hc, st));
+        n += 9;
+    }
+    if (with_head) {
+        ARC_TRY(mv(m->out_type, m->out_w, m->lm_rows, H, hc, m->out_norm, c.rms_eps, nullptr, nullptr,
+                   m->logits + m->lm_row0, st));
+        ARC_TRY(launch_argmax(m->logits, c.vocab, &m->state->argmax_key, &m->state->nonfinite, st));
+        n += 2;
+    }
+    ARC_TRY(launch_greedy_finalize(m->state, m->prompt, m->out_tokens, c.max_ctx, st));
+    ++n;
+    if (n_launch) *n_launch = n;
+    return ARC_OK;
+}
+
+int capture(arcllm_cuda_model* m, bool with_head, cudaGraphExec_t* out, uint32_t* n_launch) {
+    cudaStream_t cs;
+    cudaError_t e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return set_cuda_error(e, "capture stream");
+    e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(cs);
+        return set_cuda_error(e, "begin capture");
+    }
+    int st = enqueue_step(m, with_head, cs, n_launch);
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(cs, &g);
+    cudaStreamDestroy(cs);
+    if (st != ARC_OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (e != cudaSuccess) return set_cuda_error(e, "end capture");
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return set_cuda_error(e, "graph instantiate");
+    return ARC_OK;
+}
+
+}  // namespace
+
+// RoPE table: cos/sin of pos * theta^(-2p/d) computed with the reference's
+// float expression (src/p8c_segmented_access_correctness.cpp:1010-1011).
+std::vector<float> rope_table(uint32_t max_ctx, uint32_t head_dim, float theta) {
+    const uint32_t half = head_dim / 2u;
+    std::vector<float> t((size_t)max_ctx * half * 2u);
+    for (uint32_t pos = 0; pos < max_ctx; ++pos) {
+        for (uint32_t p = 0; p < half; ++p) {
+            volatile float ex = -2.0f * (float)p;
+            ex = ex / (float)head_dim;
+            volatile float pw = std::pow(theta, (float)ex);
+            volatile float angle = (float)pos * (float)pw;
+            t[((size_t)pos * half + p) * 2 + 0] = std::cos((float)angle);
+            t[((size_t)pos * half + p) * 2 + 1] = std::sin((float)angle);
+        }
+    }
+    return t;
+}
+
+int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
+    if (!cfg || !out) return set_error(ARC_E_INVALID_ARGUMENT, "model_create: null pointer");
+    const arcllm_cuda_model_config& c = *cfg;
+    if (c.n_layers == 0 || c.hidden == 0 || c.hidden % 256u || c.ffn % 256u || c.ffn == 0 || c.head_dim != 128u ||
+        c.n_heads == 0 || c.n_kv_heads == 0 || c.n_heads % c.n_kv_heads || c.n_heads * c.head_dim != c.hidden ||
+        c.vocab == 0 || c.max_ctx == 0)
+        return set_error(ARC_E_UNSUPPORTED_SHAPE,
+                         "model_create: needs hidden,ffn multiples of 256, head_dim 128, heads*head_dim == hidden");
+    ARC_TRY(matvec_prepare());
+    ARC_TRY(decode_ops_prepare());
+    if (!dev_error_word()) return set_error(ARC_E_CUDA, "model_create: device error word unavailable");
+    auto* m = new (std::nothrow) arcllm_cuda_model();
+    if (!m) return set_error(ARC_E_OUT_OF_MEMORY, "model_create: host allocation");
+    cudaGetDevice(&m->device);
+    m->cfg = c;
+    m->layers.resize(c.n_layers);
+    m->layer_set.assign(c.n_layers, 0);
+    m->lm_row0 = 0;
+    m->lm_rows = c.vocab;
+    const uint32_t gq = c.n_heads / c.n_kv_heads;
+    const size_t kv_dim = (size_t)c.n_kv_heads * c.head_dim;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const size_t o_h0 = take(4 * c.hidden), o_h1 = take(4 * c.hidden), o_q = take(4 * c.hidden),
+                 o_k = take(4 * kv_dim), o_v = take(4 * kv_dim), o_attn = take(4 * c.hidden),
+                 o_s = take(4 * (size_t)c.ffn), o_logits = take(4 * (size_t)c.vocab),
+                 o_part = take(4 * (size_t)c.n_kv_heads * m->attn_splits * gq * (c.head_dim + 2)),
+                 o_kc = take(2 * (size_t)c.n_layers * c.max_ctx * kv_dim),
+                 o_vc = take(2 * (size_t)c.n_layers * c.max_ctx * kv_dim),
+                 o_rope = take(8 * (size_t)c.max_ctx * (c.head_dim / 2)), o_state = take(sizeof(GreedyState)),
+                 o_prompt = take(4 * (size_t)c.max_ctx), o_out = take(4 * (size_t)c.max_ctx);
+    cudaError_t e = cudaMalloc(&m->arena, off);
+    if (e != cudaSuccess) {
+        delete m;
+        return set_cuda_error(e, "model_create: device arena");
+    }
+    uint8_t* a = static_cast<uint8_t*>(m->arena);
+    m->h0 = reinterpret_cast<float*>(a + o_h0);
+    m->h1 = reinterpret_cast<float*>(a + o_h1);
+    m->q = reinterpret_cast<float*>(a + o_q);
+    m->k = reinterpret_cast<float*>(a + o_k);
+    m->v = reinterpret_cast<float*>(a + o_v);
+    m->attn = reinterpret_cast<float*>(a + o_attn);
+    m->s = reinterpret_cast<float*>(a + o_s);
+    m->logits = reinterpret_cast<float*>(a + o_logits);
+    m->part = reinterpret_cast<float*>(a + o_part);
+    m->kc = reinterpret_cast<uint16_t*>(a + o_kc);
+    m->vc = reinterpret_cast<uint16_t*>(a + o_vc);
+    m->rope = reinterpret_cast<float2*>(a + o_rope);
+    m->state = reinterpret_cast<GreedyState*>(a + o_state);
+    m->prompt = reinterpret_cast<uint32_t*>(a + o_prompt);
+    m->out_tokens = reinterpret_cast<uint32_t*>(a + o_out);
+    std::vector<float> rt = rope_table(c.max_ctx, c.head_dim, c.rope_theta);
+    e = cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(m->logits, 0, 4 * (size_t)c.vocab);
+    if (e != cudaSuccess) {
+        cudaFree(m->arena);
+        delete m;
+        return set_cuda_error(e, "model_create: init");
+    }
+    *out = m;
+    return ARC_OK;
+}
+
+int model_set_layer(arcllm_cuda_model* m, uint32_t layer, const arcllm_cuda_layer* L) {
+    if (!m || !L) return set_error(ARC_E_INVALID_ARGUMENT, "model_set_layer: null pointer");
+    if (layer >= m->cfg.n_layers) return set_error(ARC_E_INVALID_ARGUMENT, "model_set_layer: layer out of range");
+    ARC_TRY(check_layer(m->cfg, *L));
+    m->layers[layer] = *L;
+    m->layer_set[layer] = 1;
+    return ARC_OK;
+}
+
+int model_set_endpoints(arcllm_cuda_model* m, const void* tok_embd, int tok_embd_type, const float* out_norm,
+                        const void* out_w, int out_type) {
+    if (!m || !tok_embd || !out_norm || !out_w) return set_error(ARC_E_INVALID_ARGUMENT, "set_endpoints: null pointer");
+    if ((tok_embd_type != ARC_GGML_F16 && tok_embd_type != ARC_GGML_Q4_K) || !quant_ok(out_type))
+        return set_error(ARC_E_UNSUPPORTED_SHAPE, "set_endpoints: embedding F16/Q4_K, output Q4_K/Q6_K");
+    m->tok_embd = tok_embd;
+    m->tok_embd_type = tok_embd_type;
+    m->out_norm = out_norm;
+    m->out_w = out_w;
+    m->out_type = out_type;
+    m->endpoints_set = true;
+    return ARC_OK;
+}
+
+int model_shard_lm_head(arcllm_cuda_model* m, uint32_t row0, uint32_t rows) {
+    if (!m || rows == 0 || row0 + rows > m->cfg.vocab) return set_error(ARC_E_INVALID_ARGUMENT, "shard: bad range");
+    m->lm_row0 = row0;
+    m->lm_rows = rows;
+    if (m->g_decode) {
+        cudaGraphExecDestroy(m->g_decode);
+        m->g_decode = nullptr;
+    }
+    return ARC_OK;
+}
+
+static int ready(arcllm_cuda_model* m) {
+    if (!m->endpoints_set) return set_error(ARC_E_INVALID_ARGUMENT, "model: endpoints not set");
+    for (uint8_t f : m->layer_set)
+        if (!f) return set_error(ARC_E_INVALID_ARGUMENT, "model: not every layer was set");
+    return ARC_OK;
+}
+
+int model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
+                cudaStream_t st) {
+    if (!m || !prompt_host) return set_error(ARC_E_INVALID_ARGUMENT, "begin: null pointer");
+    ARC_TRY(ready(m));
+    if (n_prompt == 0 || max_new == 0) return set_error(ARC_E_INVALID_ARGUMENT, "begin: empty prompt or max_new 0");
+    if ((uint64_t)n_prompt + max_new - 1u > m->cfg.max_ctx)
+        return set_error(ARC_E_INVALID_ARGUMENT, "begin: request exceeds the KV context limit");
+    for (uint32_t i = 0; i < n_prompt; ++i)
+        if (prompt_host[i] >= m->cfg.vocab) return set_error(ARC_E_INVALID_ARGUMENT, "begin: token out of vocabulary");
+    GreedyState s{};
+    s.token = prompt_host[0];
+    s.pos = 0;
+    s.n_prompt = n_prompt;
+    cudaError_t e = cudaMemcpyAsync(m->prompt, prompt_host, 4ull * n_prompt, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->state, &s, sizeof s, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // `s` lives on this stack frame
+    if (e != cudaSuccess) return set_cuda_error(e, "begin: upload");
+    return ARC_OK;
+}
+
+int model_step(arcllm_cuda_model* m, int with_head, int use_graph, cudaStream_t st) {
+    if (!m) return set_error(ARC_E_INVALID_ARGUMENT, "step: null model");
+    ARC_TRY(ready(m));
+    if (!use_graph) return enqueue_step(m, with_head != 0, st, nullptr);
+    cudaGraphExec_t* g = with_head ? &m->g_decode : &m->g_prefill;
+    if (!*g) {
+        ARC_TRY(capture(m, with_head != 0, g, with_head ? &m->launches_decode_step : &m->launches_prefill_step));
+    }
+    const cudaError_t e = cudaGraphLaunch(*g, st);
+    return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "graph launch");
+}
+
+int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
+                   uint32_t* out_host, arcllm_cuda_gen_stats* stats, cudaStream_t st) {
+    if (!out_host) return set_error(ARC_E_INVALID_ARGUMENT, "generate: null output");
+    ARC_TRY(model_begin(m, prompt_host, n_prompt, max_new, st));
+    // make sure both graphs exist before timing (capture is host work)
+    if (!m->g_prefill) ARC_TRY(capture(m, false, &m->g_prefill, &m->launches_prefill_step));
+    if (!m->g_decode) ARC_TRY(capture(m, true, &m->g_decode, &m->launches_decode_step));
+    cudaEvent_t e0, e1, e2;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventCreate(&e2);
+    cudaEventRecord(e0, st);
+    for (uint32_t i = 0; i + 1 < n_prompt; ++i) ARC_TRY(model_step(m, 0, 1, st));
+    ARC_TRY(model_step(m, 1, 1, st));  // last prompt token: first generated token
+    cudaEventRecord(e1, st);
+    for (uint32_t i = 1; i < max_new; ++i) ARC_TRY(model_step(m, 1, 1, st));
+    cudaEventRecord(e2, st);
+    GreedyState s{};
+    cudaError_t e = cudaMemcpyAsync(out_host, m->out_tokens, 4ull * max_new, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&s, m->state, sizeof s, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    float ms_p = 0.f, ms_d = 0.f;
+    if (e == cudaSuccess) {
+        cudaEventElapsedTime(&ms_p, e0, e1);
+        cudaEventElapsedTime(&ms_d, e1, e2);
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(e2);
+    if (e != cudaSuccess) return set_cuda_error(e, "generate: readback");
+    if (stats) {
+        stats->prefill_launches = m->launches_prefill_step * (n_prompt - 1u) + m->launches_decode_step;
+        stats->prefill_graph_launches = n_prompt;
+        stats->decode_launches_per_step = m->launches_decode_step;
+        stats->decode_graph_launches_per_step = 1;
+        stats->decode_steps = max_new - 1u;
+        stats->prefill_ms = ms_p;
+        stats->decode_ms = ms_d;
+        stats->finite = (s.nonfinite == 0) ? 1 : 0;
+    }
+    if (s.n_generated != max_new) return set_error(ARC_E_INVALID_ARGUMENT, "generate: generated-token count mismatch");
+    if (s.nonfinite) return set_error(ARC_E_NONFINITE, "generate: non-finite logits");
+    return ARC_OK;
+}
+
+int model_logits(arcllm_cuda_model* m, const float** out) {
+    if (!m || !out) return set_error(ARC_E_INVALID_ARGUMENT, "logits: null pointer");
+    *out = m->logits;
+    return ARC_OK;
+}
+
+int model_kv_cache(arcllm_cuda_model* m, const uint16_t** k, const uint16_t** v) {
+    if (!m || !k || !v) return set_error(ARC_E_INVALID_ARGUMENT, "kv_cache: null pointer");
+    *k = m->kc;
+    *v = m->vc;
+    return ARC_OK;
+}
+
+int model_destroy(arcllm_cuda_model* m) {
+    if (!m) return ARC_OK;
+    if (m->g_prefill) cudaGraphExecDestroy(m->g_prefill);
+    if (m->g_decode) cudaGraphExecDestroy(m->g_decode);
+    if (m->arena) cudaFree(m->arena);
+    delete m;
+    return ARC_OK;
+}
+
+}  // namespace arc

@@ -231,6 +231,10 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the extra configs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-IO leg")
+    ap.add_argument("--fmt", default="q6k", choices=["q6k", "q4k"], help="profiling override of the workload")
+    ap.add_argument("--rows", type=int, default=LM_ROWS, help="profiling override of the workload")
+    ap.add_argument("--k", type=int, default=HIDDEN, help="profiling override of the workload")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
@@ -263,22 +267,25 @@ def main(argv=None):
         torch.cuda.synchronize()
 
     # ---- headline: LM head (rows sharded over ranks) ----
-    rows_per = LM_ROWS // world
+    fmt, ROWS, K = args.fmt, args.rows, args.k
+    headline = (fmt, ROWS, K) == ("q6k", LM_ROWS, HIDDEN)
+    TY = A.GGML_Q6_K if fmt == "q6k" else A.GGML_Q4_K
+    rows_per = ROWS // world
     r0 = rank * rows_per
-    rb = q_bytes("q6k", 1, HIDDEN)
+    rb = q_bytes(fmt, 1, K)
     w = torch.empty(rows_per * rb + 16, dtype=torch.uint8, device=dev)
-    A.call("arcllm_cuda_fill_q6k", C.c_void_p(w.data_ptr()), r0 * (HIDDEN // 256), rows_per * (HIDDEN // 256),
+    A.call("arcllm_cuda_fill_" + fmt, C.c_void_p(w.data_ptr()), r0 * (K // 256), rows_per * (K // 256),
            0x1A4D, sp)
     # x ~ N(0,1) generated with the library's fixture stream (same as the oracle's)
-    x = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
-    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(x.data_ptr()), 0, HIDDEN, 0x1A4E, C.c_float(0.0),
+    x = torch.empty(K, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(x.data_ptr()), 0, K, 0x1A4E, C.c_float(0.0),
            C.c_float(1.0), sp)
     y = torch.empty(rows_per, dtype=torch.float32, device=dev)
-    logits = torch.empty(LM_ROWS, dtype=torch.float32, device=dev)
+    logits = torch.empty(rows_per * world, dtype=torch.float32, device=dev)
     wp, xp, yp = C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr())
 
     def step():
-        st = L.arcllm_cuda_matvec(A.GGML_Q6_K, wp, rows_per, HIDDEN, xp, None, C.c_float(0.0), None, None, yp, sp)
+        st = L.arcllm_cuda_matvec(TY, wp, rows_per, K, xp, None, C.c_float(0.0), None, None, yp, sp)
         if st:
             A.check(st, "matvec")
         if dist is not None:
@@ -296,7 +303,7 @@ def main(argv=None):
     t_start.record()
     for i in range(args.steps):
         ev[i][0].record()
-        st = L.arcllm_cuda_matvec(A.GGML_Q6_K, wp, rows_per, HIDDEN, xp, None, C.c_float(0.0), None, None, yp, sp)
+        st = L.arcllm_cuda_matvec(TY, wp, rows_per, K, xp, None, C.c_float(0.0), None, None, yp, sp)
         if st:
             A.check(st, "matvec")
         ev[i][1].record()
@@ -314,23 +321,23 @@ def main(argv=None):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         total_ms, kern_ms = float(tt[0]), float(tt[1])
     ms_per_step = total_ms / args.steps
-    alg_total = matvec_alg_bytes("q6k", LM_ROWS, HIDDEN)
+    alg_total = matvec_alg_bytes(fmt, rows_per * world, K)
     value = alg_total / (ms_per_step * 1e-3) / 1e9
-    alg_shard = matvec_alg_bytes("q6k", rows_per, HIDDEN)
+    alg_shard = matvec_alg_bytes(fmt, rows_per, K)
     achieved = alg_shard / (kern_ms * 1e-3) / 1e9
     hbm_peak, _, peak_src = measured_peaks()
-    traffic = committed_traffic("lmhead_q6k_%d" % world)
+    traffic = committed_traffic("lmhead_q6k_%d" % world) if headline else None
 
     # ---- e2e through the C-ABI host-IO entry point (rank-local shard + all-gather) ----
-    xh = torch.empty(HIDDEN, dtype=torch.float32).pin_memory()
+    xh = torch.empty(K, dtype=torch.float32).pin_memory()
     xh.copy_(x.cpu())
     yh = torch.empty(rows_per, dtype=torch.float32).pin_memory()
-    xd = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
-    lh = torch.empty(LM_ROWS, dtype=torch.float32).pin_memory()
-    e2e_steps = max(10, min(args.steps, 500))
+    xd = torch.empty(K, dtype=torch.float32, device=dev)
+    lh = torch.empty(rows_per * world, dtype=torch.float32).pin_memory()
+    e2e_steps = 0 if args.no_e2e else max(10, min(args.steps, 500))
 
     def e2e_step():
-        A.check(L.arcllm_cuda_matvec_hostio(A.GGML_Q6_K, wp, rows_per, HIDDEN, C.c_void_p(xh.data_ptr()),
+        A.check(L.arcllm_cuda_matvec_hostio(TY, wp, rows_per, K, C.c_void_p(xh.data_ptr()),
                                             C.c_void_p(xd.data_ptr()), yp, C.c_void_p(yh.data_ptr()), sp),
                 "matvec_hostio")
         if dist is not None:
@@ -338,7 +345,7 @@ def main(argv=None):
             lh.copy_(logits, non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
-    for _ in range(3):
+    for _ in range(3 if e2e_steps else 0):
         e2e_step()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -347,20 +354,22 @@ def main(argv=None):
         e2e_step()
     e1.record()
     barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    e2e_ms = e0.elapsed_time(e1) / max(1, e2e_steps)
     if dist is not None:
         tt = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt[0])
     e2e_val = alg_total / (e2e_ms * 1e-3) / 1e9
-    d2h = 4 * (LM_ROWS if dist is not None else rows_per)
+    d2h = 4 * rows_per * world
+    if not e2e_steps:
+        e2e_val = None
 
     extra = {}
-    if world == 1 and not args.no_extra:
+    if world == 1 and headline and not args.no_extra:
         extra = run_extra(A, L, torch, dev, sp, hbm_peak)
 
     if rank == 0:
-        cpu = None if args.no_cpu or world > 1 else cpu_baseline()
+        cpu = None if args.no_cpu or world > 1 or not headline else cpu_baseline()
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -375,20 +384,23 @@ def main(argv=None):
             "dtype": "f32",
             "data": "synthetic",
             "config": {
-                "workload": "config1: Q6_K LM-head matvec 152064x3584 (447.07 MB packed weights), fp32 x ~ N(0,1)"
+                "workload": ("config1: Q6_K LM-head matvec 152064x3584 (447.07 MB packed weights), fp32 x ~ N(0,1)"
+                             if headline else "profiling case: %s matvec %dx%d" % (fmt, ROWS, K))
                             + ("; rows sharded over %d GPUs + NCCL all-gather of fp32 logits" % world
                                if world > 1 else ""),
-                "l2": "weights larger than L2 (447 MB vs 126 MB): no flush needed between steps",
+                "l2": "weights larger than L2 (%.0f MB vs 126 MB): no flush needed between steps"
+                      % (q_bytes(fmt, ROWS, K) / 1e6),
                 "parallelism": "row-shard%d" % world,
                 "algorithmic_bytes_per_step": alg_total,
             },
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "kernel": "matvec_stream_kernel<14,8,false> (Q6_K, 8-row groups)",
+                "kernel": "matvec_stream_kernel (%s)" % fmt,
                 "kernel_ms": round(kern_ms, 5), "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
             },
-            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * HIDDEN,
+            "e2e": {"value": None if e2e_val is None else round(e2e_val, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": 4 * K,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
                     "api": "arcllm_cuda_matvec_hostio (pinned host x in, logits out, stream sync)"},
             "gpu_launches": args.steps,
@@ -485,7 +497,42 @@ def run_extra(A, L, torch, dev, sp, hbm_peak):
     out["config2_ffn_block_q4k"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
                                     "frac_of_hbm": round(alg / (ms * 1e-3) / 1e9 / hbm_peak, 4),
                                     "us": round(ms * 1e3, 2), "launches": 2}
+    del wg, wu, wd
+    torch.cuda.empty_cache()
+    out["config3_decode"] = run_decode(A, torch, hbm_peak)
     return out
+
+
+def run_decode(A, torch, hbm_peak, n_prompt=256, max_new=128):
+    """Config 3: greedy decode of a random-init Qwen2.5-7B-shaped model (q/k/o/
+    gate/up Q4_K; v, down, LM head Q6_K; fp16 embedding; fp16 KV cache, max
+    context 4096): 256 seeded uniform prompt ids, then 128 greedy tokens, one
+    CUDA-graph launch per token, the next token chosen on the device."""
+    from arcllm_b200.synthetic import QWEN25_7B, SyntheticModel
+    m = SyntheticModel(QWEN25_7B, seed=0xC3)
+    prompt = [int(splitmix_token(i, QWEN25_7B["vocab"])) for i in range(n_prompt)]
+    m.generate(prompt[:8], 4)  # warm-up: captures the two step graphs
+    t0 = time.perf_counter()
+    toks, st = m.generate(prompt, max_new)
+    wall = time.perf_counter() - t0
+    bpt = m.bytes_per_token()
+    dec_s = st.decode_ms * 1e-3
+    tps = st.decode_steps / dec_s
+    res = {"tok/s": round(tps, 1), "ms_per_token": round(st.decode_ms / st.decode_steps, 4),
+           "weight_GB/s": round(bpt * tps / 1e9, 1), "frac_of_hbm": round(bpt * tps / 1e9 / hbm_peak, 4),
+           "bytes_per_token": bpt, "prefill_ms_256_tokens": round(st.prefill_ms, 2),
+           "e2e_generate_s": round(wall, 4),
+           "e2e_tok_s_incl_prefill": round(max_new / wall, 1),
+           "launches_per_token": st.decode_launches_per_step, "graph_launches_per_token": 1,
+           "first_tokens": toks[:4], "finite": bool(st.finite)}
+    m.close()
+    torch.cuda.empty_cache()
+    return res
+
+
+def splitmix_token(i, vocab, seed=0x70C):
+    from arcllm_b200.synthetic import splitmix64_at
+    return ((splitmix64_at(seed, i) >> 32) * vocab) >> 32
 
 
 if __name__ == "__main__":

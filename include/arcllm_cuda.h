@@ -125,6 +125,113 @@ ARCLLM_CUDA_API int arcllm_cuda_fill_normal_f32(float *y, uint64_t begin, uint64
 ARCLLM_CUDA_API int arcllm_cuda_fill_normal_f16(uint16_t *y, uint64_t begin, uint64_t n, uint64_t seed, float mu, float sigma,
                                 void *stream);
 
+
+/* ---- decode-step ops (the model runs these; exposed for tests and callers
+ * that drive their own step) ------------------------------------------------ */
+/* Fill table[max_ctx][head_dim/2] with (cos, sin) of pos*theta^(-2p/head_dim),
+ * evaluated in fp32 exactly as src/p8c_segmented_access_correctness.cpp:1010-1011.
+ * Synchronous. */
+ARCLLM_CUDA_API int arcllm_cuda_rope_table(float *table, uint32_t max_ctx, uint32_t head_dim, float theta);
+/* RoPE on q [q_heads*head_dim] and k [kv_heads*head_dim] in place (adjacent
+ * pairs, shaders/p7_rope_seq.comp:15-38, PCRope runtime.cpp:273) and store k, v
+ * as fp16 into caches [layers][max_ctx][kv_heads*head_dim] at position *pos_dev
+ * of `layer` (shaders/p7_kv_store.comp:14-25, PCKV runtime.cpp:274). */
+ARCLLM_CUDA_API int arcllm_cuda_rope_kv_store(float *q, float *k, const float *v, const float *table,
+                                              const uint32_t *pos_dev, uint16_t *k_cache, uint16_t *v_cache,
+                                              uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                                              uint32_t max_ctx, uint32_t layer, void *stream);
+/* Cached GQA decode attention for position *pos_dev over fp16 caches
+ * (shaders/p7_attention_kv_online.comp, PCAttnKV runtime.cpp:275; CPU form
+ * src/p8c_segmented_access_correctness.cpp:1136-1158), split over n_splits
+ * position slices per KV head.  head_dim must be 128.  `scratch` holds
+ * kv_heads*n_splits*(q_heads/kv_heads)*(head_dim+2) floats. */
+ARCLLM_CUDA_API int arcllm_cuda_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                                 const uint32_t *pos_dev, uint32_t q_heads, uint32_t kv_heads,
+                                                 uint32_t head_dim, uint32_t max_ctx, uint32_t layer,
+                                                 uint32_t n_splits, float *scratch, float *out, void *stream);
+/* Embedding row *token_dev of an F16 (1) or Q4_K (12) table into out[hidden]
+ * (shaders/p8c_embedding_q4k_segmented_probe.comp, runtime.cpp:373). */
+ARCLLM_CUDA_API int arcllm_cuda_embed(int type, const void *table, const uint32_t *token_dev, uint32_t hidden,
+                                      uint32_t vocab, float *out, void *stream);
+/* Greedy select over logits[n] (runtime_top2 top-1, runtime.cpp:132-148):
+ * writes the first index of the maximum finite logit to *index_host and 1/0
+ * to *finite_host (0 when any logit is non-finite).  Synchronous;
+ * `scratch_dev` holds 16 bytes. */
+ARCLLM_CUDA_API int arcllm_cuda_argmax(const float *logits, uint32_t n, void *scratch_dev, uint32_t *index_host,
+                                       int *finite_host, void *stream);
+
+/* ---- device memory and streams (for hosts that do not link the CUDA runtime) --- */
+ARCLLM_CUDA_API int arcllm_cuda_set_device(int device);
+ARCLLM_CUDA_API int arcllm_cuda_malloc(uint64_t bytes, void **out);
+ARCLLM_CUDA_API int arcllm_cuda_free(void *p);
+ARCLLM_CUDA_API int arcllm_cuda_memcpy_h2d(void *dst, const void *src_host, uint64_t bytes, void *stream);
+ARCLLM_CUDA_API int arcllm_cuda_memcpy_d2h(void *dst_host, const void *src, uint64_t bytes, void *stream);
+ARCLLM_CUDA_API int arcllm_cuda_stream_create(void **out);
+ARCLLM_CUDA_API int arcllm_cuda_stream_destroy(void *stream);
+ARCLLM_CUDA_API int arcllm_cuda_stream_synchronize(void *stream);
+
+/* ---- greedy decode of one Qwen2-family model -----------------------------
+ * The device half of arcllm::v1::runtime::generate() (src/arcllm_v1_runtime.cpp:
+ * 149-536).  The caller owns the weight memory (device pointers into its
+ * arenas); the model owns activations, an fp16 KV cache [layer][max_ctx]
+ * [kv_heads*head_dim] (request-scoped, like the reference's :261-263), the
+ * RoPE table and the device-side greedy state.  Each token is one CUDA-graph
+ * launch; the next token is chosen on the device.  Not thread-safe per model. */
+typedef struct arcllm_cuda_model arcllm_cuda_model;
+
+typedef struct {
+    uint32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_ctx;
+    float rms_eps;    /* GGUF qwen2.attention.layer_norm_rms_epsilon (runtime.cpp:183-184) */
+    float rope_theta; /* GGUF qwen2.rope.freq_base (runtime.cpp:185-186) */
+} arcllm_cuda_model_config;
+
+/* One decoder block (tensor names of runtime.cpp:190-197).  Norms and biases
+ * are fp32 device pointers; the type_* fields are ggml type ids. */
+typedef struct {
+    const float *attn_norm;
+    const void *wq; const float *bq; int type_q;
+    const void *wk; const float *bk; int type_k;
+    const void *wv; const float *bv; int type_v;
+    const void *wo; int type_o;
+    const float *ffn_norm;
+    const void *w_gate; const void *w_up; int type_gate_up;
+    const void *w_down; int type_down;
+} arcllm_cuda_layer;
+
+/* Counters mirrored into arcllm::v1::runtime::RuntimeStats (runtime.h:25-46):
+ * launches = kernel launches, graph launches = submits. */
+typedef struct {
+    uint32_t prefill_launches, prefill_graph_launches;
+    uint32_t decode_launches_per_step, decode_graph_launches_per_step, decode_steps;
+    float prefill_ms, decode_ms;
+    int finite;
+} arcllm_cuda_gen_stats;
+
+ARCLLM_CUDA_API int arcllm_cuda_model_create(const arcllm_cuda_model_config *cfg, arcllm_cuda_model **out);
+ARCLLM_CUDA_API int arcllm_cuda_model_destroy(arcllm_cuda_model *m);
+ARCLLM_CUDA_API int arcllm_cuda_model_set_layer(arcllm_cuda_model *m, uint32_t layer, const arcllm_cuda_layer *w);
+/* tok_embd_type: F16 (1, [vocab][hidden] halves) or Q4_K (12); output_type Q4_K/Q6_K */
+ARCLLM_CUDA_API int arcllm_cuda_model_set_endpoints(arcllm_cuda_model *m, const void *tok_embd, int tok_embd_type,
+                                                    const float *output_norm, const void *output, int output_type);
+/* Greedy generation: consumes the prompt (one step per token), then produces
+ * max_new tokens into out_tokens_host.  Synchronous on `stream`.  Fails with
+ * ARC_E_NONFINITE on non-finite logits (runtime.cpp:446,501). */
+ARCLLM_CUDA_API int arcllm_cuda_model_generate(arcllm_cuda_model *m, const uint32_t *prompt_host, uint32_t n_prompt,
+                                               uint32_t max_new, uint32_t *out_tokens_host,
+                                               arcllm_cuda_gen_stats *stats, void *stream);
+/* Step-level control (tests, benchmarks): begin() uploads the prompt and resets
+ * the device state; step() enqueues one token step (with_head: output norm +
+ * LM head + argmax) eagerly or as the captured graph. */
+ARCLLM_CUDA_API int arcllm_cuda_model_begin(arcllm_cuda_model *m, const uint32_t *prompt_host, uint32_t n_prompt,
+                                            uint32_t max_new, void *stream);
+ARCLLM_CUDA_API int arcllm_cuda_model_step(arcllm_cuda_model *m, int with_head, int use_graph, void *stream);
+/* Device pointers to the last logits [vocab] and to the K / V caches. */
+ARCLLM_CUDA_API int arcllm_cuda_model_logits(arcllm_cuda_model *m, const float **out);
+ARCLLM_CUDA_API int arcllm_cuda_model_kv_cache(arcllm_cuda_model *m, const uint16_t **k, const uint16_t **v);
+/* Restrict the LM head to rows [row0, row0+rows) (row sharding across GPUs;
+ * the other rows of the logits must be filled by the caller, e.g. all-gather). */
+ARCLLM_CUDA_API int arcllm_cuda_model_shard_lm_head(arcllm_cuda_model *m, uint32_t row0, uint32_t rows);
+
 #ifdef __cplusplus
 }
 #endif

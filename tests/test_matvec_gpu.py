@@ -191,8 +191,9 @@ def test_gateup_silu(rows, k):
     x = O.normal_f32(k, seed + 2)
     gamma = O.normal_f32(k, seed + 3, 1.0, 0.1)
     s = G.empty_f32(rows)
-    A.call("arcllm_cuda_gateup_silu_q4k", G.ptr(wg), G.ptr(wu), rows, k, G.ptr(G.to_dev(x)),
-           G.ptr(G.to_dev(gamma)), C.c_float(1e-6), G.ptr(s), G.stream())
+    xd, gd = G.to_dev(x), G.to_dev(gamma)  # keep both alive across the launch
+    A.call("arcllm_cuda_gateup_silu_q4k", G.ptr(wg), G.ptr(wu), rows, k, G.ptr(xd), G.ptr(gd), C.c_float(1e-6),
+           G.ptr(s), G.stream())
     xn = O.rmsnorm(x, gamma, 1e-6)
     g = O.matvec("q4k", O.fill_q4k(rows, k, seed), rows, k, xn, threads=8)
     u = O.matvec("q4k", O.fill_q4k(rows, k, seed + 1), rows, k, xn, threads=8)
