@@ -6,7 +6,7 @@ device by the library's counter-based fixture generators
 (``arcllm_cuda_fill_*``), one splitmix64 stream per tensor, so any tensor can
 be regenerated bit-for-bit elsewhere (the CPU test oracle does exactly that).
 
-Field distributions (the benchmark's config 3): Q4_K super-blocks with
+Field distributions (the benchmark's decode workload): Q4_K super-blocks with
 d ~ U[1e-3,4e-3), dmin ~ U[0,2e-3), 6-bit scales/mins and 4-bit codes uniform;
 Q6_K with uniform 6-bit codes, int8 scales in [-32,31], d ~ U[1e-3,4e-3);
 RMSNorm weights ~ N(1, 0.1); QKV biases ~ N(0, 0.02); fp16 embedding ~ N(0, 0.02)
