@@ -40,6 +40,7 @@ SIGNATURES = {
     "arcllm_cuda_rope_table": [_vp, _u32, _u32, _f32],
     "arcllm_cuda_rope_kv_store": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp],
     "arcllm_cuda_attention_decode": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp],
+    "arcllm_cuda_attention_decode_noalloc": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _vp],
     "arcllm_cuda_embed": [_i32, _vp, _vp, _u32, _u32, _vp, _vp],
     "arcllm_cuda_argmax": [_vp, _u32, _vp, C.POINTER(_u32), C.POINTER(_i32), _vp],
     "arcllm_cuda_set_device": [_i32],

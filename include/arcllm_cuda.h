@@ -149,6 +149,22 @@ ARCLLM_CUDA_API int arcllm_cuda_attention_decode(const float *q, const uint16_t 
                                                  const uint32_t *pos_dev, uint32_t q_heads, uint32_t kv_heads,
                                                  uint32_t head_dim, uint32_t max_ctx, uint32_t layer,
                                                  uint32_t n_splits, float *scratch, float *out, void *stream);
+/* Same computation as arcllm_cuda_attention_decode, for callers that cannot
+ * allocate device memory when they run a step (a host that fixes its device
+ * memory plan in advance, a latency-critical loop that must not risk the
+ * synchronisation cudaMalloc can cause, a plugin whose host owns the budget).
+ * No counterpart in the reference.  The slice partials live in a 65536-float
+ * (256 KiB) array inside the library, held on every GPU that loads it until
+ * exit; needs kv_heads*n_splits*(q_heads/kv_heads)*(head_dim+2) <= 65536, else
+ * ARC_E_UNSUPPORTED_SHAPE.  Allocates nothing.  All calls share the array:
+ * calls that overlap on the GPU race; calls ordered on one stream are fine.
+ * The first call on a device looks up the array's address (cudaGetSymbolAddress),
+ * so make it outside stream capture. */
+ARCLLM_CUDA_API int arcllm_cuda_attention_decode_noalloc(const float *q, const uint16_t *k_cache,
+                                                         const uint16_t *v_cache, const uint32_t *pos_dev,
+                                                         uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                                                         uint32_t max_ctx, uint32_t layer, uint32_t n_splits,
+                                                         float *out, void *stream);
 /* Embedding row *token_dev of an F16 (1) or Q4_K (12) table into out[hidden]
  * (shaders/p8c_embedding_q4k_segmented_probe.comp, runtime.cpp:373). */
 ARCLLM_CUDA_API int arcllm_cuda_embed(int type, const void *table, const uint32_t *token_dev, uint32_t hidden,
