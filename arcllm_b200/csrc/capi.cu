@@ -109,10 +109,8 @@ int arcllm_cuda_dequant_q6k(const void* w, uint64_t n_blocks, float* y, void* st
 int arcllm_cuda_matvec(int ggml_type, const void* w, uint32_t rows, uint32_t k, const float* x, const float* gamma,
                        float eps, const float* bias, const float* residual, float* y, void* stream) {
     ARC_GUARD_BEGIN
-    arc::MatvecPlan pl;
-    int st = arc::matvec_plan(ggml_type, false, rows, k, &pl);
-    if (st != ARC_OK) return st;
-    return arc::matvec_launch(pl, w, nullptr, x, gamma, eps, bias, residual, y, static_cast<cudaStream_t>(stream));
+    return arc::matvec_any(ggml_type, false, w, nullptr, rows, k, x, gamma, eps, bias, residual, y,
+                           static_cast<cudaStream_t>(stream));
     ARC_GUARD_END
 }
 
@@ -120,13 +118,10 @@ int arcllm_cuda_matvec_hostio(int ggml_type, const void* w, uint32_t rows, uint3
                               float* x_dev, float* y_dev, float* y_host, void* stream) {
     ARC_GUARD_BEGIN
     if (!x_host || !y_host || !x_dev || !y_dev) return set_error(ARC_E_INVALID_ARGUMENT, "matvec_hostio: null pointer");
-    arc::MatvecPlan pl;
-    int st = arc::matvec_plan(ggml_type, false, rows, k, &pl);
-    if (st != ARC_OK) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaMemcpyAsync(x_dev, x_host, sizeof(float) * k, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_hostio h2d");
-    st = arc::matvec_launch(pl, w, nullptr, x_dev, nullptr, 0.f, nullptr, nullptr, y_dev, s);
+    int st = arc::matvec_any(ggml_type, false, w, nullptr, rows, k, x_dev, nullptr, 0.f, nullptr, nullptr, y_dev, s);
     if (st != ARC_OK) return st;
     e = cudaMemcpyAsync(y_host, y_dev, sizeof(float) * rows, cudaMemcpyDeviceToHost, s);
     if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_hostio d2h");
@@ -149,11 +144,8 @@ int arcllm_cuda_matvec_q6k(const void* w, uint32_t rows, uint32_t k, const float
 int arcllm_cuda_gateup_silu_q4k(const void* w_gate, const void* w_up, uint32_t rows, uint32_t k, const float* x,
                                 const float* gamma, float eps, float* s, void* stream) {
     ARC_GUARD_BEGIN
-    arc::MatvecPlan pl;
-    int st = arc::matvec_plan(ARC_GGML_Q4_K, true, rows, k, &pl);
-    if (st != ARC_OK) return st;
-    return arc::matvec_launch(pl, w_gate, w_up, x, gamma, eps, nullptr, nullptr, s,
-                              static_cast<cudaStream_t>(stream));
+    return arc::matvec_any(ARC_GGML_Q4_K, true, w_gate, w_up, rows, k, x, gamma, eps, nullptr, nullptr, s,
+                           static_cast<cudaStream_t>(stream));
     ARC_GUARD_END
 }
 

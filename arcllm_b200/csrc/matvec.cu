@@ -35,34 +35,15 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <string>
 
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
+#include "matvec_common.cuh"
 
 namespace arc {
 
 namespace {
-
-constexpr int kMaxStages = 8;
-constexpr uint32_t kStagePad = 16;  // slack after each stage for 32-bit reads that run past a block
-
-struct MvParams {
-    const uint8_t* w0;
-    const uint8_t* w1;  // second matrix of the dual (gate/up) form
-    const float* x;
-    const float* gamma;  // fused RMSNorm weight (nullable)
-    float eps;
-    const float* bias;      // nullable
-    const float* residual;  // nullable
-    float* y;
-    unsigned int* err;  // device error word
-    uint32_t rows, k, nb, rb;
-    uint32_t G;  // rows per group (<= template G)
-    uint32_t n_groups;
-    uint32_t stages;
-    uint32_t stage_smem;  // bytes of one stage in smem (both matrices + pad)
-    uint32_t x_floats;    // padded x length in smem
-};
 
 // x lives in shared memory with 4 floats of padding every 64 so that the
 // eight lanes of a quarter-warp reading runs 64 floats apart hit distinct banks.
@@ -99,38 +80,6 @@ __device__ __forceinline__ void lds_u64_even(const uint8_t* base, uint32_t off, 
     const uint32_t w0 = p[0], w1 = p[1], w2 = p[2];
     lo = __funnelshift_r(w0, w1, sh);
     hi = __funnelshift_r(w1, w2, sh);
-}
-
-// Fold N per-row partial sums over the warp: afterwards lane L holds the full
-// sum of value index (L >> (5 - log2 N)).  One shuffle per value per step.
-template <int N>
-__device__ __forceinline__ float warp_fold(float (&v)[N], uint32_t lane) {
-    static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "N must be a power of two <= 32");
-    int n = N;
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-        if (n > 1) {
-            const int h = n >> 1;
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int i = 0; i < N / 2; ++i) {
-                if (i < h) {
-                    const float send = upper ? v[i] : v[i + h];
-                    const float keep = upper ? v[i + h] : v[i];
-                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-                }
-            }
-            n = h;
-        } else {
-            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
-        }
-    }
-    return v[0];
-}
-
-template <int N>
-constexpr int ilog2() {
-    return N <= 1 ? 0 : 1 + ilog2<N / 2>();
 }
 
 // ---------------------------------------------------------------------------
@@ -340,46 +289,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32) matvec_stream_kernel(const MvP
     __syncthreads();
 
     if (warp == NWC) {
-        // ---------------- producer warp ----------------
-        const uint64_t pol = l2_evict_first_policy();
-        uint32_t it = 0;
-        for (uint32_t grp = blockIdx.x; grp < p.n_groups; grp += gridDim.x, ++it) {
-            const uint32_t s = it % S;
-            if (it >= S) {
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(&empty[s], ((it / S) - 1u) & 1u, p.err);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok || *abort_flag) {
-                    if (lane == 0) *abort_flag = 1;
-                    break;
-                }
-            }
-            const uint32_t rows_g = min(p.G, p.rows - grp * p.G);
-            const uint32_t bytes = rows_g * p.rb;
-            const uint32_t bulk = bytes & ~15u;
-            uint8_t* dst = stages + s * p.stage_smem;
-            const uint64_t goff = (uint64_t)grp * p.G * p.rb;
-            if (bytes != bulk) {  // ragged final group: copy the last <16 bytes by hand
-                for (uint32_t i = bulk + lane; i < bytes; i += 32) {
-                    dst[i] = p.w0[goff + i];
-                    if (DUAL) dst[mat_off + i] = p.w1[goff + i];
-                }
-                __syncwarp();
-            }
-            if (lane == 0) {
-                mbar_arrive_expect_tx(&full[s], bulk * (DUAL ? 2u : 1u));
-                for (uint32_t o = 0; o < bulk; o += 32768u) {
-                    const uint32_t n = min(32768u, bulk - o);
-                    bulk_g2s(dst + o, p.w0 + goff + o, n, &full[s], pol);
-                    if (DUAL) bulk_g2s(dst + mat_off + o, p.w1 + goff + o, n, &full[s], pol);
-                }
-            }
-        }
-        // drain: no bulk copy may still be landing in this CTA's smem at exit
-        if (lane == 0 && *abort_flag) {
-            const uint32_t first = it > S ? it - S : 0;
-            for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1u, p.err);
-        }
+        produce_groups<DUAL>(p, stages, full, empty, abort_flag, mat_off, lane);
         return;
     }
 
@@ -628,6 +538,25 @@ int matvec_plan(int fmt, bool dual, uint32_t rows, uint32_t k, MatvecPlan* out) 
     const uint32_t sms = di.sms > 0 ? (uint32_t)di.sms : 148u;
     out->grid = std::min(out->n_groups, sms * ctas);
     return ARC_OK;
+}
+
+int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
+               const float* gamma, float eps, const float* bias, const float* residual, float* y,
+               cudaStream_t stream) {
+    // The CUDA-core kernel is the default: measured on B200 the tensor-core
+    // multiply-accumulate form was 9 % slower on the Q6_K LM head and 7 %
+    // faster on Q4_K K=3584 -- the integer unpack, not the FMAs, bounds both.
+    static int impl = -1;  // 0 = CUDA-core only, 1 = tensor-core where supported
+    if (impl < 0) {
+        const char* e = std::getenv("ARCLLM_MATVEC_IMPL");
+        impl = (e && std::string(e) == "mma") ? 1 : 0;
+    }
+    if (impl == 1 && matvec_mma_supported(fmt, dual, rows, k))
+        return matvec_mma_launch(fmt, dual, w0, w1, rows, k, x, gamma, eps, bias, residual, y, stream);
+    MatvecPlan pl;
+    int st = matvec_plan(fmt, dual, rows, k, &pl);
+    if (st != ARC_OK) return st;
+    return matvec_launch(pl, w0, w1, x, gamma, eps, bias, residual, y, stream);
 }
 
 int matvec_launch(const MatvecPlan& pl, const void* w0, const void* w1, const float* x, const float* gamma,

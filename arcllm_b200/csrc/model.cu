@@ -72,10 +72,7 @@ int check_layer(const arcllm_cuda_model_config& c, const arcllm_cuda_layer& L) {
 // Launch one matvec with a freshly computed plan (host-only arithmetic).
 int mv(int type, const void* w, uint32_t rows, uint32_t k, const float* x, const float* gamma, float eps,
        const float* bias, const float* residual, float* y, cudaStream_t st) {
-    MatvecPlan pl;
-    int r = matvec_plan(type, false, rows, k, &pl);
-    if (r != ARC_OK) return r;
-    return matvec_launch(pl, w, nullptr, x, gamma, eps, bias, residual, y, st);
+    return matvec_any(type, false, w, nullptr, rows, k, x, gamma, eps, bias, residual, y, st);
 }
 
 #define ARC_TRY(expr)          \
@@ -104,11 +101,8 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
                      1.0f / std::sqrt((float)c.head_dim)};
         ARC_TRY(launch_attention(m->q, m->kc, m->vc, &m->state->pos, as, m->part, m->attn, st));
         ARC_TRY(mv(L.type_o, L.wo, H, H, m->attn, nullptr, 0.f, nullptr, hc, hm, st));
-        {
-            MatvecPlan pl;
-            ARC_TRY(matvec_plan(ARC_GGML_Q4_K, true, c.ffn, H, &pl));
-            ARC_TRY(matvec_launch(pl, L.w_gate, L.w_up, hm, L.ffn_norm, c.rms_eps, nullptr, nullptr, m->s, st));
-        }
+        ARC_TRY(matvec_any(ARC_GGML_Q4_K, true, L.w_gate, L.w_up, c.ffn, H, hm, L.ffn_norm, c.rms_eps, nullptr,
+                           nullptr, m->s, st));
         ARC_TRY(mv(L.type_down, L.w_down, H, c.ffn, m->s, nullptr, 0.f, nullptr, hm, hc, st));
         n += 9;
     }
@@ -177,6 +171,7 @@ int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
         return set_error(ARC_E_UNSUPPORTED_SHAPE,
                          "model_create: needs hidden,ffn multiples of 256, head_dim 128, heads*head_dim == hidden");
     ARC_TRY(matvec_prepare());
+    ARC_TRY(matvec_mma_prepare());
     ARC_TRY(decode_ops_prepare());
     if (!dev_error_word()) return set_error(ARC_E_CUDA, "model_create: device error word unavailable");
     auto* m = new (std::nothrow) arcllm_cuda_model();
