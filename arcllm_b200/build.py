@@ -1,9 +1,13 @@
-"""Build recipe for libarcllm_cuda.so (sm_100a only).
+"""Build recipe for libarcllm_cuda.so (sm_100a only) and the C++ host runtime.
 
 Compiles every ``csrc/*.cu`` with nvcc for ``-gencode arch=compute_100a,code=sm_100a``
 into objects under ``arcllm_b200/_build/`` and links them into the in-tree
-``arcllm_b200/libarcllm_cuda.so``.  The objects are rebuilt only when a
-source or header is newer.  nvcc cross-compiles, so this runs without a GPU.
+``arcllm_b200/libarcllm_cuda.so``.  The C++17 host runtime (``runtime/*.cpp``:
+GGUF reader, tensor store, Q4CudaBackend, ``arcllm::v1::runtime::generate``) is
+compiled with g++ into ``arcllm_b200/libarcllm_runtime.so`` linked against the
+CUDA library, plus the ``arcllm_b200/arcllm_v1_runtime_cli`` executable.
+Everything is rebuilt only when a source or header is newer.  nvcc
+cross-compiles, so this runs without a GPU.
 """
 import argparse
 import concurrent.futures as cf
@@ -17,6 +21,11 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OUT = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libarcllm_cuda.so")
+RT_SRC = os.path.join(PKG, "runtime")
+RT_LIB = os.path.join(PKG, "libarcllm_runtime.so")
+RT_CLI = os.path.join(PKG, "arcllm_v1_runtime_cli")
+CXX = os.environ.get("CXX", "g++")
+CXXFLAGS = ["-std=c++17", "-O2", "-fPIC", "-Wall", "-Wextra", "-I", os.path.join(ROOT, "include")]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
@@ -67,6 +76,30 @@ def build(force=False, verbose_ptxas=False, jobs=None):
     return LIB, logs
 
 
+def _stale(target, deps):
+    return not os.path.exists(target) or os.path.getmtime(target) < max(os.path.getmtime(d) for d in deps)
+
+
+def build_runtime(force=False):
+    """g++ the host runtime into libarcllm_runtime.so (+ the CLI), linked to libarcllm_cuda.so."""
+    srcs = sorted(s for s in glob.glob(os.path.join(RT_SRC, "*.cpp")) if not s.endswith("_cli.cpp"))
+    hdrs = glob.glob(os.path.join(ROOT, "include", "*.h")) + glob.glob(os.path.join(ROOT, "include", "arcllm", "v1",
+                                                                                    "*.h"))
+    deps = srcs + hdrs + [LIB, __file__]
+    if force or _stale(RT_LIB, deps):
+        tmp = RT_LIB + ".tmp%d" % os.getpid()
+        _run([CXX] + CXXFLAGS + ["-shared", "-o", tmp] + srcs +
+             ["-L", PKG, "-larcllm_cuda", "-Wl,-rpath,$ORIGIN"])
+        os.replace(tmp, RT_LIB)
+    cli = os.path.join(RT_SRC, "runtime_cli.cpp")
+    if force or _stale(RT_CLI, [cli, RT_LIB] + hdrs):
+        tmp = RT_CLI + ".tmp%d" % os.getpid()
+        _run([CXX] + CXXFLAGS + ["-o", tmp, cli, "-L", PKG, "-larcllm_runtime", "-larcllm_cuda",
+                                 "-Wl,-rpath,$ORIGIN"])
+        os.replace(tmp, RT_CLI)
+    return RT_LIB, RT_CLI
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -77,6 +110,7 @@ def main(argv=None):
         if l.strip():
             print(l)
     print(lib)
+    print(*build_runtime(a.force))
 
 
 if __name__ == "__main__":

@@ -251,6 +251,18 @@ int arcllm_cuda_set_device(int device) {
     return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "set_device");
 }
 
+int arcllm_cuda_device_count(int* out) {
+    if (!out) return set_error(ARC_E_INVALID_ARGUMENT, "device_count: null out");
+    *out = 0;
+    const cudaError_t e = cudaGetDeviceCount(out);
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) {
+        cudaGetLastError();
+        *out = 0;
+        return ARC_OK;
+    }
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "device_count");
+}
+
 int arcllm_cuda_malloc(uint64_t bytes, void** out) {
     if (!out) return set_error(ARC_E_INVALID_ARGUMENT, "malloc: null out");
     const cudaError_t e = cudaMalloc(out, bytes);

@@ -1,0 +1,90 @@
+// Q4CudaBackend: the CUDA implementation of the ArcLLM Q4_K FFN-down backend.
+//
+// It implements binding_v4::BackendAdapter with the status semantics of the
+// reference's Vulkan backend (src/arcllm_v1_q4_vulkan_backend_v4_runtime.h:
+// acquire :210-275, validate :277-305, release :307-321, resolve_primitive
+// :323-345) so the reference's policy layer (binding_v4::apply_decision) can
+// drive it unchanged.  Primitive A is the plain Q4_K split-K matvec over the
+// GGUF layout (launch_ffn_down below, the counterpart of append_ffn_down_op
+// :347-385).  Primitive B, the re-laid-out EXEC148 image, is not provided by
+// this version: acquire() of B answers UNAVAILABLE and resolve_primitive(B)
+// PRIMITIVE_UNAVAILABLE, both with last_error() saying so.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "arcllm/v1/backend_adapter_v4.h"
+
+namespace arcllm::v1::cuda {
+
+// Ids of the Q4 FFN-down registration bundle
+// (src/registrations/arcllm_v1_q4k_down_reference_registration_v2.h:12-19).
+inline constexpr registry::CapabilityId kCapability{0x00010001ull};
+inline constexpr registry::PrimitiveId kPrimitiveA{0xA001ull};
+inline constexpr registry::PrimitiveId kPrimitiveB{0xB001ull};
+inline constexpr registry::AcquisitionPathId kAcquirePrimary{0xC101ull};
+inline constexpr registry::AcquisitionPathId kAcquireSecondary{0xC102ull};
+inline constexpr registry::AcquisitionPathId kAcquireTertiary{0xC103ull};
+inline constexpr registry::AcquisitionPathId kAcquireDisabledWarm{0xC104ull};
+
+struct BackendCounters {
+    std::uint64_t b_allocations = 0;
+    std::uint64_t b_materializations = 0;
+    std::uint64_t b_validations = 0;
+    std::uint64_t b_releases = 0;
+    std::uint64_t p1_calls = 0;
+    std::uint64_t p3_calls = 0;
+    std::uint64_t p0_calls = 0;
+    std::uint64_t resolve_a = 0;
+    std::uint64_t resolve_b = 0;
+};
+
+class Q4CudaBackend final : public binding_v4::BackendAdapter {
+public:
+    // One Q4_K ffn_down weight routed through this backend.
+    struct Source {
+        std::uint32_t layer = 0;
+        const void* device = nullptr;  // Q4_K rows in device memory, 16-byte aligned
+    };
+    // rows x k is the shape of every source (hidden x ffn); sidecar is the
+    // optional pre-materialised image path (acquisition P3).
+    Q4CudaBackend(std::vector<Source> sources, std::uint32_t rows, std::uint32_t k, std::string sidecar);
+    ~Q4CudaBackend() override;
+
+    binding_v4::BackendStatus acquire(registry::AcquisitionPathId path, registry::PrimitiveId target,
+                                      std::uint64_t residency_bytes,
+                                      binding_v4::RepresentationHandle& out) noexcept override;
+    binding_v4::BackendStatus validate(binding_v4::RepresentationHandle representation,
+                                       registry::CapabilityId capability,
+                                       registry::PrimitiveId target) noexcept override;
+    binding_v4::BackendStatus release(registry::PrimitiveId target,
+                                      binding_v4::RepresentationHandle representation) noexcept override;
+    binding_v4::BackendStatus resolve_primitive(registry::PrimitiveId primitive,
+                                                binding_v4::PrimitiveHandle& out) noexcept override;
+
+    // Enqueue y = W_down(layer) * s (+ residual) on `stream` with the primitive
+    // `handle` resolved above.  Returns an arcllm_cuda status (0 = OK).
+    int launch_ffn_down(binding_v4::PrimitiveHandle handle, std::uint32_t layer, const float* s,
+                        const float* residual, float* y, void* stream) const noexcept;
+
+    // Bytes of the EXEC148 image for all sources (148 B per Q4_K super-block).
+    std::uint64_t exec_family_bytes() const noexcept;
+    bool resident() const noexcept { return resident_; }
+    bool validated() const noexcept { return validated_; }
+    bool p3_available() const noexcept;
+    const BackendCounters& counters() const noexcept { return counters_; }
+    const std::string& last_error() const noexcept { return last_error_; }
+
+private:
+    const Source* find(std::uint32_t layer) const noexcept;
+    std::vector<Source> sources_;
+    std::uint32_t rows_, k_;
+    std::string sidecar_;
+    bool resident_ = false;
+    bool validated_ = false;
+    BackendCounters counters_{};
+    std::string last_error_;
+};
+
+}  // namespace arcllm::v1::cuda

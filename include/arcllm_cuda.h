@@ -178,6 +178,8 @@ ARCLLM_CUDA_API int arcllm_cuda_argmax(const float *logits, uint32_t n, void *sc
 
 /* ---- device memory and streams (for hosts that do not link the CUDA runtime) --- */
 ARCLLM_CUDA_API int arcllm_cuda_set_device(int device);
+/* Number of visible CUDA devices (0 when none); fails only on a driver error. */
+ARCLLM_CUDA_API int arcllm_cuda_device_count(int *out);
 ARCLLM_CUDA_API int arcllm_cuda_malloc(uint64_t bytes, void **out);
 ARCLLM_CUDA_API int arcllm_cuda_free(void *p);
 ARCLLM_CUDA_API int arcllm_cuda_memcpy_h2d(void *dst, const void *src_host, uint64_t bytes, void *stream);
