@@ -32,14 +32,15 @@ struct MatvecPlan {
 // call before capturing launches into a CUDA graph.
 int matvec_prepare();
 int matvec_plan(int fmt, bool dual, uint32_t rows, uint32_t k, MatvecPlan* out);
-// Tensor-core multiply-accumulate variant (matvec_mma.cu), K/256 <= 14.
-int matvec_mma_prepare();
-bool matvec_mma_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
-int matvec_mma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
-                      const float* gamma, float eps, const float* bias, const float* residual, float* y,
-                      cudaStream_t stream);
-// Pick the kernel for a matvec: the CUDA-core streaming form
-// (ARCLLM_MATVEC_IMPL=mma selects the tensor-core form where it applies).
+// Integer tensor-core variant (matvec_imma.cu), K/256 <= 14 (even for Q6_K).
+int matvec_imma_prepare();
+bool matvec_imma_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
+int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
+                       const float* gamma, float eps, const float* bias, const float* residual, float* y,
+                       cudaStream_t stream);
+// Pick the kernel for a matvec: the integer tensor-core form where it
+// applies, else the CUDA-core streaming form (ARCLLM_MATVEC_IMPL=cuda forces
+// the CUDA-core form).
 int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                const float* gamma, float eps, const float* bias, const float* residual, float* y,
                cudaStream_t stream);

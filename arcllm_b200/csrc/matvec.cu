@@ -543,16 +543,16 @@ int matvec_plan(int fmt, bool dual, uint32_t rows, uint32_t k, MatvecPlan* out) 
 int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                const float* gamma, float eps, const float* bias, const float* residual, float* y,
                cudaStream_t stream) {
-    // The CUDA-core kernel is the default: measured on B200 the tensor-core
-    // multiply-accumulate form was 9 % slower on the Q6_K LM head and 7 %
-    // faster on Q4_K K=3584 -- the integer unpack, not the FMAs, bounds both.
+    // Integer tensor-core kernel (matvec_imma.cu) wherever its shape rules
+    // hold (K <= 3584); the CUDA-core streaming kernel otherwise.
+    // ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core kernel (for comparisons).
     static int impl = -1;  // 0 = CUDA-core only, 1 = tensor-core where supported
     if (impl < 0) {
         const char* e = std::getenv("ARCLLM_MATVEC_IMPL");
-        impl = (e && std::string(e) == "mma") ? 1 : 0;
+        impl = (e && std::string(e) == "cuda") ? 0 : 1;
     }
-    if (impl == 1 && matvec_mma_supported(fmt, dual, rows, k))
-        return matvec_mma_launch(fmt, dual, w0, w1, rows, k, x, gamma, eps, bias, residual, y, stream);
+    if (impl == 1 && matvec_imma_supported(fmt, dual, rows, k))
+        return matvec_imma_launch(fmt, dual, w0, w1, rows, k, x, gamma, eps, bias, residual, y, stream);
     MatvecPlan pl;
     int st = matvec_plan(fmt, dual, rows, k, &pl);
     if (st != ARC_OK) return st;

@@ -171,7 +171,7 @@ int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
         return set_error(ARC_E_UNSUPPORTED_SHAPE,
                          "model_create: needs hidden,ffn multiples of 256, head_dim 128, heads*head_dim == hidden");
     ARC_TRY(matvec_prepare());
-    ARC_TRY(matvec_mma_prepare());
+    ARC_TRY(matvec_imma_prepare());
     ARC_TRY(decode_ops_prepare());
     if (!dev_error_word()) return set_error(ARC_E_CUDA, "model_create: device error word unavailable");
     auto* m = new (std::nothrow) arcllm_cuda_model();

@@ -221,3 +221,35 @@ def test_matvec_rejects_bad_arguments():
     assert L.arcllm_cuda_status_string(st) == b"ARC_E_INVALID_ARGUMENT"
     st = L.arcllm_cuda_matvec(7, G.ptr(w), 8, 512, G.ptr(x), None, C.c_float(0), None, None, G.ptr(y), G.stream())
     assert L.arcllm_cuda_status_string(st) == b"ARC_E_INVALID_ARGUMENT"
+
+
+@pytest.mark.parametrize("fmt", ["q4k", "q6k"])
+@pytest.mark.parametrize("scale", [1e-30, 1.0, 1e25])
+def test_matvec_x_dynamic_range(fmt, scale):
+    """Activations far from unit scale, with per-block outliers: the matvec
+    must stay within the tolerance relative to ||x|| at any magnitude."""
+    rows, k, seed = 96, 3584, 777
+    w = gpu_fill(fmt, rows, k, seed)
+    x = O.normal_f32(k, seed + 1)
+    x[::97] *= 1000.0  # one large value in many 32-element blocks
+    x[5:40] = 0.0      # an all-zero block and a partly zero one
+    x = (x.astype(np.float64) * scale).astype(np.float32)
+    y = run_matvec(fmt, w, rows, k, x)
+    y_ref = O.matvec(fmt, O.fill_weights(fmt, rows, k, seed), rows, k, x, threads=8)
+    assert_matvec_close(y, y_ref, x, max_abs_w(fmt, w, rows, k), "%s x scale %g" % (fmt, scale))
+
+
+@pytest.mark.parametrize("fmt", ["q4k", "q6k"])
+@pytest.mark.parametrize("bad", [np.nan, np.inf])
+def test_matvec_nonfinite_x_propagates(fmt, bad):
+    """A non-finite activation makes every output non-finite, as the
+    reference's fp32 loop does (the runtime then refuses the logits)."""
+    rows, k, seed = 40, 3584, 778
+    w = gpu_fill(fmt, rows, k, seed)
+    x = O.normal_f32(k, seed + 1)
+    x[1234] = bad
+    y = run_matvec(fmt, w, rows, k, x)
+    y_ref = O.matvec(fmt, O.fill_weights(fmt, rows, k, seed), rows, k, x, threads=8)
+    assert not np.isfinite(y_ref).any()
+    assert not np.isfinite(y).any()
+    G.check_device_error()
