@@ -544,14 +544,16 @@ int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows
                const float* gamma, float eps, const float* bias, const float* residual, float* y,
                cudaStream_t stream) {
     // Integer tensor-core kernel (matvec_imma.cu) wherever its shape rules
-    // hold (K <= 3584); the CUDA-core streaming kernel otherwise.
+    // hold (K <= 3584, 16-byte aligned x and gamma); the CUDA-core streaming
+    // kernel otherwise.
     // ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core kernel (for comparisons).
     static int impl = -1;  // 0 = CUDA-core only, 1 = tensor-core where supported
     if (impl < 0) {
         const char* e = std::getenv("ARCLLM_MATVEC_IMPL");
         impl = (e && std::string(e) == "cuda") ? 0 : 1;
     }
-    if (impl == 1 && matvec_imma_supported(fmt, dual, rows, k))
+    const bool x_aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma)) & 15u) == 0u;
+    if (impl == 1 && x_aligned && matvec_imma_supported(fmt, dual, rows, k))
         return matvec_imma_launch(fmt, dual, w0, w1, rows, k, x, gamma, eps, bias, residual, y, stream);
     MatvecPlan pl;
     int st = matvec_plan(fmt, dual, rows, k, &pl);

@@ -235,10 +235,20 @@ def main(argv=None):
     ap.add_argument("--fmt", default="q6k", choices=["q6k", "q4k"], help="profiling override of the workload")
     ap.add_argument("--rows", type=int, default=LM_ROWS, help="profiling override of the workload")
     ap.add_argument("--k", type=int, default=HIDDEN, help="profiling override of the workload")
+    ap.add_argument("--only", choices=["decode"], help="profiling: run only the config-3 decode and print its result")
+    ap.add_argument("--decode-prompt", type=int, default=256)
+    ap.add_argument("--decode-new", type=int, default=128)
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return run_reference(args)
+    if args.only == "decode":
+        import torch
+
+        import arcllm_b200 as A
+        torch.cuda.set_device(0)
+        print(json.dumps(run_decode(A, torch, measured_peaks()[0], args.decode_prompt, args.decode_new)), flush=True)
+        return 0
 
     import numpy as np
     import torch
@@ -396,7 +406,7 @@ def main(argv=None):
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "kernel": "matvec_stream_kernel (%s)" % fmt,
+                "kernel": "matvec_imma_kernel (%s)" % fmt,
                 "kernel_ms": round(kern_ms, 5), "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
             },
             "e2e": {"value": None if e2e_val is None else round(e2e_val, 2), "unit": "GB/s",
@@ -418,19 +428,30 @@ def main(argv=None):
 
 def run_extra(A, L, torch, dev, sp, hbm_peak):
     """Configs 0, 1b and 2 at N=1 (each timed over rotating weight copies whose
-    total exceeds 3x L2, CUDA events, 200 launches after 10 warm-ups)."""
+    total exceeds 3x L2; 200 launches after 10 warm-ups, captured in one CUDA
+    graph and timed with CUDA events)."""
     out = {}
 
     def timed(launch, n_iter=200, warm=10):
+        """Device time per launch: the n_iter launches are captured into one
+        CUDA graph (so host launch overhead does not gap the stream) and the
+        graph replay is timed with CUDA events on its stream."""
         for i in range(warm):
-            launch(i)
+            launch(i, sp)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for i in range(n_iter):
+                launch(i, cs)
+        g.replay()  # warm replay
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for i in range(n_iter):
-            launch(i)
+        g.replay()
         b.record()
         torch.cuda.synchronize()
+        del g
         return a.elapsed_time(b) / n_iter
 
     def copies(nbytes):
@@ -459,9 +480,9 @@ def run_extra(A, L, torch, dev, sp, hbm_peak):
         ws = make_w(fmt, rows, k, n, 0x100)
         ty = A.GGML_Q4_K if fmt == "q4k" else A.GGML_Q6_K
 
-        def launch(i, ws=ws, ty=ty, rows=rows, k=k, xv=xv, yv=yv):
+        def launch(i, stream, ws=ws, ty=ty, rows=rows, k=k, xv=xv, yv=yv):
             st = L.arcllm_cuda_matvec(ty, C.c_void_p(ws[i % len(ws)].data_ptr()), rows, k, C.c_void_p(xv.data_ptr()),
-                                      None, C.c_float(0), None, None, C.c_void_p(yv.data_ptr()), sp)
+                                      None, C.c_float(0), None, None, C.c_void_p(yv.data_ptr()), stream)
             if st:
                 A.check(st, name)
 
@@ -483,14 +504,14 @@ def run_extra(A, L, torch, dev, sp, hbm_peak):
     s = torch.empty(FFN, dtype=torch.float32, device=dev)
     h = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
 
-    def ffn(i):
+    def ffn(i, stream):
         c = i % n
         A.check(L.arcllm_cuda_gateup_silu_q4k(C.c_void_p(wg[c].data_ptr()), C.c_void_p(wu[c].data_ptr()), FFN, HIDDEN,
                                               C.c_void_p(x35.data_ptr()), C.c_void_p(gamma.data_ptr()),
-                                              C.c_float(1e-6), C.c_void_p(s.data_ptr()), sp), "gateup")
+                                              C.c_float(1e-6), C.c_void_p(s.data_ptr()), stream), "gateup")
         A.check(L.arcllm_cuda_matvec(A.GGML_Q4_K, C.c_void_p(wd[c].data_ptr()), HIDDEN, FFN, C.c_void_p(s.data_ptr()),
                                      None, C.c_float(0), None, C.c_void_p(x35.data_ptr()), C.c_void_p(h.data_ptr()),
-                                     sp), "down")
+                                     stream), "down")
 
     ms = timed(ffn, n_iter=100)
     alg = 3 * q_bytes("q4k", FFN, HIDDEN) + 4 * (HIDDEN * 3 + FFN * 2)
@@ -511,7 +532,7 @@ def run_decode(A, torch, hbm_peak, n_prompt=256, max_new=128):
     from arcllm_b200.synthetic import QWEN25_7B, SyntheticModel
     m = SyntheticModel(QWEN25_7B, seed=0xC3)
     prompt = [int(splitmix_token(i, QWEN25_7B["vocab"])) for i in range(n_prompt)]
-    m.generate(prompt[:8], 4)  # warm-up: captures the two step graphs
+    m.generate(prompt[:min(8, n_prompt)], 4)  # warm-up: captures the two step graphs
     t0 = time.perf_counter()
     toks, st = m.generate(prompt, max_new)
     wall = time.perf_counter() - t0
