@@ -18,6 +18,41 @@ int set_cuda_error(cudaError_t e, const char* where);
 // (nullptr if it cannot be resolved).
 unsigned int* dev_error_word();
 
+// Programmatic dependent launch (PDL).  While a PdlScope is active on this
+// thread, kernels are launched with programmatic stream serialization: the
+// next kernel may start while the previous one drains, every kernel waits
+// (griddepcontrol.wait) before touching its predecessors' outputs, and the
+// matvecs stream their weights before that wait.  Only code whose weights are
+// not written by the preceding kernels may enable it (the model's decode
+// graphs); ARCLLM_PDL=0 disables it.
+bool pdl_enabled();
+class PdlScope {
+public:
+    explicit PdlScope(bool on);
+    ~PdlScope();
+private:
+    bool prev_;
+};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (pdl_enabled()) {
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
 struct MatvecPlan {
     int fmt = 0;
     bool dual = false;
@@ -38,9 +73,19 @@ bool matvec_imma_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
 int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                        const float* gamma, float eps, const float* bias, const float* residual, float* y,
                        cudaStream_t stream);
+// Integer tensor-core split-K variant (matvec_imma_splitk.cu) for K > 3584.
+// It adds CTA partials through a per-device scratch: launches of it on one
+// device must not overlap in time (one stream, or ordered streams).
+// matvec_splitk_reserve sizes that scratch ahead of graph capture.
+int matvec_splitk_prepare();
+int matvec_splitk_reserve(int fmt, uint32_t rows, uint32_t k);
+bool matvec_splitk_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
+int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, const float* x, const float* gamma,
+                         float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
 // Pick the kernel for a matvec: the integer tensor-core form where it
-// applies, else the CUDA-core streaming form (ARCLLM_MATVEC_IMPL=cuda forces
-// the CUDA-core form).
+// applies (whole rows, K <= 3584), else the CUDA-core streaming form
+// (ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core form, =splitk opts K > 3584
+// into the split-K tensor-core form).
 int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                const float* gamma, float eps, const float* bias, const float* residual, float* y,
                cudaStream_t stream);

@@ -4,6 +4,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
@@ -33,6 +34,21 @@ unsigned int* dev_error_word() {
     }
     return slot;
 }
+
+namespace {
+thread_local bool g_pdl = false;
+bool pdl_allowed() {
+    static const bool allowed = [] {
+        const char* e = std::getenv("ARCLLM_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return allowed;
+}
+}  // namespace
+
+bool pdl_enabled() { return g_pdl && pdl_allowed(); }
+PdlScope::PdlScope(bool on) : prev_(g_pdl) { g_pdl = on; }
+PdlScope::~PdlScope() { g_pdl = prev_; }
 
 int set_error(int status, const char* msg) {
     std::snprintf(g_msg, sizeof g_msg, "%s", msg ? msg : "");

@@ -118,6 +118,13 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
 
 // Bit-level fp16 -> fp32 (normal, subnormal, inf and NaN payload preserved),
 // so dequantised values match the reference's half_to_float bit for bit.
+// Programmatic dependent launch: pdl_wait() blocks until the grids this one
+// depends on have completed and their writes are visible (a no-op for a
+// launch without a programmatic dependency); pdl_trigger() lets the dependent
+// grid be scheduled once every CTA of this grid has triggered or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
     const uint32_t sign = (h & 0x8000u) << 16;
     const uint32_t exp = (h >> 10) & 0x1fu;

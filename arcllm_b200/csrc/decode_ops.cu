@@ -31,6 +31,8 @@ namespace {
 
 __global__ void embed_f16_kernel(const uint16_t* __restrict__ table, const uint32_t* __restrict__ token_src,
                                  uint32_t h, uint32_t vocab, float* __restrict__ out, unsigned int* err) {
+    pdl_trigger();
+    pdl_wait();  // inputs come from the preceding kernels
     const uint32_t tok = *token_src;
     if (tok >= vocab) {
         if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, ARC_DEV_ERR_BOUNDS);
@@ -43,6 +45,8 @@ __global__ void embed_f16_kernel(const uint16_t* __restrict__ table, const uint3
 
 __global__ void embed_q4k_kernel(const uint8_t* __restrict__ table, const uint32_t* __restrict__ token_src,
                                  uint32_t h, uint32_t vocab, float* __restrict__ out, unsigned int* err) {
+    pdl_trigger();
+    pdl_wait();  // inputs come from the preceding kernels
     const uint32_t tok = *token_src;
     if (tok >= vocab) {
         if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, ARC_DEV_ERR_BOUNDS);
@@ -77,6 +81,8 @@ __global__ void rope_kv_store_kernel(float* __restrict__ q, float* __restrict__ 
                                      const float2* __restrict__ table, const uint32_t* __restrict__ pos_src,
                                      uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, RopeKvShape s,
                                      unsigned int* err) {
+    pdl_trigger();
+    pdl_wait();  // inputs come from the preceding kernels
     const uint32_t pos = *pos_src;
     if (pos >= s.max_ctx) {
         if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, ARC_DEV_ERR_BOUNDS);
@@ -120,6 +126,8 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
                                                            const uint16_t* __restrict__ vc,
                                                            const uint32_t* __restrict__ pos_src, AttnShape s,
                                                            float* __restrict__ part) {
+    pdl_trigger();
+    pdl_wait();  // inputs come from the preceding kernels
     constexpr int D = 128, NW = 8;
     __shared__ float sm_m[NW][GQ], sm_l[NW][GQ];
     __shared__ float sm_acc[NW][GQ][D];
@@ -198,6 +206,8 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
 
 __global__ void attn_merge_kernel(const float* __restrict__ part, const uint32_t* __restrict__ pos_src, AttnShape s,
                                   uint32_t gq, float* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();  // inputs come from the preceding kernels
     constexpr int D = 128;
     const uint32_t qh = blockIdx.x, d = threadIdx.x;
     const uint32_t kvh = qh / gq, g = qh - kvh * gq;
@@ -228,6 +238,8 @@ __device__ __forceinline__ uint32_t f2ord(float f) {
 // among equal values, the smallest index (the reference's strict '>' scan).
 __global__ void argmax_key_kernel(const float* __restrict__ logits, uint32_t n, unsigned long long* key_out,
                                   uint32_t* nonfinite_out) {
+    pdl_trigger();
+    pdl_wait();  // inputs come from the preceding kernels
     unsigned long long best = 0ull;
     uint32_t nonfinite = 0;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -255,6 +267,8 @@ __global__ void argmax_key_kernel(const float* __restrict__ logits, uint32_t n, 
 // prompt is being consumed, else the greedy argmax; record generated tokens.
 __global__ void greedy_finalize_kernel(GreedyState* st, const uint32_t* __restrict__ prompt, uint32_t* out_tokens,
                                        uint32_t max_out) {
+    pdl_trigger();
+    pdl_wait();  // inputs come from the preceding kernels
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     const uint32_t pos = st->pos;
     uint32_t next;
@@ -290,27 +304,29 @@ int decode_ops_prepare() {
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "decode ops prepare");
 }
 
+int launch_checked(cudaError_t e, const char* what) { return e == cudaSuccess ? ARC_OK : set_cuda_error(e, what); }
+
 int launch_embed(int type, const void* table, const uint32_t* token_src, uint32_t h, uint32_t vocab, float* out,
                  cudaStream_t stream) {
     if (type == 1)
-        embed_f16_kernel<<<(h + 255) / 256, 256, 0, stream>>>(static_cast<const uint16_t*>(table), token_src, h, vocab,
-                                                             out, dev_error_word());
-    else if (type == 12)
-        embed_q4k_kernel<<<h / 256, 256, 0, stream>>>(static_cast<const uint8_t*>(table), token_src, h, vocab, out,
-                                                     dev_error_word());
-    else
-        return set_error(ARC_E_UNSUPPORTED_SHAPE, "embedding: type must be F16 (1) or Q4_K (12)");
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "embed launch");
+        return launch_checked(launch_kernel(embed_f16_kernel, dim3((h + 255) / 256), dim3(256), 0, stream,
+                                            static_cast<const uint16_t*>(table), token_src, h, vocab, out,
+                                            dev_error_word()),
+                              "embed launch");
+    if (type == 12)
+        return launch_checked(launch_kernel(embed_q4k_kernel, dim3(h / 256), dim3(256), 0, stream,
+                                            static_cast<const uint8_t*>(table), token_src, h, vocab, out,
+                                            dev_error_word()),
+                              "embed launch");
+    return set_error(ARC_E_UNSUPPORTED_SHAPE, "embedding: type must be F16 (1) or Q4_K (12)");
 }
 
 int launch_rope_kv_store(float* q, float* k, const float* v, const float2* table, const uint32_t* pos_src,
                          uint16_t* kc, uint16_t* vc, const RopeKvShape& s, cudaStream_t stream) {
     const uint32_t pairs = (s.q_heads + s.kv_heads) * (s.head_dim / 2u);
-    rope_kv_store_kernel<<<(pairs + 127) / 128, 128, 0, stream>>>(q, k, v, table, pos_src, kc, vc, s,
-                                                                  dev_error_word());
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "rope_kv_store launch");
+    return launch_checked(launch_kernel(rope_kv_store_kernel, dim3((pairs + 127) / 128), dim3(128), 0, stream, q, k, v,
+                                        table, pos_src, kc, vc, s, dev_error_word()),
+                          "rope_kv_store launch");
 }
 
 int launch_attention(const float* q, const uint16_t* kc, const uint16_t* vc, const uint32_t* pos_src,
@@ -320,31 +336,30 @@ int launch_attention(const float* q, const uint16_t* kc, const uint16_t* vc, con
     if (gq * s.kv_heads != s.q_heads || gq > 8u || gq == 0u)
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: q_heads must be 1..8 x kv_heads");
     dim3 grid(s.n_splits, s.kv_heads);
+    cudaError_t e;
     switch (gq) {
-        case 1: attn_partial_kernel<1><<<grid, 256, 0, stream>>>(q, kc, vc, pos_src, s, part); break;
-        case 2: attn_partial_kernel<2><<<grid, 256, 0, stream>>>(q, kc, vc, pos_src, s, part); break;
-        case 4: attn_partial_kernel<4><<<grid, 256, 0, stream>>>(q, kc, vc, pos_src, s, part); break;
-        case 7: attn_partial_kernel<7><<<grid, 256, 0, stream>>>(q, kc, vc, pos_src, s, part); break;
-        case 8: attn_partial_kernel<8><<<grid, 256, 0, stream>>>(q, kc, vc, pos_src, s, part); break;
+        case 1: e = launch_kernel(attn_partial_kernel<1>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
+        case 2: e = launch_kernel(attn_partial_kernel<2>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
+        case 4: e = launch_kernel(attn_partial_kernel<4>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
+        case 7: e = launch_kernel(attn_partial_kernel<7>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
+        case 8: e = launch_kernel(attn_partial_kernel<8>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
         default: return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: q heads per kv head must be 1, 2, 4, 7 or 8");
     }
-    attn_merge_kernel<<<s.q_heads, 128, 0, stream>>>(part, pos_src, s, gq, out);
-    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = launch_kernel(attn_merge_kernel, dim3(s.q_heads), dim3(128), 0, stream, part, pos_src, s, gq, out);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "attention launch");
 }
 
 int launch_argmax(const float* logits, uint32_t n, unsigned long long* key, uint32_t* nonfinite,
                   cudaStream_t stream) {
-    argmax_key_kernel<<<148, 256, 0, stream>>>(logits, n, key, nonfinite);
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "argmax launch");
+    return launch_checked(launch_kernel(argmax_key_kernel, dim3(148), dim3(256), 0, stream, logits, n, key, nonfinite),
+                          "argmax launch");
 }
 
 int launch_greedy_finalize(GreedyState* st, const uint32_t* prompt, uint32_t* out_tokens, uint32_t max_out,
                            cudaStream_t stream) {
-    greedy_finalize_kernel<<<1, 32, 0, stream>>>(st, prompt, out_tokens, max_out);
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "finalize launch");
+    return launch_checked(launch_kernel(greedy_finalize_kernel, dim3(1), dim3(32), 0, stream, st, prompt, out_tokens,
+                                        max_out),
+                          "finalize launch");
 }
 
 }  // namespace arc

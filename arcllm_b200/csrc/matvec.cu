@@ -35,6 +35,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "arcllm_cuda_internal.h"
@@ -276,6 +277,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32) matvec_stream_kernel(const MvP
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t S = p.stages;
     const uint32_t mat_off = p.G * p.rb;  // offset of the second matrix inside a stage
+    pdl_trigger();
 
     if (tid == NT) {
         for (uint32_t s = 0; s < S; ++s) {
@@ -294,6 +296,7 @@ __global__ void __launch_bounds__((NWC + 1) * 32) matvec_stream_kernel(const MvP
     }
 
     // ---------------- consumer warps ----------------
+    pdl_wait();  // x, gamma, bias and residual come from the preceding kernels
     // stage x once (optionally RMS-normalised as src/p8c_segmented_access_correctness.cpp:958-969)
     float inv = 1.0f;
     if (p.gamma) {
@@ -433,8 +436,8 @@ template <int FMT, int G, bool DUAL, bool XREG, int NWC>
 cudaError_t launch_t(const MvParams& p, uint32_t smem, uint32_t grid, cudaStream_t stream) {
     cudaError_t e = prepare_all();
     if (e != cudaSuccess) return e;
-    matvec_stream_kernel<FMT, G, DUAL, XREG, NWC><<<grid, (NWC + 1) * 32, smem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_kernel(matvec_stream_kernel<FMT, G, DUAL, XREG, NWC>, dim3(grid), dim3((NWC + 1) * 32), smem, stream,
+                         p);
 }
 
 template <int FMT, int G, bool DUAL>
@@ -545,16 +548,17 @@ int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows
                cudaStream_t stream) {
     // Integer tensor-core kernel (matvec_imma.cu) wherever its shape rules
     // hold (K <= 3584, 16-byte aligned x and gamma); the CUDA-core streaming
-    // kernel otherwise.
-    // ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core kernel (for comparisons).
-    static int impl = -1;  // 0 = CUDA-core only, 1 = tensor-core where supported
-    if (impl < 0) {
-        const char* e = std::getenv("ARCLLM_MATVEC_IMPL");
-        impl = (e && std::string(e) == "cuda") ? 0 : 1;
-    }
+    // kernel otherwise.  ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core kernel;
+    // ARCLLM_MATVEC_IMPL=splitk routes K > 3584 to the split-K tensor-core
+    // kernel (matvec_imma_splitk.cu), which measured slower than the CUDA-core
+    // kernel on B200 for the FFN down shape and is therefore not the default.
+    const char* env = std::getenv("ARCLLM_MATVEC_IMPL");
+    const int impl = !env ? 1 : (std::strcmp(env, "cuda") == 0 ? 0 : (std::strcmp(env, "splitk") == 0 ? 2 : 1));
     const bool x_aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma)) & 15u) == 0u;
-    if (impl == 1 && x_aligned && matvec_imma_supported(fmt, dual, rows, k))
+    if (impl >= 1 && x_aligned && matvec_imma_supported(fmt, dual, rows, k))
         return matvec_imma_launch(fmt, dual, w0, w1, rows, k, x, gamma, eps, bias, residual, y, stream);
+    if (impl == 2 && x_aligned && matvec_splitk_supported(fmt, dual, rows, k))
+        return matvec_splitk_launch(fmt, w0, rows, k, x, gamma, eps, bias, residual, y, stream);
     MatvecPlan pl;
     int st = matvec_plan(fmt, dual, rows, k, &pl);
     if (st != ARC_OK) return st;
@@ -585,6 +589,7 @@ int matvec_launch(const MatvecPlan& pl, const void* w0, const void* w1, const fl
     p.stages = pl.stages;
     p.stage_smem = pl.stage_smem;
     p.x_floats = pl.x_floats;
+    p.early = pdl_enabled() ? 1u : 0u;
     cudaError_t e;
     if (pl.fmt == 12) {
         if (pl.dual) {

@@ -29,6 +29,7 @@ struct MvParams {
     uint32_t stages;
     uint32_t stage_smem;  // bytes of one stage in smem (both matrices + pad)
     uint32_t x_floats;    // padded x length in smem
+    uint32_t early;       // 1: weights may be streamed before the PDL wait (they are not written upstream)
 };
 
 // Fold N per-row partial sums over the warp: afterwards lane L holds the full
@@ -74,6 +75,7 @@ __device__ __forceinline__ void produce_groups(const MvParams& p, uint8_t* stage
                                                volatile int* abort_flag, uint32_t mat_off, uint32_t lane) {
     const uint32_t S = p.stages;
     const uint64_t pol = l2_evict_first_policy();
+    if (!p.early) pdl_wait();
     uint32_t it = 0;
     for (uint32_t grp = blockIdx.x; grp < p.n_groups; grp += gridDim.x, ++it) {
         const uint32_t s = it % S;

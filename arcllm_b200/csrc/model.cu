@@ -127,7 +127,11 @@ int capture(arcllm_cuda_model* m, bool with_head, cudaGraphExec_t* out, uint32_t
         cudaStreamDestroy(cs);
         return set_cuda_error(e, "begin capture");
     }
-    int st = enqueue_step(m, with_head, cs, n_launch);
+    int st;
+    {
+        PdlScope pdl(true);  // weights are constant for the graph's lifetime
+        st = enqueue_step(m, with_head, cs, n_launch);
+    }
     cudaGraph_t g = nullptr;
     e = cudaStreamEndCapture(cs, &g);
     cudaStreamDestroy(cs);
@@ -172,6 +176,8 @@ int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
                          "model_create: needs hidden,ffn multiples of 256, head_dim 128, heads*head_dim == hidden");
     ARC_TRY(matvec_prepare());
     ARC_TRY(matvec_imma_prepare());
+    ARC_TRY(matvec_splitk_prepare());
+    ARC_TRY(matvec_splitk_reserve(ARC_GGML_Q4_K, cfg->hidden, cfg->ffn));  // FFN down, before any graph capture
     ARC_TRY(decode_ops_prepare());
     if (!dev_error_word()) return set_error(ARC_E_CUDA, "model_create: device error word unavailable");
     auto* m = new (std::nothrow) arcllm_cuda_model();

@@ -128,7 +128,17 @@ CASES = [
     ("q4k", 37, 512),
     ("q6k", 13, 18944),
     ("q6k", 5, 768),        # odd block count per row
+    ("q4k", 1, 18944),
+    ("q6k", 2, 4096),
+    ("q4k", 40, 4608),
+    ("q6k", 700, 18944),
 ]
+
+# split-K tensor-core kernel (opt-in for K > 3584): single row, several 32-row
+# groups, ragged last group, K not a multiple of the 6-super-block chunk, more
+# work units than SMs, a 13-row matrix whose last row ends inside a 16-byte word
+SPLITK_CASES = [("q4k", 1, 18944), ("q6k", 2, 4096), ("q4k", 40, 4608), ("q6k", 700, 18944), ("q6k", 13, 18944),
+                ("q4k", 3584, 18944), ("q6k", 3584, 18944)]
 
 
 @pytest.mark.parametrize("fmt,rows,k", CASES)
@@ -141,6 +151,26 @@ def test_matvec_parity(fmt, rows, k):
     y_ref = O.matvec(fmt, O.fill_weights(fmt, rows, k, seed), rows, k, x, bias, threads=8)
     assert_matvec_close(y, y_ref, x, max_abs_w(fmt, w, rows, k), "%s %dx%d" % (fmt, rows, k))
     G.check_device_error()
+
+
+@pytest.mark.parametrize("fmt,rows,k", SPLITK_CASES)
+def test_matvec_splitk_parity(fmt, rows, k, monkeypatch):
+    monkeypatch.setenv("ARCLLM_MATVEC_IMPL", "splitk")
+    test_matvec_parity(fmt, rows, k)
+
+
+@pytest.mark.parametrize("fmt", ["q4k", "q6k"])
+def test_matvec_splitk_rmsnorm_residual(fmt, monkeypatch):
+    monkeypatch.setenv("ARCLLM_MATVEC_IMPL", "splitk")
+    rows, k, seed = 200, 18944, 4343
+    w = gpu_fill(fmt, rows, k, seed)
+    x = O.normal_f32(k, seed + 1)
+    gamma = O.normal_f32(k, seed + 2, 1.0, 0.1)
+    res = O.normal_f32(rows, seed + 3)
+    y = run_matvec(fmt, w, rows, k, x, gamma=gamma, residual=res)
+    xn = O.rmsnorm(x, gamma, 1e-6)
+    y_ref = O.add(res, O.matvec(fmt, O.fill_weights(fmt, rows, k, seed), rows, k, xn, threads=8))
+    assert_matvec_close(y, y_ref, xn, max_abs_w(fmt, w, rows, k), fmt + " split-K rmsnorm+residual")
 
 
 @pytest.mark.parametrize("fmt", ["q4k", "q6k"])
