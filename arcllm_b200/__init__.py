@@ -33,6 +33,7 @@ SIGNATURES = {
     "arcllm_cuda_matvec_q4k": [_vp, _u32, _u32, _vp, _vp, _vp, _vp],
     "arcllm_cuda_matvec_q6k": [_vp, _u32, _u32, _vp, _vp, _vp, _vp],
     "arcllm_cuda_gateup_silu_q4k": [_vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp],
+    "arcllm_cuda_gemm_q4k_bf16": [_vp, _u32, _u32, _vp, _u32, _vp, _vp],
     "arcllm_cuda_fill_q4k": [_vp, _u64, _u64, _u64, _vp],
     "arcllm_cuda_fill_q6k": [_vp, _u64, _u64, _u64, _vp],
     "arcllm_cuda_fill_normal_f32": [_vp, _u64, _u64, _u64, _f32, _f32, _vp],

@@ -92,6 +92,11 @@ int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows
 int matvec_launch(const MatvecPlan& pl, const void* w0, const void* w1, const float* x, const float* gamma,
                   float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
 
+// Prefill GEMM on tcgen05 (gemm_tcgen05.cu).
+int gemm_q4k_bf16_prepare();
+int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,
+                  cudaStream_t stream);
+
 std::vector<float> rope_table(uint32_t max_ctx, uint32_t head_dim, float theta);
 int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out);
 int model_destroy(arcllm_cuda_model* m);

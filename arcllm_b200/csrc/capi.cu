@@ -165,6 +165,13 @@ int arcllm_cuda_gateup_silu_q4k(const void* w_gate, const void* w_up, uint32_t r
     ARC_GUARD_END
 }
 
+int arcllm_cuda_gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x_bf16, uint32_t m, float* y,
+                              void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::gemm_q4k_bf16(w, n, k, x_bf16, m, y, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_fill_q4k(void* w, uint64_t block_begin, uint64_t n_blocks, uint64_t seed, void* stream) {
     ARC_GUARD_BEGIN
     return arc::fill_blocks(12, w, block_begin, n_blocks, seed, static_cast<cudaStream_t>(stream));

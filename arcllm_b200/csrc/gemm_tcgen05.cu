@@ -1,0 +1,344 @@
+// Prefill GEMM on the 5th-generation tensor cores: Y[M x N] (fp32) =
+// X[M x K] (bf16) * W^T with W the N x K Q4_K matrix of a projection, M <= 256
+// prompt tokens.  The counterpart of the reference's prefill kernels
+// (shaders/p7l_ffn_q4k_gateup_fused.comp, shaders/p7g_ffn_q4k_tiled16.comp:
+// weights dequantised into shared memory, then a tiled multiply), rebuilt for
+// sm_100a with tcgen05.mma, TMEM accumulators and TMA.
+//
+// One CTA computes all M (<= 256) rows x 128 columns of Y:
+//   warp 0      TMA producer: two 128-row boxes of X per 64-wide K step
+//               (128-byte swizzle, the UMMA K-major SW128 layout);
+//   warp 1      allocates 256 TMEM columns (two 128x128 fp32 accumulators)
+//               and issues tcgen05.mma (M=128, N=128, K=16, bf16 x bf16 -> f32)
+//               from one thread, committing each stage back to its "empty"
+//               barrier;
+//   warps 2..5  dequantise the 128 W rows x 64 K of each stage from Q4_K to
+//               bf16 straight into the swizzled layout (one row per thread),
+//               then read the accumulators back with tcgen05.ld and store Y.
+// Both MMAs of a K step share the dequantised B tile, so each weight is
+// dequantised once per CTA.  All waits are bounded; on a timeout the kernel
+// sets the device error word, lets in-flight copies and MMAs finish (bounded),
+// frees its TMEM and returns.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "arcllm_cuda_internal.h"
+#include "common.cuh"
+
+namespace arc {
+namespace {
+
+constexpr uint32_t kBN = 128;          // output columns per CTA
+constexpr uint32_t kBK = 64;           // K per stage (128 bytes of bf16: one swizzle row)
+constexpr uint32_t kStages = 4;
+constexpr uint32_t kAHalf = 128 * kBK * 2;   // 16 KB: one 128-row box of X
+constexpr uint32_t kBTile = kBN * kBK * 2;   // 16 KB: dequantised W tile
+constexpr uint32_t kStageBytes = 2 * kAHalf + kBTile;  // 48 KB
+constexpr uint32_t kThreads = 6 * 32;
+constexpr uint32_t kTmemCols = 256;
+
+struct GemmSmemTail {
+    uint64_t full_a[kStages];
+    uint64_t full_b[kStages];
+    uint64_t empty[kStages];
+    uint64_t done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + sizeof(GemmSmemTail) + 1024;  // + alignment slack
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// UMMA shared-memory descriptor for a K-major tile in the 128-byte swizzle
+// layout: 8-row x 128-byte atoms stacked along M/N (stride 1024 bytes).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);        // start address / 16
+    d |= (uint64_t)1u << 16;                         // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024u >> 4) << 32;               // stride byte offset: 8 rows x 128 B
+    d |= (uint64_t)1u << 46;                         // descriptor version (sm_100)
+    d |= (uint64_t)2u << 61;                         // layout: 128-byte swizzle
+    return d;
+}
+
+// kind::f16 instruction descriptor: bf16 A and B (K-major), f32 accumulator, M=128, N=128
+constexpr uint32_t kIdesc = (1u << 4)          // D format f32
+                            | (1u << 7)        // A format bf16
+                            | (1u << 10)       // B format bf16
+                            | ((kBN >> 3) << 17)
+                            | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :
+        : "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :
+        : "r"(tmem_d), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Dequantise 64 weights (one Q4_K row, K elements kb*64 .. +63) to bf16 and
+// store them as row n of the swizzled B tile.
+__device__ __forceinline__ void dequant_row_chunk(const uint8_t* __restrict__ row, uint32_t kb, uint32_t n,
+                                                  uint8_t* btile) {
+    const uint32_t sb = kb >> 2, c = kb & 3u;
+    const uint8_t* blk = row + sb * 144u;
+    const uint4 hd = ld_nc_v4(blk);
+    const uint4 q0 = ld_nc_v4(blk + 16u + 32u * c);
+    const uint4 q1 = ld_nc_v4(blk + 32u + 32u * c);
+    // scale/min of sub-blocks 2c (low nibbles) and 2c+1 (high nibbles):
+    // src/p8c_segmented_access_correctness.cpp:531-540
+    const uint32_t S[3] = {hd.y, hd.z, hd.w};  // scale bytes 0..11
+    auto sbyte = [&](uint32_t i) { return (S[i >> 2] >> (8u * (i & 3u))) & 0xFFu; };
+    float scl[2], mns[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t j = 2u * c + h;
+        uint32_t sc, mn;
+        if (j < 4) {
+            sc = sbyte(j) & 63u;
+            mn = sbyte(j + 4) & 63u;
+        } else {
+            sc = (sbyte(j + 4) & 15u) | ((sbyte(j - 4) >> 6) << 4);
+            mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
+        }
+        scl[h] = (float)sc;
+        mns[h] = (float)mn;
+    }
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+    const float f0 = d * scl[0], o0 = dmin * mns[0], f1 = d * scl[1], o1 = dmin * mns[1];
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    uint8_t* rowbase = btile + (n >> 3) * 1024u + (n & 7u) * 128u;
+#pragma unroll
+    for (int c16 = 0; c16 < 8; ++c16) {
+        // chunk c16 holds elements 8*c16 .. +7: low nibbles of bytes 8*c16.. for c16 < 4, high nibbles after
+        const bool hi = c16 >= 4;
+        const uint32_t wa = w[2 * (c16 & 3)], wb = w[2 * (c16 & 3) + 1];
+        const float f = hi ? f1 : f0, o = hi ? o1 : o0;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t byte = ((i < 4 ? wa : wb) >> (8 * (i & 3))) & 0xFFu;
+            const uint32_t q = hi ? (byte >> 4) : (byte & 15u);
+            v[i] = fmaf(f, (float)q, -o);
+        }
+        const uint4 packed = make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
+        *reinterpret_cast<uint4*>(rowbase + ((c16 ^ (n & 7u)) << 4)) = packed;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_q4k_bf16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w, uint32_t n_total,
+                         uint32_t k, uint32_t m, float* __restrict__ y, unsigned int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + kStages * kStageBytes);
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const uint32_t n0 = blockIdx.x * kBN;
+    const uint32_t nkb = k / kBK;
+    const uint32_t rb = (k / 256u) * 144u;
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < kStages; ++s) {
+            mbar_init(&tail->full_a[s], 1);
+            mbar_init(&tail->full_b[s], 4);
+            mbar_init(&tail->empty[s], 1);
+        }
+        mbar_init(&tail->done, 1);
+        tail->abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {  // TMEM: two 128x128 fp32 accumulators
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tail->tmem_base)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = tail->tmem_base;
+    volatile int* abort_flag = &tail->abort_flag;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (X) ----------------
+        uint32_t issued = 0;
+        if (lane == 0) {
+            for (uint32_t kb = 0; kb < nkb; ++kb) {
+                const uint32_t s = kb % kStages;
+                if (kb >= kStages && !mbar_wait(&tail->empty[s], ((kb / kStages) - 1u) & 1u, err)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                if (*abort_flag) break;
+                uint8_t* st = smem + s * kStageBytes;
+                mbar_arrive_expect_tx(&tail->full_a[s], 2 * kAHalf);
+                tma_load_2d(smem_u32(st), &xmap, (int)(kb * kBK), 0, &tail->full_a[s]);
+                tma_load_2d(smem_u32(st + kAHalf), &xmap, (int)(kb * kBK), 128, &tail->full_a[s]);
+                ++issued;
+            }
+            if (*abort_flag)  // no copy may still be landing at exit
+                for (uint32_t j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
+                    mbar_wait(&tail->full_a[j % kStages], (j / kStages) & 1u, err);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            for (uint32_t kb = 0; kb < nkb; ++kb) {
+                const uint32_t s = kb % kStages, ph = (kb / kStages) & 1u;
+                if (!mbar_wait(&tail->full_a[s], ph, err) || !mbar_wait(&tail->full_b[s], ph, err)) *abort_flag = 1;
+                if (*abort_flag) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t st = smem_u32(smem + s * kStageBytes);
+#pragma unroll
+                for (uint32_t kk = 0; kk < kBK / 16u; ++kk) {
+                    const uint64_t db = sw128_desc(st + 2 * kAHalf + 32u * kk);
+                    const uint32_t acc = (kb | kk) != 0u;
+                    umma_bf16(tmem, sw128_desc(st + 32u * kk), db, acc);
+                    umma_bf16(tmem + 128u, sw128_desc(st + kAHalf + 32u * kk), db, acc);
+                }
+                umma_commit(&tail->empty[s]);  // stage free once these MMAs have read it
+            }
+            umma_commit(&tail->done);  // accumulators complete (also after an abort: drains issued MMAs)
+        }
+    } else {
+        // ---------------- dequant producers, then epilogue ----------------
+        const uint32_t dt = tid - 64u;  // 0..127: W row of this CTA
+        const uint8_t* row = w + (uint64_t)(n0 + dt) * rb;
+        for (uint32_t kb = 0; kb < nkb; ++kb) {
+            const uint32_t s = kb % kStages;
+            bool ok = true;
+            if (kb >= kStages) {
+                if (lane == 0) ok = mbar_wait(&tail->empty[s], ((kb / kStages) - 1u) & 1u, err);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+            }
+            if (!ok) *abort_flag = 1;
+            if (*abort_flag) break;
+            dequant_row_chunk(row, kb, dt, smem + s * kStageBytes + 2 * kAHalf);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tail->full_b[s]);
+        }
+        // epilogue: warp (2..5) % 4 owns TMEM lanes 32*q .. 32*q+31
+        const bool ok = mbar_wait(&tail->done, 0, err);
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const uint32_t q = warp & 3u;
+        const bool store = ok && !*abort_flag;
+#pragma unroll 1
+        for (uint32_t acc = 0; acc < 2; ++acc) {
+#pragma unroll 1
+            for (uint32_t cb = 0; cb < kBN / 32u; ++cb) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((32u * q) << 16) + acc * 128u + cb * 32u, r);
+                const uint32_t mrow = acc * 128u + 32u * q + lane;
+                if (store && mrow < m) {
+                    float4* dst = reinterpret_cast<float4*>(y + (uint64_t)mrow * n_total + n0 + cb * 32u);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                             __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+}  // namespace
+
+int gemm_q4k_bf16_prepare() {
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (done[dev & 63]) return ARC_OK;
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemm_q4k_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return set_cuda_error(e, "gemm prepare");
+    done[dev & 63] = true;
+    return ARC_OK;
+}
+
+int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,
+                  cudaStream_t stream) {
+    if (!w || !x || !y) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: null pointer");
+    if (m == 0 || m > 256 || n == 0 || n % kBN || k == 0 || k % 256u)
+        return set_error(ARC_E_UNSUPPORTED_SHAPE, "gemm: needs 1 <= M <= 256, N % 128 == 0, K % 256 == 0");
+    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u)
+        return set_error(ARC_E_ALIGNMENT, "gemm: W, X and Y must be 16-byte aligned");
+    int st = gemm_q4k_bf16_prepare();
+    if (st != ARC_OK) return st;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(ARC_E_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {k, m};
+    const cuuint64_t strides[1] = {(cuuint64_t)k * 2u};
+    const cuuint32_t box[2] = {kBK, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: tensor map for X rejected");
+    const cudaError_t e = launch_kernel(gemm_q4k_bf16_kernel, dim3(n / kBN), dim3(kThreads), kSmemBytes, stream, map,
+                                        static_cast<const uint8_t*>(w), n, k, m, y, dev_error_word());
+    return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "gemm launch");
+}
+
+}  // namespace arc

@@ -113,6 +113,16 @@ ARCLLM_CUDA_API int arcllm_cuda_matvec_hostio(int ggml_type, const void *w, uint
 ARCLLM_CUDA_API int arcllm_cuda_gateup_silu_q4k(const void *w_gate, const void *w_up, uint32_t rows, uint32_t k,
                                 const float *x, const float *gamma, float eps, float *s, void *stream);
 
+/* Prefill GEMM (config 4) on the tcgen05 tensor cores: y[m][n] (fp32, row-major)
+ * = x[m][k] (bf16, row-major) * W^T for the n x k Q4_K matrix W, weights
+ * dequantised to bf16 in shared memory, fp32 accumulation in TMEM.  Replaces
+ * the prefill kernels shaders/p7l_ffn_q4k_gateup_fused.comp:22-38 and
+ * shaders/p7g_ffn_q4k_tiled16.comp:15-34 (PCGemm/PCFusedGU with batch = seq,
+ * src/arcllm_v1_runtime.cpp:343-366).  1 <= m <= 256, n % 128 == 0,
+ * k % 256 == 0; w, x, y 16-byte aligned. */
+ARCLLM_CUDA_API int arcllm_cuda_gemm_q4k_bf16(const void *w, uint32_t n, uint32_t k, const uint16_t *x_bf16,
+                                              uint32_t m, float *y, void *stream);
+
 /* ---- synthetic fixture streams -------------------------------------------
  * Deterministic, counter-based generators (element n of a splitmix64
  * sequence), identical bit for bit to the CPU test oracle, so multi-GB
