@@ -12,9 +12,11 @@
 //               and issues tcgen05.mma (M=128, N=128, K=16, bf16 x bf16 -> f32)
 //               from one thread, committing each stage back to its "empty"
 //               barrier;
-//   warps 2..5  dequantise the 128 W rows x 64 K of each stage from Q4_K to
-//               bf16 straight into the swizzled layout (one row per thread),
-//               then read the accumulators back with tcgen05.ld and store Y.
+//   warps 2..9  dequantise the 128 W rows x 64 K of each stage from Q4_K to
+//               bf16 straight into the swizzled layout (one 32-weight
+//               sub-block per thread, packed bytes prefetched 4 stages
+//               ahead), then read the accumulators back with tcgen05.ld
+//               (warp w serves TMEM lanes 32*(w%4)..) and store Y.
 // Both MMAs of a K step share the dequantised B tile, so each weight is
 // dequantised once per CTA.  All waits are bounded; on a timeout the kernel
 // sets the device error word, lets in-flight copies and MMAs finish (bounded),
@@ -36,7 +38,8 @@ constexpr uint32_t kStages = 4;
 constexpr uint32_t kAHalf = 128 * kBK * 2;   // 16 KB: one 128-row box of X
 constexpr uint32_t kBTile = kBN * kBK * 2;   // 16 KB: dequantised W tile
 constexpr uint32_t kStageBytes = 2 * kAHalf + kBTile;  // 48 KB
-constexpr uint32_t kThreads = 6 * 32;
+constexpr uint32_t kDqWarps = 8;                         // dequantising warps: 2 threads per W row
+constexpr uint32_t kThreads = (2 + kDqWarps) * 32;
 constexpr uint32_t kTmemCols = 256;
 
 struct GemmSmemTail {
@@ -114,23 +117,30 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
     return r;
 }
 
-// Dequantise 64 weights (one Q4_K row, K elements kb*64 .. +63) to bf16 and
-// store them as row n of the swizzled B tile.
-__device__ __forceinline__ void dequant_row_chunk(const uint8_t* __restrict__ row, uint32_t kb, uint32_t n,
-                                                  uint8_t* btile) {
-    const uint32_t sb = kb >> 2, c = kb & 3u;
-    const uint8_t* blk = row + sb * 144u;
-    const uint4 hd = ld_nc_v4(blk);
-    const uint4 q0 = ld_nc_v4(blk + 16u + 32u * c);
-    const uint4 q1 = ld_nc_v4(blk + 32u + 32u * c);
-    // scale/min of sub-blocks 2c (low nibbles) and 2c+1 (high nibbles):
-    // src/p8c_segmented_access_correctness.cpp:531-540
-    const uint32_t S[3] = {hd.y, hd.z, hd.w};  // scale bytes 0..11
+// bf16x2 arithmetic on raw bits (both halves)
+__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t bfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// Per super-block constants of one thread's sub-blocks 2c + hi (c = 0..3):
+// scale f = d*sc and offset -(dmin*mn), each rounded to bf16 and broadcast to
+// both halves of a bf16x2.  src/p8c_segmented_access_correctness.cpp:531-540
+// (scale/min unpacking), :1166-1181 (w = d*sc*q - dmin*mn).
+__device__ __forceinline__ void subblock_consts(uint4 hd, uint32_t hi, uint32_t (&fb)[4], uint32_t (&ob)[4]) {
+    const uint32_t S[3] = {hd.y, hd.z, hd.w};
     auto sbyte = [&](uint32_t i) { return (S[i >> 2] >> (8u * (i & 3u))) & 0xFFu; };
-    float scl[2], mns[2];
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint32_t j = 2u * c + h;
+    for (uint32_t c = 0; c < 4; ++c) {
+        const uint32_t j = 2u * c + hi;
         uint32_t sc, mn;
         if (j < 4) {
             sc = sbyte(j) & 63u;
@@ -139,29 +149,34 @@ __device__ __forceinline__ void dequant_row_chunk(const uint8_t* __restrict__ ro
             sc = (sbyte(j + 4) & 15u) | ((sbyte(j - 4) >> 6) << 4);
             mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
         }
-        scl[h] = (float)sc;
-        mns[h] = (float)mn;
+        fb[c] = bf16x2(d * (float)sc, d * (float)sc);
+        ob[c] = bf16x2(-(dmin * (float)mn), -(dmin * (float)mn));
     }
-    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
-    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
-    const float f0 = d * scl[0], o0 = dmin * mns[0], f1 = d * scl[1], o1 = dmin * mns[1];
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+}
+
+// Dequantise the 32 weights of sub-block 2c+hi of one Q4_K row -- elements
+// 32*hi .. +31 of the 64-element stage row, the low (hi=0) or high (hi=1)
+// nibbles of its 32 code bytes -- to bf16 pairs: q as bf16 via 128+q (exact)
+// minus 128, then one bf16x2 FMA q*f - o (one rounding).  Stored as 16-byte
+// chunks 4*hi .. 4*hi+3 of row n of the swizzled B tile.
+__device__ __forceinline__ void dequant_subblock(uint4 q0, uint4 q1, uint32_t fb, uint32_t ob, uint32_t n, uint32_t hi,
+                                                 uint8_t* btile) {
+    const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     uint8_t* rowbase = btile + (n >> 3) * 1024u + (n & 7u) * 128u;
+    constexpr uint32_t k128 = 0x43004300u;  // bf16x2(128, 128)
 #pragma unroll
-    for (int c16 = 0; c16 < 8; ++c16) {
-        // chunk c16 holds elements 8*c16 .. +7: low nibbles of bytes 8*c16.. for c16 < 4, high nibbles after
-        const bool hi = c16 >= 4;
-        const uint32_t wa = w[2 * (c16 & 3)], wb = w[2 * (c16 & 3) + 1];
-        const float f = hi ? f1 : f0, o = hi ? o1 : o0;
-        float v[8];
+    for (int ch = 0; ch < 4; ++ch) {  // output chunk: elements 8*ch .. +7 = code bytes 8*ch .. +7
+        uint32_t out[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t byte = ((i < 4 ? wa : wb) >> (8 * (i & 3))) & 0xFFu;
-            const uint32_t q = hi ? (byte >> 4) : (byte & 15u);
-            v[i] = fmaf(f, (float)q, -o);
+        for (int pr = 0; pr < 4; ++pr) {
+            const uint32_t word = w8[2 * ch + (pr >> 1)];
+            // bytes (2*(pr&1), 2*(pr&1)+1) of the word into the low byte of each 16-bit half
+            const uint32_t spread = __byte_perm(word, 0u, (pr & 1) ? 0x4342u : 0x4140u);
+            const uint32_t q = hi ? ((spread >> 4) & 0x000F000Fu) : (spread & 0x000F000Fu);
+            out[pr] = bfma2(bsub2(q | k128, k128), fb, ob);
         }
-        const uint4 packed = make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
-        *reinterpret_cast<uint4*>(rowbase + ((c16 ^ (n & 7u)) << 4)) = packed;
+        const uint32_t chunk = 4u * hi + ch;
+        *reinterpret_cast<uint4*>(rowbase + ((chunk ^ (n & 7u)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
     }
 }
 
@@ -179,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
         for (uint32_t s = 0; s < kStages; ++s) {
             mbar_init(&tail->full_a[s], 1);
-            mbar_init(&tail->full_b[s], 4);
+            mbar_init(&tail->full_b[s], kDqWarps);
             mbar_init(&tail->empty[s], 1);
         }
         mbar_init(&tail->done, 1);
@@ -240,31 +255,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------- dequant producers, then epilogue ----------------
-        const uint32_t dt = tid - 64u;  // 0..127: W row of this CTA
-        const uint8_t* row = w + (uint64_t)(n0 + dt) * rb;
-        for (uint32_t kb = 0; kb < nkb; ++kb) {
-            const uint32_t s = kb % kStages;
-            bool ok = true;
-            if (kb >= kStages) {
-                if (lane == 0) ok = mbar_wait(&tail->empty[s], ((kb / kStages) - 1u) & 1u, err);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
+        const uint32_t dt = tid - 64u;  // 0..255: W row dt >> 1 of this CTA, sub-block half dt & 1 of the stage
+        const uint32_t nrow = dt >> 1, hi = dt & 1u;
+        const uint8_t* row = w + (uint64_t)(n0 + nrow) * rb;
+        // the code bytes of stage kb are loaded kPrefetch stages ahead, so
+        // global-memory latency overlaps the dequantisation of earlier stages;
+        // scales are unpacked once per super-block (every 4 stages)
+        constexpr uint32_t kPrefetch = 4;
+        uint4 pq0[kPrefetch], pq1[kPrefetch];
+        auto load_codes = [&](uint32_t kb, uint4& a, uint4& b) {
+            const uint8_t* blk = row + (kb >> 2) * 144u + 16u + 32u * (kb & 3u);
+            a = ld_nc_v4(blk);
+            b = ld_nc_v4(blk + 16u);
+        };
+#pragma unroll
+        for (uint32_t i = 0; i < kPrefetch; ++i)
+            if (i < nkb) load_codes(i, pq0[i], pq1[i]);
+        uint4 hd_next = ld_nc_v4(row);
+        uint32_t fb[4], ob[4];
+        bool stop = false;
+        for (uint32_t kb0 = 0; kb0 < nkb && !stop; kb0 += kPrefetch) {  // kPrefetch == 4: one super-block
+            subblock_consts(hd_next, hi, fb, ob);
+            if (kb0 + 4u < nkb) hd_next = ld_nc_v4(row + ((kb0 >> 2) + 1u) * 144u);
+#pragma unroll
+            for (uint32_t i = 0; i < kPrefetch; ++i) {
+                const uint32_t kb = kb0 + i;
+                if (kb >= nkb) break;
+                const uint4 c0 = pq0[i], c1 = pq1[i];
+                if (kb + kPrefetch < nkb) load_codes(kb + kPrefetch, pq0[i], pq1[i]);
+                const uint32_t s = kb % kStages;
+                bool ok = true;
+                if (kb >= kStages) {
+                    if (lane == 0) ok = mbar_wait(&tail->empty[s], ((kb / kStages) - 1u) & 1u, err);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                }
+                if (!ok) *abort_flag = 1;
+                if (*abort_flag) {
+                    stop = true;
+                    break;
+                }
+                dequant_subblock(c0, c1, fb[i], ob[i], nrow, hi, smem + s * kStageBytes + 2 * kAHalf);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tail->full_b[s]);
             }
-            if (!ok) *abort_flag = 1;
-            if (*abort_flag) break;
-            dequant_row_chunk(row, kb, dt, smem + s * kStageBytes + 2 * kAHalf);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tail->full_b[s]);
         }
         // epilogue: warp (2..5) % 4 owns TMEM lanes 32*q .. 32*q+31
         const bool ok = mbar_wait(&tail->done, 0, err);
         asm volatile("tcgen05.fence::after_thread_sync;");
-        const uint32_t q = warp & 3u;
+        const uint32_t q = warp & 3u, sub = (warp - 2u) >> 2;  // lane quarter; which of its 4 warps
         const bool store = ok && !*abort_flag;
 #pragma unroll 1
-        for (uint32_t acc = 0; acc < 2; ++acc) {
-#pragma unroll 1
-            for (uint32_t cb = 0; cb < kBN / 32u; ++cb) {
+        for (uint32_t pair = sub; pair < 2u * (kBN / 32u); pair += kDqWarps / 4u) {
+            const uint32_t acc = pair / (kBN / 32u), cb = pair % (kBN / 32u);
+            {
                 uint32_t r[32];
                 tmem_ld32(tmem + ((32u * q) << 16) + acc * 128u + cb * 32u, r);
                 const uint32_t mrow = acc * 128u + 32u * q + lane;

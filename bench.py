@@ -235,19 +235,25 @@ def main(argv=None):
     ap.add_argument("--fmt", default="q6k", choices=["q6k", "q4k"], help="profiling override of the workload")
     ap.add_argument("--rows", type=int, default=LM_ROWS, help="profiling override of the workload")
     ap.add_argument("--k", type=int, default=HIDDEN, help="profiling override of the workload")
-    ap.add_argument("--only", choices=["decode"], help="profiling: run only the config-3 decode and print its result")
+    ap.add_argument("--only", choices=["decode", "prefill"],
+                    help="profiling: run only the config-3 decode or the config-4 prefill GEMMs and print the result")
     ap.add_argument("--decode-prompt", type=int, default=256)
     ap.add_argument("--decode-new", type=int, default=128)
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return run_reference(args)
-    if args.only == "decode":
+    if args.only:
         import torch
 
         import arcllm_b200 as A
         torch.cuda.set_device(0)
-        print(json.dumps(run_decode(A, torch, measured_peaks()[0], args.decode_prompt, args.decode_new)), flush=True)
+        if args.only == "decode":
+            res = run_decode(A, torch, measured_peaks()[0], args.decode_prompt, args.decode_new)
+        else:
+            res = run_extra(A, A.lib(), torch, torch.device("cuda", 0),
+                            C.c_void_p(torch.cuda.current_stream().cuda_stream), measured_peaks()[0], which="prefill")
+        print(json.dumps(res), flush=True)
         return 0
 
     import numpy as np
@@ -426,7 +432,7 @@ def main(argv=None):
     return 0
 
 
-def run_extra(A, L, torch, dev, sp, hbm_peak):
+def run_extra(A, L, torch, dev, sp, hbm_peak, which="all"):
     """Configs 0, 1b and 2 at N=1 (each timed over rotating weight copies whose
     total exceeds 3x L2; 200 launches after 10 warm-ups, captured in one CUDA
     graph and timed with CUDA events)."""
@@ -465,6 +471,9 @@ def run_extra(A, L, torch, dev, sp, hbm_peak):
             A.call("arcllm_cuda_fill_" + fmt, C.c_void_p(t.data_ptr()), 0, rows * nb, seed + c, sp)
             ws.append(t)
         return ws
+
+    if which == "prefill":
+        return run_prefill_gemm(A, L, torch, dev, sp, timed, copies, make_w)
 
     x18 = torch.empty(FFN, dtype=torch.float32, device=dev)
     A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(x18.data_ptr()), 0, FFN, 0x77, C.c_float(0), C.c_float(1), sp)
@@ -520,7 +529,37 @@ def run_extra(A, L, torch, dev, sp, hbm_peak):
                                     "us": round(ms * 1e3, 2), "launches": 2}
     del wg, wu, wd
     torch.cuda.empty_cache()
+    out.update(run_prefill_gemm(A, L, torch, dev, sp, timed, copies, make_w))
     out["config3_decode"] = run_decode(A, torch, hbm_peak)
+    return out
+
+
+def run_prefill_gemm(A, L, torch, dev, sp, timed, copies, make_w, m=256):
+    """Config 4: the prefill GEMMs at M=256 prompt tokens on tcgen05 (bf16 x,
+    Q4_K weights dequantised to bf16 on chip, fp32 accumulation), over rotating
+    weight copies; TFLOP/s against the measured bf16 peak."""
+    _, tflops_peak, _ = measured_peaks()
+    out = {}
+    xf = torch.empty(m * FFN, dtype=torch.float32, device=dev)  # seeded N(0,1) activations, as bf16
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(xf.data_ptr()), 0, m * FFN, 0x7A, C.c_float(0), C.c_float(1), sp)
+    x = xf.to(torch.bfloat16)
+    for name, n, k in (("config4_prefill_gate_256x18944x3584", FFN, HIDDEN),
+                       ("config4_prefill_down_256x3584x18944", HIDDEN, FFN)):
+        nc = copies(q_bytes("q4k", n, k))
+        ws = make_w("q4k", n, k, nc, 0x500)
+        y = torch.empty(m, n, dtype=torch.float32, device=dev)
+
+        def launch(i, stream, ws=ws, n=n, k=k, y=y):
+            A.check(L.arcllm_cuda_gemm_q4k_bf16(C.c_void_p(ws[i % len(ws)].data_ptr()), n, k,
+                                                C.c_void_p(x.data_ptr()), m, C.c_void_p(y.data_ptr()), stream),
+                    "gemm")
+
+        ms = timed(launch, n_iter=50)
+        tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+        out[name] = {"TFLOP/s": round(tf, 1), "frac_of_bf16_peak": round(tf / tflops_peak, 4) if tflops_peak else None,
+                     "us": round(ms * 1e3, 2), "weight_copies": nc}
+        del ws
+        torch.cuda.empty_cache()
     return out
 
 

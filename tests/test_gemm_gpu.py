@@ -1,8 +1,8 @@
 """Prefill GEMM on tcgen05 (arcllm_cuda_gemm_q4k_bf16): y = x * W^T with x bf16
-[m x k], W Q4_K [n x k], fp32 accumulation.  Checked against the CPU oracle's
-bit-exact Q4_K dequantisation: tightly against the same product with W rounded
-to bf16 (what the tensor cores multiply), and at the row's stated 1e-2 rel-L2
-against the fp32 dequantised weights."""
+[m x k], W Q4_K [n x k], fp32 accumulation.  Checked tightly against the same
+product with W dequantised the way the kernel does it (bf16 scale and offset
+per sub-block, one bf16 rounding of q*f - o), and at the stated 1e-2 rel-L2
+against the CPU oracle's bit-exact fp32 dequantisation."""
 import ctypes as C
 
 import numpy as np
@@ -20,6 +20,32 @@ def bf16_round(a):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).to(torch.float32).numpy()
 
 
+def q4k_bf16_weights(w_host, n, k):
+    """The kernel's bf16 weights: f = bf16(d*sc), o = bf16(dmin*mn) per
+    sub-block, w = bf16(q*f - o) with one rounding."""
+    nb = k // 256
+    blk = w_host.reshape(n * nb, 144)
+    d = blk[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    dmin = blk[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
+    s = blk[:, 4:16].astype(np.int32)
+    sc = np.empty((n * nb, 8), np.int32)
+    mn = np.empty((n * nb, 8), np.int32)
+    for j in range(8):
+        if j < 4:
+            sc[:, j] = s[:, j] & 63
+            mn[:, j] = s[:, j + 4] & 63
+        else:
+            sc[:, j] = (s[:, j + 4] & 15) | ((s[:, j - 4] >> 6) << 4)
+            mn[:, j] = (s[:, j + 4] >> 4) | ((s[:, j] >> 6) << 4)
+    f = bf16_round((d[:, None] * sc.astype(np.float32)).astype(np.float32)).astype(np.float64)
+    o = bf16_round((dmin[:, None] * mn.astype(np.float32)).astype(np.float32)).astype(np.float64)
+    kk = np.arange(256)
+    byte = blk[:, 16 + (kk >> 6) * 32 + (kk & 31)].astype(np.int32)
+    q = np.where((kk & 63) < 32, byte & 15, byte >> 4).astype(np.float64)
+    w = q * f[:, kk >> 5] - o[:, kk >> 5]
+    return bf16_round(w.astype(np.float32)).reshape(n, k)
+
+
 def run_gemm(m, n, k, seed):
     w_host = O.fill_weights("q4k", n, k, seed)
     w = G.to_dev(w_host)
@@ -32,19 +58,19 @@ def run_gemm(m, n, k, seed):
     G.check_device_error()
     wd = O.dequant("q4k", w_host, n, k).reshape(n, k)
     xf = xb.float().cpu().numpy().astype(np.float64)
-    return y.cpu().numpy().astype(np.float64), xf, wd
+    return y.cpu().numpy().astype(np.float64), xf, wd, q4k_bf16_weights(w_host, n, k)
 
 
 @pytest.mark.parametrize("m,n,k", [(256, 128, 256), (256, 384, 3584), (100, 256, 1024), (1, 128, 512),
                                    (256, 18944, 3584)])
 def test_gemm_q4k_bf16(m, n, k):
-    y, xf, wd = run_gemm(m, n, k, 900 + m + n + k)
+    y, xf, wd, wb = run_gemm(m, n, k, 900 + m + n + k)
     assert np.isfinite(y).all()
-    y_b = xf @ bf16_round(wd).astype(np.float64).T      # what the tensor cores compute
+    y_b = xf @ wb.astype(np.float64).T                  # what the tensor cores compute
     y_f = xf @ wd.astype(np.float64).T                  # fp32 dequantised weights (the reference's)
     rel_b = np.linalg.norm(y - y_b) / np.linalg.norm(y_b)
     rel_f = np.linalg.norm(y - y_f) / np.linalg.norm(y_f)
-    print("gemm %dx%dx%d: rel-L2 %.2e (bf16 W), %.2e (fp32 W)" % (m, n, k, rel_b, rel_f))
+    print("gemm %dx%dx%d: rel-L2 %.2e (kernel's bf16 W), %.2e (fp32 W)" % (m, n, k, rel_b, rel_f))
     assert rel_b <= 1e-5
     assert rel_f <= 1e-2
 
