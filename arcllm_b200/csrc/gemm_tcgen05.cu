@@ -18,7 +18,9 @@
 //               ahead), then read the accumulators back with tcgen05.ld
 //               (warp w serves TMEM lanes 32*(w%4)..) and store Y.
 // Both MMAs of a K step share the dequantised B tile, so each weight is
-// dequantised once per CTA.  All waits are bounded; on a timeout the kernel
+// dequantised once per CTA.  When N/128 tiles leave SMs idle (the FFN-down
+// shape, N = 3584), K is split across CTAs and the partial tiles are added
+// in split order by the last CTA of each column tile.  All waits are bounded; on a timeout the kernel
 // sets the device error word, lets in-flight copies and MMAs finish (bounded),
 // frees its TMEM and returns.
 #include <cuda.h>
@@ -49,6 +51,16 @@ struct GemmSmemTail {
     uint64_t done;
     uint32_t tmem_base;
     int abort_flag;
+    int last_split;
+};
+
+// Split-K: CTAs (tile, split) cover K super-blocks [nsb*split/ks, nsb*(split+1)/ks).
+// Partial tiles go to ws[split][m][n]; the last CTA of a column tile to arrive
+// (per-tile counter) adds them in split order (deterministic) and writes y.
+struct SplitKWs {
+    float* ws;
+    uint32_t* cnt;  // per 128-column tile, zero between launches
+    uint32_t ks;
 };
 
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + sizeof(GemmSmemTail) + 1024;  // + alignment slack
@@ -182,13 +194,16 @@ __device__ __forceinline__ void dequant_subblock(uint4 q0, uint4 q1, uint32_t fb
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q4k_bf16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w, uint32_t n_total,
-                         uint32_t k, uint32_t m, float* __restrict__ y, unsigned int* err) {
+                         uint32_t k, uint32_t m, float* __restrict__ y, unsigned int* err, const SplitKWs sk) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + kStages * kStageBytes);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t n0 = blockIdx.x * kBN;
-    const uint32_t nkb = k / kBK;
+    const uint32_t nsb = k / 256u, split = blockIdx.y;
+    const uint32_t sb_begin = nsb * split / sk.ks, sb_end = nsb * (split + 1u) / sk.ks;
+    const uint32_t kbase = 4u * sb_begin;          // first 64-wide K block of this CTA
+    const uint32_t nkb = 4u * (sb_end - sb_begin);  // K blocks of this CTA
     const uint32_t rb = (k / 256u) * 144u;
 
     if (tid == 0) {
@@ -225,8 +240,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (*abort_flag) break;
                 uint8_t* st = smem + s * kStageBytes;
                 mbar_arrive_expect_tx(&tail->full_a[s], 2 * kAHalf);
-                tma_load_2d(smem_u32(st), &xmap, (int)(kb * kBK), 0, &tail->full_a[s]);
-                tma_load_2d(smem_u32(st + kAHalf), &xmap, (int)(kb * kBK), 128, &tail->full_a[s]);
+                tma_load_2d(smem_u32(st), &xmap, (int)((kbase + kb) * kBK), 0, &tail->full_a[s]);
+                tma_load_2d(smem_u32(st + kAHalf), &xmap, (int)((kbase + kb) * kBK), 128, &tail->full_a[s]);
                 ++issued;
             }
             if (*abort_flag)  // no copy may still be landing at exit
@@ -257,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- dequant producers, then epilogue ----------------
         const uint32_t dt = tid - 64u;  // 0..255: W row dt >> 1 of this CTA, sub-block half dt & 1 of the stage
         const uint32_t nrow = dt >> 1, hi = dt & 1u;
-        const uint8_t* row = w + (uint64_t)(n0 + nrow) * rb;
+        const uint8_t* row = w + (uint64_t)(n0 + nrow) * rb + (uint64_t)sb_begin * 144u;  // this split's K range
         // the code bytes of stage kb are loaded kPrefetch stages ahead, so
         // global-memory latency overlaps the dequantisation of earlier stages;
         // scales are unpacked once per super-block (every 4 stages)
@@ -303,22 +318,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         // epilogue: warp (2..5) % 4 owns TMEM lanes 32*q .. 32*q+31
         const bool ok = mbar_wait(&tail->done, 0, err);
         asm volatile("tcgen05.fence::after_thread_sync;");
-        const uint32_t q = warp & 3u, sub = (warp - 2u) >> 2;  // lane quarter; which of its 4 warps
+        const uint32_t q = warp & 3u, sub = (warp - 2u) >> 2;  // lane quarter; which of its warps
         const bool store = ok && !*abort_flag;
+        constexpr uint32_t kPairs = 2u * (kBN / 32u), kPerQuarter = kDqWarps / 4u;
+        // accumulators -> y (single split) or -> this split's partial tile
+        float* dst_base = sk.ks == 1u ? y : sk.ws + (uint64_t)split * m * n_total;
 #pragma unroll 1
-        for (uint32_t pair = sub; pair < 2u * (kBN / 32u); pair += kDqWarps / 4u) {
+        for (uint32_t pair = sub; pair < kPairs; pair += kPerQuarter) {
             const uint32_t acc = pair / (kBN / 32u), cb = pair % (kBN / 32u);
-            {
-                uint32_t r[32];
-                tmem_ld32(tmem + ((32u * q) << 16) + acc * 128u + cb * 32u, r);
-                const uint32_t mrow = acc * 128u + 32u * q + lane;
-                if (store && mrow < m) {
-                    float4* dst = reinterpret_cast<float4*>(y + (uint64_t)mrow * n_total + n0 + cb * 32u);
+            uint32_t r[32];
+            tmem_ld32(tmem + ((32u * q) << 16) + acc * 128u + cb * 32u, r);
+            const uint32_t mrow = acc * 128u + 32u * q + lane;
+            if (store && mrow < m) {
+                float4* dst = reinterpret_cast<float4*>(dst_base + (uint64_t)mrow * n_total + n0 + cb * 32u);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                             __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                for (int i = 0; i < 8; ++i)
+                    dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                         __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+            }
+        }
+        if (sk.ks > 1u) {
+            __threadfence();
+            named_bar_sync(1, kDqWarps * 32u);
+            if (dt == 0) tail->last_split = atomicAdd(&sk.cnt[blockIdx.x], 1u) == sk.ks - 1u;
+            named_bar_sync(1, kDqWarps * 32u);
+            if (tail->last_split) {
+                __threadfence();
+#pragma unroll 1
+                for (uint32_t pair = sub; pair < kPairs; pair += kPerQuarter) {
+                    const uint32_t acc = pair / (kBN / 32u), cb = pair % (kBN / 32u);
+                    const uint32_t mrow = acc * 128u + 32u * q + lane;
+                    if (!(store && mrow < m)) continue;
+                    const uint64_t off = (uint64_t)mrow * n_total + n0 + cb * 32u;
+                    float4 t[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) t[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (uint32_t sp = 0; sp < sk.ks; ++sp) {
+                        const float4* src = reinterpret_cast<const float4*>(sk.ws + (uint64_t)sp * m * n_total + off);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 v = __ldcg(src + i);
+                            t[i].x += v.x, t[i].y += v.y, t[i].z += v.z, t[i].w += v.w;
+                        }
+                    }
+                    float4* dst = reinterpret_cast<float4*>(y + off);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dst[i] = t[i];
                 }
+                if (dt == 0) atomicExch(&sk.cnt[blockIdx.x], 0u);
             }
         }
     }
@@ -344,6 +391,46 @@ EncodeTiledFn encode_fn() {
         return reinterpret_cast<EncodeTiledFn>(p);
     }();
     return fn;
+}
+
+struct GemmScratch {
+    float* ws = nullptr;
+    uint32_t* cnt = nullptr;
+    size_t ws_floats = 0, cnt_n = 0;
+};
+std::mutex g_gemm_mutex;
+GemmScratch g_gemm_scratch[64];
+
+// Per-device split-K scratch, grown on demand (not while a graph is being
+// captured; split-K launches on one device must not overlap in time).
+int gemm_splitk_reserve(size_t ws_floats, size_t tiles, float** ws, uint32_t** cnt) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(g_gemm_mutex);
+    GemmScratch& g = g_gemm_scratch[dev & 63];
+    if (g.ws_floats < ws_floats || g.cnt_n < tiles) {
+        const size_t nw = std::max(ws_floats, g.ws_floats), nc = std::max(tiles, g.cnt_n);
+        float* nws = nullptr;
+        uint32_t* ncnt = nullptr;
+        cudaError_t e = cudaMalloc(&nws, nw * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&ncnt, nc * sizeof(uint32_t));
+        if (e == cudaSuccess) e = cudaMemset(ncnt, 0, nc * sizeof(uint32_t));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) {
+            cudaFree(nws);
+            cudaFree(ncnt);
+            return set_cuda_error(e, "gemm split-K scratch");
+        }
+        cudaFree(g.ws);
+        cudaFree(g.cnt);
+        g.ws = nws;
+        g.cnt = ncnt;
+        g.ws_floats = nw;
+        g.cnt_n = nc;
+    }
+    *ws = g.ws;
+    *cnt = g.cnt;
+    return ARC_OK;
 }
 
 }  // namespace
@@ -380,8 +467,20 @@ int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: tensor map for X rejected");
-    const cudaError_t e = launch_kernel(gemm_q4k_bf16_kernel, dim3(n / kBN), dim3(kThreads), kSmemBytes, stream, map,
-                                        static_cast<const uint8_t*>(w), n, k, m, y, dev_error_word());
+    // split K so that about one CTA per SM is busy (whole super-blocks per split)
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t tiles = n / kBN;
+    const uint32_t ks = std::max(1u, std::min((uint32_t)sms / tiles, k / 256u));
+    SplitKWs sk{nullptr, nullptr, ks};
+    if (ks > 1) {
+        st = gemm_splitk_reserve((size_t)ks * m * n, tiles, &sk.ws, &sk.cnt);
+        if (st != ARC_OK) return st;
+    }
+    const cudaError_t e = launch_kernel(gemm_q4k_bf16_kernel, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
+                                        static_cast<const uint8_t*>(w), n, k, m, y, dev_error_word(), sk);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "gemm launch");
 }
 

@@ -62,7 +62,9 @@ def run_gemm(m, n, k, seed):
 
 
 @pytest.mark.parametrize("m,n,k", [(256, 128, 256), (256, 384, 3584), (100, 256, 1024), (1, 128, 512),
-                                   (256, 18944, 3584)])
+                                   (256, 18944, 3584),
+                                   # split-K: the FFN-down shape (28 column tiles x 5 splits), many small splits
+                                   (256, 3584, 18944), (64, 256, 2048), (1, 128, 4096)])
 def test_gemm_q4k_bf16(m, n, k):
     y, xf, wd, wb = run_gemm(m, n, k, 900 + m + n + k)
     assert np.isfinite(y).all()
