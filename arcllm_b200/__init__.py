@@ -13,6 +13,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libarcllm_cuda.so")
 
 GGML_F32, GGML_F16, GGML_Q4_K, GGML_Q6_K = 0, 1, 12, 14
+TYPE_EXEC148 = 148  # EXEC148 image of a Q4_K matrix (route B of the Q4 FFN-down capability)
 Q4K_BLOCK_BYTES, Q6K_BLOCK_BYTES = 144, 210
 
 _lock = threading.Lock()
@@ -34,6 +35,8 @@ SIGNATURES = {
     "arcllm_cuda_matvec_q6k": [_vp, _u32, _u32, _vp, _vp, _vp, _vp],
     "arcllm_cuda_gateup_silu_q4k": [_vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp],
     "arcllm_cuda_gemm_q4k_bf16": [_vp, _u32, _u32, _vp, _u32, _vp, _vp],
+    "arcllm_cuda_exec148_materialize": [_vp, _u64, _vp, _vp],
+    "arcllm_cuda_exec148_validate": [_vp, _vp, _u64, C.POINTER(C.c_uint64), _vp],
     "arcllm_cuda_fill_q4k": [_vp, _u64, _u64, _u64, _vp],
     "arcllm_cuda_fill_q6k": [_vp, _u64, _u64, _u64, _vp],
     "arcllm_cuda_fill_normal_f32": [_vp, _u64, _u64, _u64, _f32, _f32, _vp],

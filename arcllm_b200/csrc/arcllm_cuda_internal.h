@@ -92,6 +92,13 @@ int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows
 int matvec_launch(const MatvecPlan& pl, const void* w0, const void* w1, const float* x, const float* gamma,
                   float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
 
+// EXEC148 image of Q4_K weights (exec148.cu).
+int exec148_materialize(const void* src, uint64_t n_blocks, void* dst, cudaStream_t stream);
+int exec148_validate(const void* src, const void* img, uint64_t n_blocks, uint64_t* mismatches_host,
+                     cudaStream_t stream);
+int exec148_matvec(const void* w, uint32_t rows, uint32_t k, const float* x, const float* residual, float* y,
+                   cudaStream_t stream);
+
 // Prefill GEMM on tcgen05 (gemm_tcgen05.cu).
 int gemm_q4k_bf16_prepare();
 int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,

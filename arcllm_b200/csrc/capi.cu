@@ -165,6 +165,19 @@ int arcllm_cuda_gateup_silu_q4k(const void* w_gate, const void* w_up, uint32_t r
     ARC_GUARD_END
 }
 
+int arcllm_cuda_exec148_materialize(const void* q4k, uint64_t n_blocks, void* exec, void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::exec148_materialize(q4k, n_blocks, exec, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_exec148_validate(const void* q4k, const void* exec, uint64_t n_blocks, uint64_t* mismatches_host,
+                                 void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::exec148_validate(q4k, exec, n_blocks, mismatches_host, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x_bf16, uint32_t m, float* y,
                               void* stream) {
     ARC_GUARD_BEGIN

@@ -552,6 +552,10 @@ int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows
     // ARCLLM_MATVEC_IMPL=splitk routes K > 3584 to the split-K tensor-core
     // kernel (matvec_imma_splitk.cu), which measured slower than the CUDA-core
     // kernel on B200 for the FFN down shape and is therefore not the default.
+    if (fmt == ARC_TYPE_EXEC148) {  // route B of the Q4 FFN-down capability
+        if (dual || gamma || bias) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec EXEC148: no gamma, bias or dual");
+        return exec148_matvec(w0, rows, k, x, residual, y, stream);
+    }
     const char* env = std::getenv("ARCLLM_MATVEC_IMPL");
     const int impl = !env ? 1 : (std::strcmp(env, "cuda") == 0 ? 0 : (std::strcmp(env, "splitk") == 0 ? 2 : 1));
     const bool x_aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma)) & 15u) == 0u;

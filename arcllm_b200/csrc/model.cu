@@ -61,7 +61,7 @@ int check_layer(const arcllm_cuda_model_config& c, const arcllm_cuda_layer& L) {
     if (!L.attn_norm || !L.ffn_norm || !L.wq || !L.wk || !L.wv || !L.wo || !L.w_gate || !L.w_up || !L.w_down)
         return set_error(ARC_E_INVALID_ARGUMENT, "model_set_layer: null tensor pointer");
     if (!quant_ok(L.type_q) || !quant_ok(L.type_k) || !quant_ok(L.type_v) || !quant_ok(L.type_o) ||
-        !quant_ok(L.type_down) || L.type_gate_up != ARC_GGML_Q4_K)
+        !(quant_ok(L.type_down) || L.type_down == ARC_TYPE_EXEC148) || L.type_gate_up != ARC_GGML_Q4_K)
         return set_error(ARC_E_UNSUPPORTED_SHAPE,
                          "model_set_layer: projections must be Q4_K/Q6_K and gate/up Q4_K "
                          "(reference contract: src/arcllm_v1_runtime.cpp:194-211)");
@@ -243,6 +243,15 @@ int model_set_layer(arcllm_cuda_model* m, uint32_t layer, const arcllm_cuda_laye
     ARC_TRY(check_layer(m->cfg, *L));
     m->layers[layer] = *L;
     m->layer_set[layer] = 1;
+    // captured step graphs hold the previous weight pointers: re-capture on next use
+    if (m->g_prefill) {
+        cudaGraphExecDestroy(m->g_prefill);
+        m->g_prefill = nullptr;
+    }
+    if (m->g_decode) {
+        cudaGraphExecDestroy(m->g_decode);
+        m->g_decode = nullptr;
+    }
     return ARC_OK;
 }
 

@@ -25,6 +25,7 @@
 
 #include "arcllm/v1/gguf.h"
 #include "arcllm/v1/q4_cuda_backend.h"
+#include "arcllm/v1/q4_down_policy.h"
 #include "arcllm_cuda.h"
 
 namespace arcllm::v1::runtime {
@@ -180,24 +181,91 @@ RunResult generate(const RunRequest& request) {
     check(arcllm_cuda_model_create(&cfg, &model.m), "model create");
     std::vector<cuda::Q4CudaBackend::Source> q4_down;
     for (std::uint32_t l = 0; l < L; ++l) {
-        const LayerTensors& z = layers[l];
+        const LayerTensors& z = layers[l];  // decoder tensors (routed through A until the policy says B)
         arcllm_cuda_layer lay{devf(z.an), dev(z.qw), devf(z.qb), int(z.qw->ggml_type), dev(z.kw), devf(z.kb),
                               int(z.kw->ggml_type), dev(z.vw), devf(z.vb), int(z.vw->ggml_type), dev(z.ow),
                               int(z.ow->ggml_type), devf(z.fn), dev(z.gw), dev(z.uw), int(z.gw->ggml_type),
                               dev(z.dw), int(z.dw->ggml_type)};
         check(arcllm_cuda_model_set_layer(model.m, l, &lay), "layer binding");
-        if (z.dw->ggml_type == Q4) q4_down.push_back({l, dev(z.dw)});
+        if (z.dw->ggml_type == Q4) q4_down.push_back({l, dev(z.dw), store.tensor_data(g, *z.dw)});
     }
     check(arcllm_cuda_model_set_endpoints(model.m, dev(emb), int(emb->ggml_type),
                                           devf(gg::find_tensor(g, "output_norm.weight")), dev(outw),
                                           int(outw->ggml_type)),
           "endpoint binding");
 
-    // ---- Q4 FFN-down primitive: route A (the plain Q4_K split-K matvec) ----
-    cuda::Q4CudaBackend q4_backend(std::move(q4_down), H, FFN, request.sidecar_path);
-    binding_v4::PrimitiveHandle route{};
-    if (q4_backend.resolve_primitive(cuda::kPrimitiveA, route) != binding_v4::BackendStatus::OK)
+    // ---- Q4 FFN-down primitive: route per decode step from the policy (runtime.cpp:313-339,461-475) ----
+    cuda::Q4CudaBackend q4_backend(q4_down, H, FFN, request.sidecar_path);
+    binding_v4::PrimitiveHandle route_a{};
+    if (q4_backend.resolve_primitive(cuda::kPrimitiveA, route_a) != binding_v4::BackendStatus::OK)
         fail("ArcLLM runtime Q4 binding not ready");
+    const bool profile1 = request.evidence_profile == EvidenceProfile::PROFILE_1;
+    binding_v4::RepresentationHandle b_handle{};
+    auto runtime_state = [&] {
+        cuda::Q4DownRuntime rt;
+        rt.b_resident = q4_backend.resident();
+        rt.b_identity_valid = q4_backend.validated();
+        rt.p3_available = q4_backend.p3_available();
+        return rt;
+    };
+    // Apply one decision the way binding_v4::apply_decision does: evict ->
+    // release; acquire -> acquire, validate (release on failure); then the
+    // route's primitive must resolve.  Returns the routed primitive.
+    std::uint32_t acquire_events = 0, evict_events = 0;
+    auto apply = [&](const cuda::Q4DownDecision& d) {
+        if (d.lifecycle == cuda::Q4DownLifecycle::EVICT && b_handle) {
+            if (q4_backend.release(cuda::kPrimitiveB, b_handle) != binding_v4::BackendStatus::OK)
+                fail("ArcLLM runtime Q4 binding not ready");
+            b_handle = {};
+            ++evict_events;
+        }
+        if (d.lifecycle == cuda::Q4DownLifecycle::ACQUIRE) {
+            if (q4_backend.acquire(d.acquisition, cuda::kPrimitiveB, d.requested_residency_bytes, b_handle) !=
+                    binding_v4::BackendStatus::OK ||
+                !b_handle)
+                fail("ArcLLM runtime Q4 binding not ready: " + q4_backend.last_error());
+            if (d.require_post_acquisition_identity_validation &&
+                q4_backend.validate(b_handle, cuda::kCapability, cuda::kPrimitiveB) != binding_v4::BackendStatus::OK) {
+                q4_backend.release(cuda::kPrimitiveB, b_handle);
+                b_handle = {};
+                fail("ArcLLM runtime Q4 binding not ready: " + q4_backend.last_error());
+            }
+            ++acquire_events;
+        }
+        binding_v4::PrimitiveHandle h{};
+        if (q4_backend.resolve_primitive(d.route, h) != binding_v4::BackendStatus::OK)
+            fail("ArcLLM runtime Q4 binding not ready");
+        return d.route;
+    };
+    // Decode step di decides with future reuse max_new - 1 - di.  With this
+    // bundle the route cannot change inside a request (an image acquired at
+    // step 0 stays valid and reusable while reuse > 0), so the decisions are
+    // taken up front and the model runs the whole request on that route.
+    std::uint32_t route_a_steps = 0, route_b_steps = 0;
+    registry::PrimitiveId decode_route = cuda::kPrimitiveA;
+    if (q4_backend.has_sources()) {
+        for (std::uint32_t di = 0; di + 1u < request.max_new_tokens; ++di) {
+            const auto d = cuda::decide_q4_down(profile1, request.request_within_validated_domain,
+                                                std::uint64_t(request.max_new_tokens - 1u - di), runtime_state(),
+                                                q4_backend.exec_family_bytes());
+            const registry::PrimitiveId r = apply(d);
+            if (di == 0) decode_route = r;
+            else if (r != decode_route) fail("ArcLLM runtime Q4 route changed within request");
+            (r == cuda::kPrimitiveB ? route_b_steps : route_a_steps)++;
+        }
+    } else {
+        route_a_steps = request.max_new_tokens - 1u;  // no Q4_K down layer: every step is plain A
+    }
+    if (decode_route == cuda::kPrimitiveB) {  // rebind the Q4_K down layers to the EXEC148 image
+        for (const auto& src : q4_down) {
+            const LayerTensors& z = layers[src.layer];
+            arcllm_cuda_layer lay{devf(z.an), dev(z.qw), devf(z.qb), int(z.qw->ggml_type), dev(z.kw), devf(z.kb),
+                                  int(z.kw->ggml_type), dev(z.vw), devf(z.vb), int(z.vw->ggml_type), dev(z.ow),
+                                  int(z.ow->ggml_type), devf(z.fn), dev(z.gw), dev(z.uw), int(z.gw->ggml_type),
+                                  q4_backend.exec_image(src.layer), ARC_TYPE_EXEC148};
+            check(arcllm_cuda_model_set_layer(model.m, src.layer, &lay), "route B binding");
+        }
+    }
 
     // ---- prefill + greedy decode ----
     RunResult result;
@@ -210,13 +278,22 @@ RunResult generate(const RunRequest& request) {
     if (!st.finite) fail("ArcLLM runtime non-finite logits");
     if (st.decode_steps + 1u != request.max_new_tokens) fail("ArcLLM runtime generated-token count mismatch");
 
+    // request close: reuse 0 evicts a resident image (runtime.cpp:508-517)
+    if (q4_backend.has_sources())
+        apply(cuda::decide_q4_down(profile1, request.request_within_validated_domain, 0u, runtime_state(),
+                                   q4_backend.exec_family_bytes()));
+    if (q4_backend.resident()) fail("ArcLLM runtime represented Q4 image still resident after request close");
+
     RuntimeStats& s = result.stats;
     s.prefill_dispatches = st.prefill_launches;
     s.prefill_submits = st.prefill_graph_launches;
     s.decode_dispatches_per_step = request.max_new_tokens > 1 ? st.decode_launches_per_step : 0u;
     s.decode_submits_per_step = request.max_new_tokens > 1 ? st.decode_graph_launches_per_step : 0u;
     s.decode_steps = st.decode_steps;
-    s.route_a_steps = st.decode_steps;
+    s.route_a_steps = route_a_steps;
+    s.route_b_steps = route_b_steps;
+    s.acquire_events = acquire_events;
+    s.evict_events = evict_events;
     const auto& c = q4_backend.counters();
     s.b_allocations = c.b_allocations;
     s.b_materializations = c.b_materializations;

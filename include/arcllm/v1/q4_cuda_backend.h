@@ -5,10 +5,11 @@
 // acquire :210-275, validate :277-305, release :307-321, resolve_primitive
 // :323-345) so the reference's policy layer (binding_v4::apply_decision) can
 // drive it unchanged.  Primitive A is the plain Q4_K split-K matvec over the
-// GGUF layout (launch_ffn_down below, the counterpart of append_ffn_down_op
-// :347-385).  Primitive B, the re-laid-out EXEC148 image, is not provided by
-// this version: acquire() of B answers UNAVAILABLE and resolve_primitive(B)
-// PRIMITIVE_UNAVAILABLE, both with last_error() saying so.
+// GGUF layout; primitive B is the EXEC148 image of all Q4_K FFN-down layers
+// (148 bytes per super-block), acquired by GPU materialisation (P1), a cold
+// sidecar read (P3) or CPU materialisation (P0), and validated block by block
+// against its Q4_K source (canonical tuples identical).  launch_ffn_down is
+// the counterpart of append_ffn_down_op (:347-385).
 #pragma once
 #include <cstdint>
 #include <string>
@@ -45,12 +46,15 @@ public:
     // One Q4_K ffn_down weight routed through this backend.
     struct Source {
         std::uint32_t layer = 0;
-        const void* device = nullptr;  // Q4_K rows in device memory, 16-byte aligned
+        const void* device = nullptr;         // Q4_K rows in device memory, 16-byte aligned
+        const std::uint8_t* host = nullptr;  // the same bytes in host memory (P0; may be null)
     };
     // rows x k is the shape of every source (hidden x ffn); sidecar is the
     // optional pre-materialised image path (acquisition P3).
     Q4CudaBackend(std::vector<Source> sources, std::uint32_t rows, std::uint32_t k, std::string sidecar);
     ~Q4CudaBackend() override;
+    Q4CudaBackend(const Q4CudaBackend&) = delete;
+    Q4CudaBackend& operator=(const Q4CudaBackend&) = delete;
 
     binding_v4::BackendStatus acquire(registry::AcquisitionPathId path, registry::PrimitiveId target,
                                       std::uint64_t residency_bytes,
@@ -70,6 +74,10 @@ public:
 
     // Bytes of the EXEC148 image for all sources (148 B per Q4_K super-block).
     std::uint64_t exec_family_bytes() const noexcept;
+    // Device address of `layer`'s slot in the resident EXEC148 image (null if
+    // the image is not resident or the layer is not a source).
+    const void* exec_image(std::uint32_t layer) const noexcept;
+    bool has_sources() const noexcept { return !sources_.empty(); }
     bool resident() const noexcept { return resident_; }
     bool validated() const noexcept { return validated_; }
     bool p3_available() const noexcept;
@@ -78,9 +86,12 @@ public:
 
 private:
     const Source* find(std::uint32_t layer) const noexcept;
+    std::uint64_t layer_bytes() const noexcept { return std::uint64_t(rows_) * (k_ / 256u) * 148u; }
+    void free_image() noexcept;
     std::vector<Source> sources_;
     std::uint32_t rows_, k_;
     std::string sidecar_;
+    void* image_ = nullptr;  // device memory of the EXEC148 image
     bool resident_ = false;
     bool validated_ = false;
     BackendCounters counters_{};

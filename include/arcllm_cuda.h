@@ -54,6 +54,11 @@ enum arcllm_cuda_status {
 };
 
 enum arcllm_ggml_type { ARC_GGML_F32 = 0, ARC_GGML_F16 = 1, ARC_GGML_Q4_K = 12, ARC_GGML_Q6_K = 14 };
+/* Not a GGUF type: the EXEC148 image of a Q4_K matrix (primitive B of the
+ * Q4 FFN-down capability, src/q4_down_exec148_materializer.h:14), 148 bytes
+ * per super-block.  Accepted by arcllm_cuda_matvec (without gamma or bias)
+ * and as a layer's type_down. */
+enum { ARC_TYPE_EXEC148 = 148 };
 
 ARCLLM_CUDA_API int arcllm_cuda_abi_version(void);
 ARCLLM_CUDA_API const char *arcllm_cuda_status_string(int status);
@@ -112,6 +117,17 @@ ARCLLM_CUDA_API int arcllm_cuda_matvec_hostio(int ggml_type, const void *w, uint
  * ffn_norm shaders/p7_rmsnorm_seq.comp before them (:389). */
 ARCLLM_CUDA_API int arcllm_cuda_gateup_silu_q4k(const void *w_gate, const void *w_up, uint32_t rows, uint32_t k,
                                 const float *x, const float *gamma, float eps, float *s, void *stream);
+
+/* EXEC148 image of n_blocks Q4_K super-blocks (src/q4_down_exec148_materializer.h:14,
+ * shaders/b1_2_exec148_gpu_materialize.comp: acquisition path P1 on the GPU).
+ * q4k 16-byte aligned, exec 4-byte aligned, exec holds 148 * n_blocks bytes. */
+ARCLLM_CUDA_API int arcllm_cuda_exec148_materialize(const void *q4k, uint64_t n_blocks, void *exec, void *stream);
+/* Identity validation of an EXEC148 image against its Q4_K source
+ * (src/q4_down_exec148_materializer.h:16-18: canonical tuples d, dmin,
+ * 8 x (sc, mn), 256 codes must be identical).  Synchronous; writes the number
+ * of differing blocks (0 = exact) to *mismatches_host. */
+ARCLLM_CUDA_API int arcllm_cuda_exec148_validate(const void *q4k, const void *exec, uint64_t n_blocks,
+                                                 uint64_t *mismatches_host, void *stream);
 
 /* Prefill GEMM (config 4) on the tcgen05 tensor cores: y[m][n] (fp32, row-major)
  * = x[m][k] (bf16, row-major) * W^T for the n x k Q4_K matrix W, weights

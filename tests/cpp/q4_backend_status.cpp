@@ -55,11 +55,28 @@ int main(int argc, char** argv) {
     EXPECT(b.acquire(cuda::kAcquireDisabledWarm, cuda::kPrimitiveB, bytes, rep) == BackendStatus::UNAVAILABLE);
     EXPECT(b.acquire(registry::AcquisitionPathId{0x1234}, cuda::kPrimitiveB, bytes, rep) ==
            BackendStatus::UNAVAILABLE);
-    // the EXEC148 image itself is not provided: every valid path answers UNAVAILABLE
-    EXPECT(b.acquire(cuda::kAcquirePrimary, cuda::kPrimitiveB, bytes, rep) == BackendStatus::UNAVAILABLE);
-    EXPECT(b.acquire(cuda::kAcquireTertiary, cuda::kPrimitiveB, bytes, rep) == BackendStatus::UNAVAILABLE);
+    // P1 / P0 on sources that cannot be materialised (no device or null
+    // weights, no host copy): ACQUISITION_FAILED, nothing left resident
+    EXPECT(b.acquire(cuda::kAcquirePrimary, cuda::kPrimitiveB, bytes, rep) == BackendStatus::ACQUISITION_FAILED);
+    EXPECT(rep.opaque == 0 && !b.resident());
+    EXPECT(b.acquire(cuda::kAcquireTertiary, cuda::kPrimitiveB, bytes, rep) == BackendStatus::ACQUISITION_FAILED);
     EXPECT(!b.last_error().empty());
     EXPECT(!b.resident());
+    // P3 with a sidecar of the right size: on a GPU the image is read and
+    // resident (handle 1), identity validation against the null sources
+    // fails, release frees it; without a GPU the allocation fails
+    const BackendStatus p3 = b.acquire(cuda::kAcquireSecondary, cuda::kPrimitiveB, bytes, rep);
+    if (gpu) {
+        EXPECT(p3 == BackendStatus::OK && rep.opaque == 1 && b.resident() && !b.validated());
+        EXPECT(b.acquire(cuda::kAcquirePrimary, cuda::kPrimitiveB, bytes, rep) == BackendStatus::INVALID_BINDING_STATE);
+        rep.opaque = 1;
+        EXPECT(b.validate(rep, cuda::kCapability, cuda::kPrimitiveB) == BackendStatus::VALIDATION_FAILED);
+        EXPECT(!b.validated());
+        EXPECT(b.release(cuda::kPrimitiveB, rep) == BackendStatus::OK);
+        EXPECT(!b.resident());
+    } else {
+        EXPECT(p3 == BackendStatus::ACQUISITION_FAILED && !b.resident());
+    }
     // validate / release without a resident image -> INVALID_BINDING_STATE
     EXPECT(b.validate({1}, cuda::kCapability, cuda::kPrimitiveB) == BackendStatus::INVALID_BINDING_STATE);
     EXPECT(b.validate({0}, cuda::kCapability, cuda::kPrimitiveB) == BackendStatus::INVALID_BINDING_STATE);
@@ -83,7 +100,9 @@ int main(int argc, char** argv) {
     EXPECT(b.launch_ffn_down({cuda::kPrimitiveB.value}, 3, nullptr, nullptr, nullptr, nullptr) != 0);
     const auto& c = b.counters();
     EXPECT(c.resolve_a == 1 && c.resolve_b == 1);
-    EXPECT(c.b_allocations == 0 && c.b_materializations == 0 && c.b_releases == 0);
+    EXPECT(c.p1_calls == (gpu ? 1u : 0u) && c.p0_calls == (gpu ? 1u : 0u) && c.p3_calls == (gpu ? 1u : 0u));
+    EXPECT(c.b_materializations == (gpu ? 1u : 0u) && c.b_releases == (gpu ? 1u : 0u));
+    EXPECT(c.b_validations == (gpu ? 1u : 0u));
     std::printf("q4_backend_status: %d failure(s)\n", failures);
     return failures ? 1 : 0;
 }

@@ -143,6 +143,20 @@ def test_valid_model_reaches_device_stage(tiny_gguf):
     assert rc == 2 and "found no CUDA device" in err, err
 
 
+def build_test_program(tmp_path, name):
+    exe = str(tmp_path / name)
+    src = os.path.join(ROOT, "tests", "cpp", name + ".cpp")
+    subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-I", os.path.join(ROOT, "include"), src, "-o", exe,
+                    "-L", PKG, "-larcllm_runtime", "-larcllm_cuda", "-Wl,-rpath," + PKG], check=True)
+    return exe
+
+
+def test_q4_down_policy_decisions(tmp_path):
+    r = subprocess.run([build_test_program(tmp_path, "q4_down_policy")], capture_output=True, text=True, timeout=60)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
 def test_q4_backend_status_semantics(tmp_path):
     exe = str(tmp_path / "q4_backend_status")
     src = os.path.join(ROOT, "tests", "cpp", "q4_backend_status.cpp")

@@ -81,3 +81,27 @@ def test_generate_cli_single_token_and_repeat(tmp_path):
     c = run_cli(path, prompt, 4)
     assert b["generated_token_ids"] == c["generated_token_ids"]
     assert b["generated_token_ids"][0] == a["generated_token_ids"][0]
+
+
+def test_generate_route_b_inside_validated_domain(tmp_path):
+    """Q4_K FFN-down layers inside the validated domain: the policy acquires the
+    EXEC148 image through P1 at the first decode step (reuse 5 >= 2), validates
+    it, routes every decode step through it and evicts it at request close; the
+    tokens are those of route A."""
+    types = dict(w_down=GGML_Q4_K)
+    path = str(tmp_path / "m.gguf")
+    write_synthetic_gguf(path, SMALL, types=types, seed=0x5EED + 9)
+    prompt = [int(t) for t in O.tokens(6, 0x79, SMALL["vocab"])]
+    b = run_cli(path, prompt, 6, profile=0, scope=1)
+    a = run_cli(path, prompt, 6, profile=0, scope=0)
+    sb, sa = b["stats"], a["stats"]
+    assert sb["route_b_steps"] == 5 and sb["route_a_steps"] == 0
+    assert sb["acquire_events"] == 1 and sb["evict_events"] == 1
+    assert sb["p1_calls"] == 1 and sb["p3_calls"] == 0 and sb["p0_calls"] == 0
+    assert sb["b_allocations"] == 1 and sb["b_materializations"] == 1
+    assert sb["b_validations"] == 1 and sb["b_releases"] == 1
+    assert sa["route_a_steps"] == 5 and sa["route_b_steps"] == 0 and sa["acquire_events"] == 0
+    assert b["generated_token_ids"] == a["generated_token_ids"]
+    # profile 1 needs 4 tokens of reuse: 3 new tokens (reuse 2 at the first decode step) stay on A
+    c = run_cli(path, prompt, 3, profile=1, scope=1)
+    assert c["stats"]["route_a_steps"] == 2 and c["stats"]["route_b_steps"] == 0 and c["stats"]["acquire_events"] == 0
