@@ -11,6 +11,8 @@
 //                d, dmin, 8 x (sc, mn), 256 codes -- identical for source and image)
 //   matvec       shaders/q4_down_exec148_serial.comp:6 (y = W x with the same
 //                w = d*sc*q - dmin*mn per element)
+#include <algorithm>
+
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
 
@@ -92,47 +94,86 @@ __global__ void exec148_validate_kernel(const uint8_t* __restrict__ src, const u
     if (!same) atomicAdd(mismatches, 1ull);
 }
 
-// y[r] = (residual[r] +) sum_k w[r,k] x[k] over EXEC148 rows; one warp per
-// row, lane L takes sub-blocks L, L+32, ... (32 weights: 16 code bytes, one
-// (sc, mn) byte pair), then a butterfly sum.
-__global__ void __launch_bounds__(256) exec148_matvec_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t k,
-                                                             const float* __restrict__ x,
-                                                             const float* __restrict__ residual,
-                                                             float* __restrict__ y) {
+// y[r] = (residual[r] +) sum_k w[r,k] x[k] over EXEC148 rows.  Persistent
+// CTAs stage x and the per-sub-block sums of x in shared memory once; each
+// warp then takes rows in turn, lane L sub-blocks L, L+32, ... of the row,
+// loading kExecUnroll sub-blocks before using any (bytes in flight).
+// A code q enters as the float 1 + q/16 (its nibble placed in the mantissa):
+// sum(q x) = 16 (sum((1 + q/16) x) - sum(x)), and per sub-block
+// sum(w x) = d sc sum(q x) - dmin mn sum(x).
+constexpr uint32_t kExecWarps = 16;
+constexpr uint32_t kExecUnroll = 4;
+
+__global__ void __launch_bounds__(kExecWarps * 32, 2) exec148_matvec_kernel(const uint8_t* __restrict__ w,
+                                                                            uint32_t rows, uint32_t k,
+                                                                            const float* __restrict__ x,
+                                                                            const float* __restrict__ residual,
+                                                                            float* __restrict__ y) {
+    extern __shared__ __align__(16) float xs[];  // [k] x, then [k/32] sub-block sums
+    float* sxs = xs + k;
     pdl_trigger();
     pdl_wait();
-    const uint32_t row = blockIdx.x * 8u + (threadIdx.x >> 5), lane = threadIdx.x & 31u;
-    if (row >= rows) return;
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t nsub = k / 32u;
-    const uint8_t* rp = w + (uint64_t)row * (k / 256u) * 148u;
-    float acc = 0.f;
-    for (uint32_t j = lane; j < nsub; j += 32u) {
-        const uint8_t* blk = rp + (j >> 3) * 148u;
-        const uint32_t jj = j & 7u;
-        const uint32_t hd = *reinterpret_cast<const uint32_t*>(blk);
-        const float d = __half2float(__ushort_as_half((unsigned short)(hd & 0xFFFFu)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd >> 16)));
-        const float f = d * (float)blk[4 + 2 * jj];
-        const float o = dmin * (float)blk[5 + 2 * jj];
-        const uint32_t* codes = reinterpret_cast<const uint32_t*>(blk + 20u + 16u * jj);  // 4-byte aligned
-        const float4* xv = reinterpret_cast<const float4*>(x + 32u * j);
-        float qx = 0.f, sx = 0.f;
+    for (uint32_t i = tid; i < k / 4u; i += blockDim.x)
+        reinterpret_cast<float4*>(xs)[i] = reinterpret_cast<const float4*>(x)[i];
+    __syncthreads();
+    for (uint32_t j = tid; j < nsub; j += blockDim.x) {
+        float t = 0.f;
+        for (uint32_t e = 0; e < 32; ++e) t += xs[32u * j + e];
+        sxs[j] = t;
+    }
+    __syncthreads();
+    const uint64_t rb = (uint64_t)(k / 256u) * 148u;
+    for (uint32_t row = blockIdx.x * kExecWarps + warp; row < rows; row += gridDim.x * kExecWarps) {
+        const uint8_t* rp = w + row * rb;
+        float acc = 0.f;
+        for (uint32_t j0 = lane; j0 < nsub; j0 += 32u * kExecUnroll) {
+            uint32_t c[kExecUnroll][4], hd[kExecUnroll], scmn[kExecUnroll];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t c = codes[i];
-            const float4 xa = xv[2 * i], xb = xv[2 * i + 1];
-            const float xs[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            for (uint32_t u = 0; u < kExecUnroll; ++u) {
+                const uint32_t j = j0 + 32u * u;
+                if (j < nsub) {
+                    const uint8_t* blk = rp + (j >> 3) * 148u;
+                    const uint32_t jj = j & 7u;
+                    // blocks are 148 bytes apart, so the codes are only 4-byte aligned
+                    const uint32_t* cp = reinterpret_cast<const uint32_t*>(blk + 20u + 16u * jj);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float q = (float)((c >> (4 * e)) & 15u);
-                qx = fmaf(q, xs[e], qx);
-                sx += xs[e];
+                    for (int i = 0; i < 4; ++i) c[u][i] = __ldg(cp + i);
+                    hd[u] = __ldg(reinterpret_cast<const uint32_t*>(blk));
+                    scmn[u] = __ldg(reinterpret_cast<const unsigned short*>(blk + 4u + 2u * jj));
+                } else {
+                    c[u][0] = c[u][1] = c[u][2] = c[u][3] = 0u;
+                    hd[u] = scmn[u] = 0u;
+                }
+            }
+#pragma unroll
+            for (uint32_t u = 0; u < kExecUnroll; ++u) {
+                const uint32_t j = j0 + 32u * u;
+                if (j >= nsub) break;
+                const float4* xv = reinterpret_cast<const float4*>(xs + 32u * j);
+                float t = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 xa = xv[2 * i], xb = xv[2 * i + 1];
+                    const float xe[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int bit = 4 * e;  // nibble e of the word -> mantissa bits 19..22
+                        const uint32_t m = bit <= 19 ? (c[u][i] << (19 - bit)) : (c[u][i] >> (bit - 19));
+                        t = fmaf(__uint_as_float((m & 0x00780000u) | 0x3F800000u), xe[e], t);
+                    }
+                }
+                const float d = __half2float(__ushort_as_half((unsigned short)(hd[u] & 0xFFFFu)));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(hd[u] >> 16)));
+                const float sx = sxs[j];
+                const float qx = 16.0f * (t - sx);
+                acc = fmaf(d * (float)(scmn[u] & 0xFFu), qx, fmaf(-(dmin * (float)(scmn[u] >> 8)), sx, acc));
             }
         }
-        acc = fmaf(f, qx, fmaf(-o, sx, acc));
+        acc = warp_sum(acc);
+        if (lane == 0) y[row] = residual ? residual[row] + acc : acc;
     }
-    acc = warp_sum(acc);
-    if (lane == 0) y[row] = residual ? residual[row] + acc : acc;
 }
 
 }  // namespace
@@ -173,7 +214,21 @@ int exec148_matvec(const void* w, uint32_t rows, uint32_t k, const float* x, con
     if (rows == 0 || k == 0 || k % 256u) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec: K must be a multiple of 256");
     if ((reinterpret_cast<uintptr_t>(w) & 3u) || (reinterpret_cast<uintptr_t>(x) & 15u))
         return set_error(ARC_E_ALIGNMENT, "matvec EXEC148: image 4-byte, x 16-byte aligned");
-    const cudaError_t e = launch_kernel(exec148_matvec_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream,
+    const size_t smem = (size_t)k * 4u + (size_t)(k / 32u) * 4u;
+    if (smem > 227u * 1024u) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec EXEC148: K too large");
+    static bool attr_done[64] = {};
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev & 63]) {
+        const cudaError_t a = cudaFuncSetAttribute(exec148_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   227 * 1024);
+        if (a != cudaSuccess) return set_cuda_error(a, "matvec EXEC148 attribute");
+        attr_done[dev & 63] = true;
+    }
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t per_sm = smem <= 113u * 1024u ? 2u : 1u;
+    const uint32_t grid = std::min<uint32_t>((rows + kExecWarps - 1) / kExecWarps, (uint32_t)sms * per_sm);
+    const cudaError_t e = launch_kernel(exec148_matvec_kernel, dim3(grid), dim3(kExecWarps * 32), smem, stream,
                                         static_cast<const uint8_t*>(w), rows, k, x, residual, y);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "matvec EXEC148 launch");
 }

@@ -235,8 +235,9 @@ def main(argv=None):
     ap.add_argument("--fmt", default="q6k", choices=["q6k", "q4k"], help="profiling override of the workload")
     ap.add_argument("--rows", type=int, default=LM_ROWS, help="profiling override of the workload")
     ap.add_argument("--k", type=int, default=HIDDEN, help="profiling override of the workload")
-    ap.add_argument("--only", choices=["decode", "prefill"],
-                    help="profiling: run only the config-3 decode or the config-4 prefill GEMMs and print the result")
+    ap.add_argument("--only", choices=["decode", "prefill", "extra"],
+                    help="profiling: run only the config-3 decode, the config-4 prefill GEMMs or all extra "
+                         "configurations and print the result")
     ap.add_argument("--decode-prompt", type=int, default=256)
     ap.add_argument("--decode-new", type=int, default=128)
     args = ap.parse_args(argv)
@@ -252,7 +253,8 @@ def main(argv=None):
             res = run_decode(A, torch, measured_peaks()[0], args.decode_prompt, args.decode_new)
         else:
             res = run_extra(A, A.lib(), torch, torch.device("cuda", 0),
-                            C.c_void_p(torch.cuda.current_stream().cuda_stream), measured_peaks()[0], which="prefill")
+                            C.c_void_p(torch.cuda.current_stream().cuda_stream), measured_peaks()[0],
+                            which="prefill" if args.only == "prefill" else "all")
         print(json.dumps(res), flush=True)
         return 0
 
@@ -501,6 +503,30 @@ def run_extra(A, L, torch, dev, sp, hbm_peak, which="all"):
                      "weight_copies": n}
         del ws
         torch.cuda.empty_cache()
+
+    # route B of the Q4 FFN-down capability: the EXEC148 image of Q4_K 3584x18944
+    n = copies(HIDDEN * (FFN // 256) * 148)
+    src = make_w("q4k", HIDDEN, FFN, n, 0x100)
+    imgs = []
+    for t in src:
+        img = torch.empty(HIDDEN * (FFN // 256) * 148 + 16, dtype=torch.uint8, device=dev)
+        A.call("arcllm_cuda_exec148_materialize", C.c_void_p(t.data_ptr()), HIDDEN * (FFN // 256),
+               C.c_void_p(img.data_ptr()), sp)
+        imgs.append(img)
+    del src
+
+    def launch_b(i, stream):
+        A.check(L.arcllm_cuda_matvec(A.TYPE_EXEC148, C.c_void_p(imgs[i % len(imgs)].data_ptr()), HIDDEN, FFN,
+                                     C.c_void_p(x18.data_ptr()), None, C.c_float(0), None, None,
+                                     C.c_void_p(y35.data_ptr()), stream), "exec148")
+
+    ms = timed(launch_b)
+    alg = HIDDEN * (FFN // 256) * 148 + 4 * (FFN + HIDDEN)
+    out["q4k_down_route_b_exec148_3584x18944"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
+                                                   "frac_of_hbm": round(alg / (ms * 1e-3) / 1e9 / hbm_peak, 4),
+                                                   "us": round(ms * 1e3, 2), "weight_copies": n}
+    del imgs
+    torch.cuda.empty_cache()
 
     # config 2: one FFN block (RMSNorm -> fused gate/up + SiLU -> down + residual), all Q4_K
     n = copies(3 * q_bytes("q4k", FFN, HIDDEN))

@@ -51,22 +51,26 @@ def test_validate_exact_and_corrupted(rows, k):
     G.check_device_error()
 
 
-@pytest.mark.parametrize("rows,k", [(3584, 18944), (37, 512), (1, 256)])
-def test_exec148_matvec_parity(rows, k):
+@pytest.mark.parametrize("rows,k,with_res", [(3584, 18944, True), (5000, 3584, False), (37, 512, True),
+                                             (1, 256, False)])
+def test_exec148_matvec_parity(rows, k, with_res):
     seed = 77 + rows
     src = gpu_fill("q4k", rows, k, seed)
     img = materialize(src, rows * (k // 256))
     x = O.normal_f32(k, seed + 1)
-    res = O.normal_f32(rows, seed + 2)
+    res = O.normal_f32(rows, seed + 2) if with_res else None
     y = run_matvec_exec(img, rows, k, x, res)
-    y_ref = O.add(res, O.matvec("q4k", O.fill_weights("q4k", rows, k, seed), rows, k, x, threads=8))
+    y_ref = O.matvec("q4k", O.fill_weights("q4k", rows, k, seed), rows, k, x, threads=8)
+    if with_res:
+        y_ref = O.add(res, y_ref)
     assert_matvec_close(y, y_ref, x, max_abs_w("q4k", src, rows, k), "EXEC148 %dx%d" % (rows, k))
     G.check_device_error()
 
 
 def run_matvec_exec(img, rows, k, x, res):
     y = G.empty_f32(rows)
-    xd, rd = G.to_dev(x), G.to_dev(res)
+    xd = G.to_dev(x)
+    rd = G.to_dev(res) if res is not None else None
     A.call("arcllm_cuda_matvec", A.TYPE_EXEC148, G.ptr(img), rows, k, G.ptr(xd), None, C.c_float(0), None,
-           G.ptr(rd), G.ptr(y), G.stream())
+           G.ptr(rd) if rd is not None else None, G.ptr(y), G.stream())
     return G.host(y)
