@@ -1,6 +1,7 @@
 // Internal declarations shared by the CUDA translation units of
 // libarcllm_cuda.so.  Nothing here crosses the C ABI (include/arcllm_cuda.h).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -73,7 +74,7 @@ bool matvec_imma_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
 int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                        const float* gamma, float eps, const float* bias, const float* residual, float* y,
                        cudaStream_t stream);
-// Integer tensor-core split-K variant (matvec_imma_splitk.cu) for K > 3584.
+// Integer tensor-core K-slice variant (matvec_imma_splitk.cu) for K > 3584.
 // It adds CTA partials through a per-device scratch: launches of it on one
 // device must not overlap in time (one stream, or ordered streams).
 // matvec_splitk_reserve sizes that scratch ahead of graph capture.
@@ -82,15 +83,21 @@ int matvec_splitk_reserve(int fmt, uint32_t rows, uint32_t k);
 bool matvec_splitk_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
 int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, const float* x, const float* gamma,
                          float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
-// Pick the kernel for a matvec: the integer tensor-core form where it
-// applies (whole rows, K <= 3584), else the CUDA-core streaming form
-// (ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core form, =splitk opts K > 3584
-// into the split-K tensor-core form).
+// Pick the kernel for a matvec: the integer tensor-core forms where they
+// apply (whole rows for K <= 3584, K slices for Q4_K with K > 3584), else the
+// CUDA-core streaming form (ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core
+// form, =splitk also sends Q6_K with K > 3584 to the K-slice form).
 int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                const float* gamma, float eps, const float* bias, const float* residual, float* y,
                cudaStream_t stream);
 int matvec_launch(const MatvecPlan& pl, const void* w0, const void* w1, const float* x, const float* gamma,
                   float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
+
+// cuTensorMapEncodeTiled (driver entry point), or null (gemm_tcgen05.cu).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
 
 // EXEC148 image of Q4_K weights (exec148.cu).
 int exec148_materialize(const void* src, uint64_t n_blocks, void* dst, cudaStream_t stream);

@@ -104,6 +104,23 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// 16-byte cp.async global -> shared (L2 only, evict-first hint); src_bytes < 16
+// zero-fills the rest of the 16 bytes without reading past src + src_bytes.
+// dst and src must be 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(src_bytes), "l"(policy)
+                 : "memory");
+}
+
+// One arrival on `bar` once every cp.async this thread issued so far has landed
+// (the barrier's expected count includes it).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

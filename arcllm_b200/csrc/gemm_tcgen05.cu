@@ -377,22 +377,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            p = nullptr;
-        return reinterpret_cast<EncodeTiledFn>(p);
-    }();
-    return fn;
-}
-
 struct GemmScratch {
     float* ws = nullptr;
     uint32_t* cnt = nullptr;
@@ -456,7 +440,7 @@ int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint
         return set_error(ARC_E_ALIGNMENT, "gemm: W, X and Y must be 16-byte aligned");
     int st = gemm_q4k_bf16_prepare();
     if (st != ARC_OK) return st;
-    EncodeTiledFn enc = encode_fn();
+    EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(ARC_E_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
     CUtensorMap map;
     const cuuint64_t dims[2] = {k, m};
@@ -482,6 +466,20 @@ int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint
     const cudaError_t e = launch_kernel(gemm_q4k_bf16_kernel, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
                                         static_cast<const uint8_t*>(w), n, k, m, y, dev_error_word(), sk);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "gemm launch");
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda
+// symbol dependence at load time); null when the driver does not provide it.
+EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
 }
 
 }  // namespace arc

@@ -95,16 +95,6 @@ __device__ __forceinline__ void build_xfrag(const float* x, const float* gamma, 
     gather_xfrag<FMT>(xs, kc, xs, kc, lane, f);
 }
 
-// Stage-local rows of M-tile m: (row of lanes g, row of lanes g+8).  For Q6_K
-// with two tiles the rows are interleaved (4g+m, 4g+2+m) so that the eight
-// row groups of a 32-bit shared-memory read fall into different banks
-// (row stride 2940 B = -1 word mod 32 banks).
-template <int FMT, int MT>
-__device__ __forceinline__ uint2 tile_rows(int m, uint32_t g) {
-    if (FMT == 14 && MT == 2) return make_uint2(4u * g + m, 4u * g + 2u + m);
-    return make_uint2(16u * m + g, 16u * m + g + 8u);
-}
-
 // Final row sums of one finished stage round `itr`: the consumer warps' partials
 // (red[parity][slot][warp][row]) added in warp order, plus bias / residual or
 // the SiLU(gate)*up product, written to y.  Run by the producer warp.

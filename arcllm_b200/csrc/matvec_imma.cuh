@@ -196,6 +196,16 @@ __device__ __forceinline__ void gather_xfrag(const uint8_t* pA, const float* kA,
     }
 }
 
+// Stage-local rows of M-tile m: (row of lanes g, row of lanes g+8).  For Q6_K
+// with two tiles the rows are interleaved (4g+m, 4g+2+m) so that the eight
+// row groups of a 32-bit shared-memory read fall into different banks
+// (row stride 2940 B = -1 word mod 32 banks).
+template <int FMT, int MT>
+__device__ __forceinline__ uint2 tile_rows(int m, uint32_t g) {
+    if (FMT == 14 && MT == 2) return make_uint2(4u * g + m, 4u * g + 2u + m);
+    return make_uint2(16u * m + g, 16u * m + g + 8u);
+}
+
 // One 16-row tile x one Q4_K super-block: adds the rows' partial dot products
 // (this lane's sub-blocks t and 4+t) to y0 (row g) and y1 (row g+8).
 __device__ __forceinline__ void q4_tile(const uint8_t* st, uint32_t r0, uint32_t r1, uint32_t t, const XFrag& f,
@@ -303,6 +313,76 @@ __device__ __forceinline__ void q6_tile(const uint8_t* st, uint32_t row0, uint32
         const float dA = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(st + ro + offA + 208u)));
         const float dB = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(st + ro + offB + 208u)));
         out[r] = fmaf(dA, part[0], dB * part[1]);
+    }
+    y0 += out[0];
+    y1 += out[1];
+}
+
+// q6_tile with each half's scale epilogue run right after its MMAs, so only
+// half the accumulators are live at a time (for kernels with more state of
+// their own in registers).  Same arithmetic, same order of fp32 operations.
+template <bool ODD0>
+__device__ __forceinline__ void q6_tile_lowreg(const uint8_t* st, uint32_t row0, uint32_t row1, uint32_t offA,
+                                               uint32_t offB, uint32_t t, const XFrag& f, float& y0, float& y1) {
+    float part[2][2];  // [row][half]
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const bool odd = (h == 0) ? ODD0 : !ODD0;
+        const uint32_t boff = h ? offB : offA;
+        int D1[2][4], D2[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) D1[i][j] = D2[i][j] = 0;
+        uint32_t v[2][2][4];  // [lh][row][quarter]: 4 codes (l = 16lh + 4t .. +3) as u8 in [0, 63]
+#pragma unroll
+        for (int lh = 0; lh < 2; ++lh) {
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const uint32_t ro = (r ? row1 : row0) + boff + 16u * lh + 4u * t;
+                uint32_t qa, qb, qh;
+                if (odd) {
+                    qa = ld32<true>(st, ro + 64u * h);
+                    qb = ld32<true>(st, ro + 64u * h + 32u);
+                    qh = ld32<true>(st, ro + 128u + 32u * h);
+                } else {
+                    qa = ld32<false>(st, ro + 64u * h);
+                    qb = ld32<false>(st, ro + 64u * h + 32u);
+                    qh = ld32<false>(st, ro + 128u + 32u * h);
+                }
+                v[lh][r][0] = (qa & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
+                v[lh][r][1] = (qb & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
+                v[lh][r][2] = ((qa >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
+                v[lh][r][3] = ((qb >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int m = 4 * h + q, ii = q >> 1;
+            imma(D1[ii], v[0][0][q], v[0][1][q], v[1][0][q], v[1][1][q], f.b1[m][0], f.b1[m][1]);
+            imma(D2[ii], v[0][0][q], v[0][1][q], v[1][0][q], v[1][1][q], f.b2[m][0], f.b2[m][1]);
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint32_t ro = r ? row1 : row0;
+            const int8_t* sc = reinterpret_cast<const int8_t*>(st + ro + boff + 192u + t);
+            float acc = 0.f;
+#pragma unroll
+            for (int ii = 0; ii < 2; ++ii) {
+                const int i = 2 * h + ii;
+                const float F = combine(D1[ii][2 * r], D1[ii][2 * r + 1], D2[ii][2 * r], f.xh[i], f.xl[i]);
+                acc = fmaf((float)sc[4 * i] * f.sx[i], F, acc);
+            }
+            part[r][h] = acc;
+        }
+    }
+    float out[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint32_t ro = r ? row1 : row0;
+        const float dA = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(st + ro + offA + 208u)));
+        const float dB = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(st + ro + offB + 208u)));
+        out[r] = fmaf(dA, part[r][0], dB * part[r][1]);
     }
     y0 += out[0];
     y1 += out[1];

@@ -1,27 +1,46 @@
-// Integer-MMA matvec for long rows (K > 3584, e.g. the FFN down projection
-// 3584 x 18944): K-chunked stages and a split-K reduction across CTAs.
+// Integer-MMA matvec for long rows (K > 3584: the FFN down projection
+// 3584 x 18944), B200 (sm_100a).
 //
-// Work units are (32-row group, chunk of 6 super-blocks); the flattened unit
-// list (row-group major) is cut into one contiguous, equal-sized range per
-// CTA, so all SMs stream the same number of bytes whatever the row count
-// (3584 rows are 112 groups -- no whole-group split balances them over 148
-// SMs, but 112 x 13 units do).  A CTA keeps per-row sums in registers while
-// consecutive units belong to one row group and leaves a partial when the
-// group ends; the CTAs that share a group (at most a few) write their
-// partials to a per-device scratch and the last one to arrive adds them in
-// CTA order (deterministic) and writes y.
+// K is cut into P slices of at most 14 super-blocks (an even number for
+// Q6_K).  Every CTA works on ONE slice for a contiguous range of row groups,
+// so it runs the whole-row kernel's consumer scheme unchanged: consumer warp
+// w owns super-block w of its slice (Q6_K: half 0 of block w and half 1 of
+// block w^1) for the whole kernel and keeps its routed x fragments and scale
+// constants in registers.  The host gives each slice a share of the SMs in
+// proportion to its width and picks P so that the busiest CTA streams as few
+// bytes as possible (3584 rows are 112 groups of 32: no split of whole rows
+// balances them over 148 SMs, slices of rows do).
 //
-// Stages: 32 rows x 6 super-blocks, one 1-D TMA bulk copy per row issued by
-// the producer warp's lanes; 12 consumer warps each take one (16-row tile,
-// super-block) pair of every unit.  Q6_K rows are not 16-byte aligned (210-byte
-// blocks), so each row copy starts at the 16-byte boundary below the row and
-// the consumers index from the row's offset inside its slot; the matrix's
-// final partial 16 bytes are copied by hand so nothing past the weights is
-// read.  x is quantised once per CTA into an image of limb planes for all of K
-// (matvec_imma.cuh); warps gather their B fragments per unit.
+// Stages: G = 32 rows x one slice, loaded with 2-D tensor TMA boxes.  The
+// matrix is viewed as u64 words in "super-rows" of Rs rows (Q4_K: Rs = 1;
+// Q6_K: Rs = 4, because 15540-byte rows are 4 mod 16 bytes and only every
+// fourth row starts on the 16-byte boundary a tensor-map stride needs).  One
+// box takes one column of the slice (<= 2 KB of each row: <= 14 Q4_K or 8
+// Q6_K blocks, from the 16-byte boundary below the column) for every Rs-th
+// row of the group, so a Q4_K stage is ONE TMA operation and a Q6_K stage
+// 4 x (1 or 2 columns).  Measured on B200, one 1-D bulk copy per row-slice
+// (1-3 KB each) streamed at only ~110 ns per copy per SM (1.7-3.5 TB/s with
+// the consumers switched off) and 16-byte cp.async from one warp was slower
+// still: the copy engine wants few large operations.  Boxes land densely in
+// shared memory ([i][j] rows of a column region); box widths are padded so
+// that consecutive rows of one LDS sit 4 words (Q6_K, 32-bit reads of rows
+// 4g+m) or 8 words (Q4_K, 64-bit reads) apart mod 32 banks.  Rows of a Q6_K
+// matrix must come in multiples of 4; rows past the end of the matrix are
+// zero-filled by the TMA unit and never stored.
+//
+// Reduction: the producer warp adds the consumer warps' row partials in warp
+// order and stores the CTA's slice partial to a per-device scratch; once its
+// rounds are done the CTA fences once and bumps a per-group arrival counter
+// for each of its row groups, and the CTA that delivers a group's last slice
+// adds the P slice partials in slice order -- deterministic whichever CTA
+// comes last -- applies bias / residual, writes y and re-arms the counter for
+// the next launch.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
@@ -31,116 +50,172 @@
 namespace arc {
 namespace {
 
-constexpr uint32_t kSB = 6;       // super-blocks per unit (even: Q6_K half-block pairing)
-constexpr uint32_t kNW = 12;      // consumer warps: (16-row tile m, super-block j) = (w & 1, w >> 1)
-constexpr uint32_t kRowsU = 32;   // rows per unit (two 16-row MMA tiles)
-constexpr uint32_t kXimSb = 960;  // x image per super-block: 3 x 256 limb bytes + 8 x 6 window floats
+constexpr uint32_t kMaxSlices = 16;
+constexpr uint32_t kMaxMaps = 4;
+constexpr uint32_t kNW = 14;                         // consumer warps = widest slice
+constexpr uint32_t kG = 32;                          // rows per stage (two 16-row MMA tiles)
+constexpr uint32_t kXScratch = 1024;                 // per consumer warp: 3 limb planes + window constants
 constexpr uint32_t kHead = 2 * kMaxStages * 8 + 16;  // full/empty barriers, abort flag (+pad)
+constexpr uint32_t kBoxMax = 2048;                   // bytes: 256 u64 elements per box row
 
-struct SplitK {
-    float* part;    // [n_rg][slots][32] CTA partials
-    uint32_t* cnt;  // [n_rg] arrival counters (zero between launches)
-    uint32_t n_ks, n_rg, units, slots, rs;
+struct KSlice {
+    float* part;    // [P][rows] slice partials
+    uint32_t* cnt;  // [n_groups] arrival counters (zero between launches)
+    uint32_t P, tx_max;
+    uint16_t kb0[kMaxSlices], W[kMaxSlices], cta0[kMaxSlices + 1];
+    // per slice: columns (1 or 2) = (first block in the slice, box bytes, map, smem region offset)
+    uint8_t ncol[kMaxSlices], cst[kMaxSlices][2], cmap[kMaxSlices][2];
+    uint16_t cbw[kMaxSlices][2];
+    uint32_t coff[kMaxSlices][2], tx[kMaxSlices];
 };
 
-__host__ __device__ inline uint32_t sk_red_off() { return kHead + 32 * 8; }
-__host__ __device__ inline uint32_t sk_xim_off(uint32_t S) { return sk_red_off() + 2 * S * kSB * kRowsU * 4; }
-__host__ __device__ inline uint32_t sk_stage_off(uint32_t S, uint32_t nb) { return sk_xim_off(S) + nb * kXimSb; }
+struct __align__(64) KMaps {
+    CUtensorMap m[kMaxMaps];
+};
 
-// CTA that owns unit u when `units` are cut into `grid` contiguous ranges [units*i/grid, units*(i+1)/grid)
-__device__ __forceinline__ uint32_t cta_of(uint32_t u, uint32_t units, uint32_t grid) {
-    return (uint32_t)((((uint64_t)u + 1) * grid - 1) / units);
-}
+// One CTA's slice, read out of the parameter tables with compile-time
+// indices only (a runtime index into a kernel parameter array makes the
+// compiler copy the array to local memory).
+struct SliceView {
+    uint32_t sl, W, kb0, C, ci, ncol, tx;
+    uint32_t cst[2], cbw[2], coff[2], cmap[2];
+};
 
-// Byte offset of row `row`'s chunk inside its 16-byte-aligned copy.
-__device__ __forceinline__ uint32_t row_mis(const MvParams& p, uint32_t row, uint32_t sb0, uint32_t bsz) {
-    return (uint32_t)(((uint64_t)row * p.rb + (uint64_t)sb0 * bsz) & 15u);
-}
-
-template <int FMT>
-__device__ __forceinline__ void sk_finish(const MvParams& p, const SplitK& k, const float* red, uint32_t u0,
-                                          uint32_t j, uint32_t lane) {
-    const uint32_t S = p.stages, s = j % S, par = (j / S) & 1u;
-    const uint32_t u = u0 + j, rg = u / k.n_ks;
-    const uint32_t rows_g = min(kRowsU, p.rows - rg * kRowsU);
-    const float* rs = red + (par * S + s) * kSB * kRowsU;
-    const uint32_t first = cta_of(rg * k.n_ks, k.units, gridDim.x);
-    const uint32_t last = cta_of(rg * k.n_ks + k.n_ks - 1, k.units, gridDim.x);
-    const uint32_t nc = last - first + 1;
-    float a = 0.f;
-    if (lane < rows_g)
-        for (uint32_t j = 0; j < kSB; ++j) a += rs[j * kRowsU + lane];
-    const uint32_t row = rg * kRowsU + lane;
-    if (nc == 1) {
-        if (lane < rows_g) {
-            if (p.bias) a += p.bias[row];
-            if (p.residual) a = p.residual[row] + a;
-            p.y[row] = a;
+__device__ __forceinline__ SliceView slice_of(const KSlice& q, uint32_t bid) {
+    SliceView v{};
+#pragma unroll
+    for (uint32_t i = 0; i < kMaxSlices; ++i) {
+        if (i < q.P && q.cta0[i] <= bid && bid < q.cta0[i + 1]) {
+            v.sl = i;
+            v.W = q.W[i];
+            v.kb0 = q.kb0[i];
+            v.C = q.cta0[i + 1] - q.cta0[i];
+            v.ci = bid - q.cta0[i];
+            v.ncol = q.ncol[i];
+            v.tx = q.tx[i];
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                v.cst[c] = q.cst[i][c];
+                v.cbw[c] = q.cbw[i][c];
+                v.coff[c] = q.coff[i][c];
+                v.cmap[c] = q.cmap[i][c];
+            }
         }
-        return;
     }
-    float* slot = k.part + ((uint64_t)rg * k.slots) * kRowsU;
-    if (lane < rows_g) slot[(blockIdx.x - first) * kRowsU + lane] = a;
+    return v;
+}
+
+__host__ __device__ constexpr uint32_t ks_red_off() { return kHead + 32 * 8; }
+__host__ __device__ constexpr uint32_t ks_xscr_off(uint32_t S) {
+    return (ks_red_off() + 2 * S * kNW * kG * 4 + 15u) & ~15u;
+}
+__host__ __device__ constexpr uint32_t ks_stage_off(uint32_t S) { return ks_xscr_off(S) + kNW * kXScratch; }
+
+__device__ __forceinline__ void tma_box_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                           uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+// Round `itr` of this CTA (row group grp) is complete: add the consumer
+// warps' partials in warp order and store the CTA's slice partial of the
+// group's rows (plain stores; ks_close publishes them).  Run by the producer.
+__device__ __forceinline__ void ks_partial(const MvParams& p, const KSlice& q, const float* red, uint32_t W,
+                                           uint32_t sl, uint32_t itr, uint32_t grp, uint32_t lane) {
+    const uint32_t S = p.stages, s = itr % S, par = (itr / S) & 1u;
+    const uint32_t rows_g = min(kG, p.rows - grp * kG);
+    const float* rs = red + (par * S + s) * kNW * kG;
+    if (lane < rows_g) {
+        float a = 0.f;
+        for (uint32_t w = 0; w < W; ++w) a += rs[w * kG + lane];
+        q.part[(size_t)sl * p.rows + grp * kG + lane] = a;
+    }
+}
+
+// After the CTA's last round: publish its slice partials (one fence), count
+// this slice in for each of its row groups, and for every group whose last
+// slice this CTA delivered add the P slice partials in slice order
+// (deterministic whichever CTA comes last), apply bias / residual, write y
+// and re-arm the group's counter for the next launch.  The cross-CTA
+// round trips are paid once per CTA, off the streaming loop.
+__device__ __forceinline__ void ks_close(const MvParams& p, const KSlice& q, uint32_t g0, uint32_t n, uint32_t lane) {
     __threadfence();
     __syncwarp();
-    uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(&k.cnt[rg], 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != nc - 1) return;
-    __threadfence();  // the last CTA of this row group: add the partials in CTA order
-    if (lane < rows_g) {
-        const volatile float* vs = slot;
-        float t = 0.f;
-        for (uint32_t c = 0; c < nc; ++c) t += vs[c * kRowsU + lane];
-        if (p.bias) t += p.bias[row];
-        if (p.residual) t = p.residual[row] + t;
-        p.y[row] = t;
+    for (uint32_t base = 0; base < n; base += 32u) {
+        const uint32_t gi = base + lane;
+        bool last = false;
+        if (gi < n) last = atomicAdd(&q.cnt[g0 + gi], 1u) == q.P - 1u;
+        uint32_t m = __ballot_sync(0xffffffffu, last);
+        if (m) __threadfence();  // the other slices' partials of those groups are visible in L2
+        while (m) {
+            const uint32_t grp = g0 + base + (uint32_t)(__ffs(m) - 1);
+            m &= m - 1u;
+            const uint32_t rows_g = min(kG, p.rows - grp * kG);
+            const uint32_t row = grp * kG + lane;
+            if (lane < rows_g) {
+                float v[kMaxSlices];
+#pragma unroll
+                for (uint32_t j = 0; j < kMaxSlices; ++j)
+                    v[j] = j < q.P ? __ldcg(q.part + (size_t)j * p.rows + row) : 0.f;
+                float t = 0.f;
+#pragma unroll
+                for (uint32_t j = 0; j < kMaxSlices; ++j)
+                    if (j < q.P) t += v[j];
+                if (p.bias) t += p.bias[row];
+                if (p.residual) t = p.residual[row] + t;
+                p.y[row] = t;
+            }
+            __syncwarp();
+            if (lane == 0) atomicExch(&q.cnt[grp], 0u);
+        }
     }
-    if (lane == 0) atomicExch(&k.cnt[rg], 0u);
 }
 
 template <int FMT>
-__global__ void __launch_bounds__((kNW + 1) * 32, 1) matvec_imma_splitk_kernel(const MvParams p, const SplitK k) {
+__global__ void __launch_bounds__((kNW + 1) * 32, 1)
+    matvec_imma_kslice_kernel(const MvParams p, const __grid_constant__ KSlice q, const __grid_constant__ KMaps maps) {
     constexpr uint32_t bsz = FMT == 12 ? 144u : 210u;
+    constexpr uint32_t Rs = FMT == 12 ? 1u : 4u;  // rows per tensor-map super-row
+    constexpr uint32_t J = kG / Rs;               // box rows
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
     volatile int* abort_flag = reinterpret_cast<int*>(empty + kMaxStages);
-    double* red_d = reinterpret_cast<double*>(smem + kHead);                // [32]
-    float* red = reinterpret_cast<float*>(smem + sk_red_off());            // [2][S][kSB][32]
-    uint8_t* xim = smem + sk_xim_off(p.stages);                            // [nb][960]
+    double* red_d = reinterpret_cast<double*>(smem + kHead);     // [32]
+    float* red = reinterpret_cast<float*>(smem + ks_red_off());  // [2][S][kNW][kG]
+    uint8_t* xscr = smem + ks_xscr_off(p.stages);
     uint8_t* stages = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem + sk_stage_off(p.stages, p.nb)) + 127) & ~uintptr_t(127));
+        (reinterpret_cast<uintptr_t>(smem + ks_stage_off(p.stages)) + 127) & ~uintptr_t(127));
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t S = p.stages;
-    const uint32_t u0 = (uint32_t)((uint64_t)k.units * blockIdx.x / gridDim.x);
-    const uint32_t u1 = (uint32_t)((uint64_t)k.units * (blockIdx.x + 1) / gridDim.x);
-    const uint32_t n = u1 - u0;
+    // this CTA's slice and its contiguous range of row groups
+    const SliceView sv = slice_of(q, blockIdx.x);
+    const uint32_t sl = sv.sl, W = sv.W, kb0 = sv.kb0;
+    const uint32_t g0 = (uint32_t)((uint64_t)p.n_groups * sv.ci / sv.C);
+    const uint32_t n = (uint32_t)((uint64_t)p.n_groups * (sv.ci + 1) / sv.C) - g0;
     pdl_trigger();
 
     if (tid == kNW * 32) {
         for (uint32_t s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kNW);
+            mbar_init(&empty[s], W);
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    // a unit ends this CTA's stretch of its row group: the next unit starts another group, or none follows
-    auto ends_group = [&](uint32_t j) { return j + 1 == n || (u0 + j + 1) % k.n_ks == 0; };
-
     if (warp == kNW) {
         // ---------------- producer ----------------
         const uint64_t pol = l2_evict_first_policy();
-        const uint64_t total = (uint64_t)p.rows * p.rb;
-        const uint64_t total16 = total & ~(uint64_t)15;
         if (!p.early) pdl_wait();
         uint32_t it = 0;
         bool ok = true;
-        auto released = [&](uint32_t j) {
+        auto released = [&](uint32_t j) {  // wait until the consumers released round j of its slot
             bool w = true;
             if (lane == 0) w = mbar_wait(&empty[j % S], (j / S) & 1u, p.err);
             w = __shfl_sync(0xffffffffu, w, 0);
@@ -156,27 +231,28 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1) matvec_imma_splitk_kernel(c
                 ok = false;
                 break;
             }
-            const uint32_t u = u0 + it, rg = u / k.n_ks, ks = u % k.n_ks;
-            const uint32_t rows_g = min(kRowsU, p.rows - rg * kRowsU);
-            const uint32_t sb0 = ks * kSB, nsb = min(kSB, p.nb - sb0);
-            uint8_t* dst = stages + s * p.stage_smem + lane * k.rs;
-            // this lane's row: 16-byte-aligned source range [a0, a1), bytes [a1, end) by hand
-            uint64_t a0 = 0, a1 = 0, end = 0;
-            if (lane < rows_g) {
-                const uint64_t src = (uint64_t)(rg * kRowsU + lane) * p.rb + (uint64_t)sb0 * bsz;
-                end = src + (uint64_t)nsb * bsz;
-                a0 = src & ~(uint64_t)15;
-                a1 = max(min((end + 15) & ~(uint64_t)15, total16), a0);
-                for (uint64_t b = a1; b < end; ++b) dst[b - a0] = p.w0[b];
-            }
-            uint32_t bytes = (uint32_t)(a1 - a0);
+            const uint32_t grp = g0 + it;
+            if (lane == 0) {
+                uint8_t* stg = stages + s * p.stage_smem;
+                mbar_arrive_expect_tx(&full[s], sv.tx);  // whole boxes, zero-filled rows included
 #pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+                for (uint32_t c = 0; c < 2; ++c) {
+                    if (c < sv.ncol) {
+                        const uint32_t mi = sv.cmap[c];
+                        const CUtensorMap* mp = mi == 0 ? &maps.m[0] : mi == 1 ? &maps.m[1] : mi == 2 ? &maps.m[2] : &maps.m[3];
+                        const uint32_t bw = sv.cbw[c];
+#pragma unroll
+                        for (uint32_t i = 0; i < Rs; ++i) {
+                            const uint32_t xb =
+                                (uint32_t)(((uint64_t)i * p.rb + (uint64_t)(kb0 + sv.cst[c]) * bsz) & ~(uint64_t)15);
+                            tma_box_2d(stg + sv.coff[c] + i * J * bw, mp, (int)(xb / 8u), (int)(grp * J), &full[s],
+                                       pol);
+                        }
+                    }
+                }
+            }
             __syncwarp();
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes);
-            __syncwarp();
-            if (a1 > a0) bulk_g2s(dst, p.w0 + a0, (uint32_t)(a1 - a0), &full[s], pol);
-            if (it >= S && ends_group(it - S)) sk_finish<FMT>(p, k, red, u0, it - S, lane);
+            if (it >= S) ks_partial(p, q, red, W, sl, it - S, g0 + it - S, lane);
         }
         if (ok) {
             for (uint32_t j = it > S ? it - S : 0; j < it; ++j) {
@@ -184,10 +260,12 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1) matvec_imma_splitk_kernel(c
                     ok = false;
                     break;
                 }
-                if (ends_group(j)) sk_finish<FMT>(p, k, red, u0, j, lane);
+                ks_partial(p, q, red, W, sl, j, g0 + j, lane);
             }
         }
-        if (!ok && lane == 0) {  // no bulk copy may still be landing in this CTA's smem at exit
+        if (ok) {
+            ks_close(p, q, g0, n, lane);
+        } else if (lane == 0) {  // no box may still be landing in this CTA's smem at exit
             const uint32_t first = it > S ? it - S : 0;
             for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1u, p.err);
         }
@@ -198,7 +276,7 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1) matvec_imma_splitk_kernel(c
     pdl_wait();  // x, gamma, bias and residual come from the preceding kernels
     const uint32_t jw = lane >> 2, qd = lane & 3u;
     float inv = 1.0f;
-    if (p.gamma) {  // fused RMSNorm over all of K
+    if (p.gamma) {  // fused RMSNorm over all of K (every consumer warp takes part)
         double ss = 0.0;
         for (uint32_t sb = warp; sb < p.nb; sb += kNW) {
             const uint32_t e0 = 256u * sb + 32u * jw + 8u * qd;
@@ -214,137 +292,236 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1) matvec_imma_splitk_kernel(c
         for (uint32_t w = 0; w < kNW; ++w) tot += red_d[w];
         inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
     }
-    // quantise x into the image, kBatch super-blocks per warp at a time with
-    // all their global loads issued before the first is used
-    constexpr uint32_t kBatch = 5;
-    for (uint32_t sb0w = warp; sb0w < p.nb; sb0w += kBatch * kNW) {
-        float4 xa[kBatch][2], ga[kBatch][2];
-#pragma unroll
-        for (uint32_t b = 0; b < kBatch; ++b) {
-            const uint32_t sb = sb0w + b * kNW;
-            if (sb < p.nb) {
-                const uint32_t e0 = 256u * sb + 32u * jw + 8u * qd;
-                xa[b][0] = *reinterpret_cast<const float4*>(p.x + e0);
-                xa[b][1] = *reinterpret_cast<const float4*>(p.x + e0 + 4);
-                if (p.gamma) {
-                    ga[b][0] = *reinterpret_cast<const float4*>(p.gamma + e0);
-                    ga[b][1] = *reinterpret_cast<const float4*>(p.gamma + e0 + 4);
-                }
-            }
-        }
-#pragma unroll
-        for (uint32_t b = 0; b < kBatch; ++b) {
-            const uint32_t sb = sb0w + b * kNW;
-            if (sb >= p.nb) break;  // warp-uniform
-            float v[8] = {xa[b][0].x, xa[b][0].y, xa[b][0].z, xa[b][0].w, xa[b][1].x, xa[b][1].y, xa[b][1].z, xa[b][1].w};
-            if (p.gamma) {
-                const float gv[8] = {ga[b][0].x, ga[b][0].y, ga[b][0].z, ga[b][0].w,
-                                     ga[b][1].x, ga[b][1].y, ga[b][1].z, ga[b][1].w};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = (v[i] * inv) * gv[i];
-            }
-            uint8_t* img = xim + sb * kXimSb;
-            quantize8<FMT>(v, lane, img, reinterpret_cast<float*>(img + 768));
-        }
-    }
-    named_bar_sync(1, kNW * 32u);  // the whole x image is in place
+    if (warp >= W) return;  // narrower slice: this warp has no super-block
 
+    // this warp's super-block(s) of the slice: x slice, quantised, routed fragments
+    const uint32_t bA = kb0 + warp, bB = FMT == 14 ? kb0 + (warp ^ 1u) : bA;
+    XFrag f;
+    {
+        const uint32_t e0 = 256u * (jw < 4 ? bA : bB) + 32u * jw + 8u * qd;
+        const float4 a0 = *reinterpret_cast<const float4*>(p.x + e0);
+        const float4 a1 = *reinterpret_cast<const float4*>(p.x + e0 + 4);
+        float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        if (p.gamma) {
+            const float4 g0v = *reinterpret_cast<const float4*>(p.gamma + e0);
+            const float4 g1v = *reinterpret_cast<const float4*>(p.gamma + e0 + 4);
+            const float gv[8] = {g0v.x, g0v.y, g0v.z, g0v.w, g1v.x, g1v.y, g1v.z, g1v.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = (v[i] * inv) * gv[i];
+        }
+        uint8_t* xs = xscr + warp * kXScratch;
+        float* kc = reinterpret_cast<float*>(xs + 768);
+        quantize8<FMT>(v, lane, xs, kc);
+        __syncwarp();
+        gather_xfrag<FMT>(xs, kc, xs, kc, lane, f);
+    }
+    // this warp's column of the slice (Q6_K columns split at even blocks, so
+    // blocks w and w^1 share one), and where a row of it sits in a stage:
+    // region + (i * J + j) * bw + skew for row r = i + Rs * j
+    const bool c1 = sv.ncol == 2 && warp >= sv.cst[1];
+    const uint32_t cs = c1 ? sv.cst[1] : sv.cst[0];
+    const uint32_t bw = c1 ? sv.cbw[1] : sv.cbw[0];
+    const uint32_t coff = c1 ? sv.coff[1] : sv.coff[0];
     const uint32_t g = lane >> 2, t = lane & 3u;
-    const uint32_t m = warp & 1u, j = warp >> 1;  // this warp's 16-row tile and super-block of every unit
-    // tile rows (lanes g, lanes g+8): Q6_K takes rows 4g+m and 4g+2+m so each LDS sees one skew (conflict-free)
-    const uint32_t ra = FMT == 14 ? 4u * g + m : 16u * m + g;
-    const uint32_t rb2 = FMT == 14 ? 4u * g + 2u + m : 16u * m + g + 8u;
-    float y0 = 0.f, y1 = 0.f;
+    uint32_t rowA[2], rowB[2];  // stage offsets of tile m's rows (lanes g, lanes g+8); the same every round
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+        const uint2 rr = tile_rows<FMT, 2>(m, g);
+        const uint32_t r2[2] = {rr.x, rr.y};
+        uint32_t o[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t r = r2[h], i = r % Rs;
+            const uint32_t mis = (uint32_t)(((uint64_t)i * p.rb + (uint64_t)(kb0 + cs) * bsz) & 15u);
+            o[h] = coff + (i * J + r / Rs) * bw + mis;
+        }
+        rowA[m] = o[0];
+        rowB[m] = o[1];
+    }
+    const uint32_t offA = (warp - cs) * bsz, offB = (FMT == 14 ? ((warp ^ 1u) - cs) : (warp - cs)) * bsz;
+    const bool oddA = FMT == 14 && (warp & 1u) != 0u;
+
     for (uint32_t it = 0; it < n; ++it) {
         const uint32_t s = it % S;
         if (!mbar_wait(&full[s], (it / S) & 1u, p.err)) *abort_flag = 1;
         if (*abort_flag) break;
-        const uint32_t u = u0 + it, rg = u / k.n_ks, ks = u % k.n_ks;
-        const uint32_t sb0 = ks * kSB, nsb = min(kSB, p.nb - sb0);
         const uint8_t* st = stages + s * p.stage_smem;
-        if (j < nsb) {
-            const uint32_t sbA = sb0 + j, sbB = FMT == 14 ? sb0 + (j ^ 1u) : sbA;
-            const uint8_t* iA = xim + sbA * kXimSb;
-            const uint8_t* iB = xim + sbB * kXimSb;
-            XFrag f;
-            gather_xfrag<FMT>(iA, reinterpret_cast<const float*>(iA + 768), iB,
-                              reinterpret_cast<const float*>(iB + 768), lane, f);
-            const uint32_t row0 = ra * k.rs + row_mis(p, rg * kRowsU + ra, sb0, bsz);
-            const uint32_t row1 = rb2 * k.rs + row_mis(p, rg * kRowsU + rb2, sb0, bsz);
+        float y[2][2];
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            y[m][0] = y[m][1] = 0.f;
+            const uint32_t row0 = rowA[m], row1 = rowB[m];
             if (FMT == 12)
-                q4_tile(st, row0 + j * bsz, row1 + j * bsz, t, f, y0, y1);
-            else if (j & 1u)
-                q6_tile<true>(st, row0, row1, j * bsz, (j ^ 1u) * bsz, t, f, y0, y1);
+                q4_tile(st, row0 + offA, row1 + offA, t, f, y[m][0], y[m][1]);
+            else if (oddA)
+                q6_tile_lowreg<true>(st, row0, row1, offA, offB, t, f, y[m][0], y[m][1]);
             else
-                q6_tile<false>(st, row0, row1, j * bsz, (j ^ 1u) * bsz, t, f, y0, y1);
+                q6_tile_lowreg<false>(st, row0, row1, offA, offB, t, f, y[m][0], y[m][1]);
         }
-        if (ends_group(it)) {
-            // hand this warp's row sums to the producer (slot of this stage round, column j) and restart
-            float* rs = red + (((it / S) & 1u) * S + s) * kSB * kRowsU + j * kRowsU;
-            y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
-            y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
-            y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
-            y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
-            if (t == 0) {
-                rs[ra] = y0;
-                rs[rb2] = y1;
+        // sum the quad's four lanes; lanes t == 0 then hold this warp's partial of their rows
+        float* rs = red + ((((it / S) & 1u) * S + s) * kNW + warp) * kG;
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            const uint2 rr = tile_rows<FMT, 2>(m, g);
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                float v = y[m][r];
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                if (t == 0) rs[r ? rr.y : rr.x] = v;
             }
-            y0 = y1 = 0.f;
         }
         __syncwarp();
         if (lane == 0) {
             __threadfence_block();
-            mbar_arrive(&empty[s]);
+            mbar_arrive(&empty[s]);  // releases the stage and publishes this warp's partials
         }
     }
 }
 
-struct SkScratch {
+struct KsScratch {
     float* part = nullptr;
     uint32_t* cnt = nullptr;
     size_t part_floats = 0, cnt_n = 0;
 };
-std::mutex g_sk_mutex;
-SkScratch g_sk[64];
+std::mutex g_ks_mutex;
+KsScratch g_ks[64];
 
-struct SkConfig {
-    uint32_t S, rs, stage_smem, smem, grid;
-    SplitK k;
+struct KsPlan {
+    uint32_t S = 0, stage_smem = 0, smem = 0, grid = 0, n_groups = 0, nmaps = 0;
+    uint32_t map_bw[kMaxMaps] = {};  // box bytes of each tensor map
+    KSlice q{};
+    bool ok = false;
 };
 
-SkConfig sk_config(int fmt, uint32_t rows, uint32_t kk, int sms) {
-    SkConfig c{};
-    const uint32_t nb = kk / 256u;
+// Box bytes for a column of `wb` blocks: room for the widest 16-byte skew,
+// then padded so that consecutive rows of one LDS fall into distinct banks
+// (Q4_K: 8 or 24 words mod 32 for the 64-bit half-warp reads; Q6_K: an odd
+// multiple of 4 words for rows 4 apart).
+uint32_t ks_box_bytes(int fmt, uint32_t wb) {
     const uint32_t bsz = fmt == 12 ? 144u : 210u;
-    // row slot stride: Q4_K 8 words mod 32 banks (LDS.64 half-warps conflict-free); Q6_K room for the
-    // 16-byte skew and 16 x odd mod 128 bytes, so 8 rows of one residue mod 4 (one skew) hit distinct banks
-    uint32_t rs = (kSB * bsz + (fmt == 12 ? 0u : 12u) + 15u) & ~15u;
-    while (fmt == 12 ? ((rs / 4u) % 32u != 8u) : ((rs % 128u) / 16u % 2u != 1u)) rs += 16u;
-    c.rs = rs;
-    c.stage_smem = kRowsU * c.rs;
-    c.k.n_ks = (nb + kSB - 1) / kSB;
-    c.k.n_rg = (rows + kRowsU - 1) / kRowsU;
-    c.k.units = c.k.n_ks * c.k.n_rg;
-    c.k.rs = c.rs;
-    c.grid = std::min<uint32_t>(c.k.units, (uint32_t)sms);
-    // contributors per row group: CTAs whose unit range meets it
-    uint32_t slots = 1;
-    for (uint32_t rg = 0; rg < c.k.n_rg; ++rg) {
-        const uint64_t fu = (uint64_t)rg * c.k.n_ks, lu = fu + c.k.n_ks - 1;
-        const uint32_t a = (uint32_t)(((fu + 1) * c.grid - 1) / c.k.units);
-        const uint32_t b = (uint32_t)(((lu + 1) * c.grid - 1) / c.k.units);
-        slots = std::max(slots, b - a + 1);
-    }
-    c.k.slots = slots;
-    const uint32_t budget = 227u * 1024u;
-    uint32_t S = kMaxStages;
-    while (S > 2 && sk_stage_off(S, nb) + 128u + S * c.stage_smem > budget) --S;
-    c.S = S;
-    c.smem = sk_stage_off(S, nb) + 128u + S * c.stage_smem;
-    return c;
+    uint32_t bw = (wb * bsz + (fmt == 12 ? 0u : 12u) + 15u) & ~15u;
+    if (fmt == 12)
+        while ((bw / 4u) % 32u != 8u && (bw / 4u) % 32u != 24u) bw += 16u;
+    else
+        while (((bw / 16u) & 1u) == 0u) bw += 16u;
+    return bw;
 }
 
-int sk_sm_count() {
+// Slices and CTA shares for one shape: for each candidate slice count P the
+// widths are as even as possible (pairs of blocks for Q6_K), CTAs go one at a
+// time to the slice whose busiest CTA has the most work, and the P with the
+// least work on the busiest CTA wins.  Work = row groups x (width + 6): a row
+// segment costs about as much as six more blocks of it (measured on B200 with
+// the FFN-down shape: 6 slices of 12-13 blocks beat 10 slices of 7-8 by 15 %).
+// Each slice is then cut into at most two box columns of <= 2 KB per row.
+KsPlan ks_plan(int fmt, uint32_t rows, uint32_t k, uint32_t sms) {
+    KsPlan pl{};
+    const uint32_t nb = k / 256u, unit = fmt == 14 ? 2u : 1u, nu = nb / unit, wmax_u = kNW / unit;
+    pl.n_groups = (rows + kG - 1u) / kG;
+    uint64_t best = ~0ull;
+    uint32_t p_lo = (nu + wmax_u - 1u) / wmax_u;
+    uint32_t p_hi = std::min<uint32_t>(std::min<uint32_t>(kMaxSlices, nu), std::min<uint32_t>(p_lo + 4u, sms));
+    // tuning override for experiments: ARCLLM_KSLICE_P=<slice count> (kept within the legal range)
+    if (const char* e = std::getenv("ARCLLM_KSLICE_P")) {
+        const uint32_t f = (uint32_t)std::strtoul(e, nullptr, 10);
+        if (f >= p_lo && f <= std::min<uint32_t>(kMaxSlices, nu)) p_lo = p_hi = f;
+    }
+    for (uint32_t P = p_lo; P <= p_hi; ++P) {
+        uint32_t W[kMaxSlices], C[kMaxSlices];
+        for (uint32_t i = 0; i < P; ++i) {
+            W[i] = (nu / P + (i < nu % P ? 1u : 0u)) * unit;
+            C[i] = 1u;
+        }
+        auto cost = [&](uint32_t i) { return (uint64_t)(W[i] + 6u) * ((pl.n_groups + C[i] - 1u) / C[i]); };
+        for (uint32_t total = P; total < sms; ++total) {
+            uint32_t bi = P;
+            for (uint32_t i = 0; i < P; ++i)
+                if (C[i] < pl.n_groups && (bi == P || cost(i) > cost(bi))) bi = i;
+            if (bi == P) break;
+            ++C[bi];
+        }
+        uint64_t mx = 0;
+        for (uint32_t i = 0; i < P; ++i) mx = std::max(mx, cost(i));
+        if (mx < best) {
+            best = mx;
+            pl.q.P = P;
+            uint32_t kb = 0, c0 = 0;
+            for (uint32_t i = 0; i < P; ++i) {
+                pl.q.kb0[i] = (uint16_t)kb;
+                pl.q.W[i] = (uint16_t)W[i];
+                pl.q.cta0[i] = (uint16_t)c0;
+                kb += W[i];
+                c0 += C[i];
+            }
+            pl.q.cta0[P] = (uint16_t)c0;
+            pl.grid = c0;
+        }
+    }
+    // box columns: Q4_K one (14 x 144 B = 2016 B fits a box row), Q6_K up to
+    // two of <= 8 blocks, split in pairs as evenly as possible
+    const uint32_t colmax = fmt == 12 ? kNW : 8u;
+    uint32_t stage = 0;
+    for (uint32_t s = 0; s < pl.q.P; ++s) {
+        const uint32_t Wd = pl.q.W[s];
+        const uint32_t ncol = (Wd + colmax - 1u) / colmax;
+        uint32_t wcol[2] = {Wd, 0u};
+        if (ncol == 2) {
+            const uint32_t pairs = Wd / 2u;
+            wcol[0] = 2u * ((pairs + 1u) / 2u);
+            wcol[1] = Wd - wcol[0];
+        }
+        pl.q.ncol[s] = (uint8_t)ncol;
+        uint32_t off = 0, cst = 0;
+        for (uint32_t c = 0; c < ncol; ++c) {
+            const uint32_t bw = ks_box_bytes(fmt, wcol[c]);
+            if (bw > kBoxMax) return pl;
+            uint32_t mi = 0;
+            while (mi < pl.nmaps && pl.map_bw[mi] != bw) ++mi;
+            if (mi == pl.nmaps) {
+                if (pl.nmaps == kMaxMaps) return pl;
+                pl.map_bw[pl.nmaps++] = bw;
+            }
+            pl.q.cst[s][c] = (uint8_t)cst;
+            pl.q.cmap[s][c] = (uint8_t)mi;
+            pl.q.cbw[s][c] = (uint16_t)bw;
+            pl.q.coff[s][c] = off;
+            off += kG * bw;  // Rs boxes of kG / Rs rows
+            cst += wcol[c];
+        }
+        pl.q.tx[s] = off;
+        stage = std::max(stage, off);
+    }
+    pl.q.tx_max = stage;
+    pl.stage_smem = (stage + 127u) & ~127u;
+    uint32_t S = kMaxStages;
+    while (S > 2 && ks_stage_off(S) + 128u + S * pl.stage_smem > 227u * 1024u) --S;
+    pl.S = S;
+    pl.smem = ks_stage_off(S) + 128u + S * pl.stage_smem;
+    pl.ok = pl.smem <= 227u * 1024u;
+    return pl;
+}
+
+// Plans are pure functions of the shape and SM count: cache them.
+KsPlan ks_plan_cached(int fmt, uint32_t rows, uint32_t k, uint32_t sms) {
+    struct Entry {
+        int fmt;
+        uint32_t rows, k, sms;
+        KsPlan pl;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    if (std::getenv("ARCLLM_KSLICE_P")) return ks_plan(fmt, rows, k, sms);  // tuning runs bypass the cache
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry& e : cache)
+        if (e.fmt == fmt && e.rows == rows && e.k == k && e.sms == sms) return e.pl;
+    KsPlan pl = ks_plan(fmt, rows, k, sms);
+    if (cache.size() >= 64) cache.erase(cache.begin());
+    cache.push_back(Entry{fmt, rows, k, sms, pl});
+    return pl;
+}
+
+int ks_sm_count() {
     static int sm_count[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -353,15 +530,22 @@ int sk_sm_count() {
     return sms;
 }
 
+template <int FMT>
+cudaError_t set_attr_ks() {
+    return cudaFuncSetAttribute(matvec_imma_kslice_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                227 * 1024);
+}
+
 }  // namespace
 
 int matvec_splitk_reserve(int fmt, uint32_t rows, uint32_t k) {
-    const SkConfig c = sk_config(fmt, rows, k, sk_sm_count());
-    const size_t need_part = (size_t)c.k.n_rg * c.k.slots * kRowsU, need_cnt = c.k.n_rg;
+    if (!matvec_splitk_supported(fmt, false, rows, k)) return ARC_OK;  // another kernel serves this shape
+    const KsPlan pl = ks_plan_cached(fmt, rows, k, (uint32_t)ks_sm_count());
+    const size_t need_part = (size_t)pl.q.P * rows, need_cnt = pl.n_groups;
     int dev = 0;
     cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lock(g_sk_mutex);
-    SkScratch& sc = g_sk[dev & 63];
+    std::lock_guard<std::mutex> lock(g_ks_mutex);
+    KsScratch& sc = g_ks[dev & 63];
     if (sc.part_floats >= need_part && sc.cnt_n >= need_cnt) return ARC_OK;
     const size_t np = std::max(need_part, sc.part_floats), nc = std::max(need_cnt, sc.cnt_n);
     float* part = nullptr;
@@ -389,23 +573,21 @@ int matvec_splitk_prepare() {
     int dev = 0;
     cudaGetDevice(&dev);
     if (done[dev & 63]) return ARC_OK;
-    cudaError_t e = cudaFuncSetAttribute(matvec_imma_splitk_kernel<12>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(matvec_imma_splitk_kernel<14>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 227 * 1024);
+    cudaError_t e = set_attr_ks<12>();
+    if (e == cudaSuccess) e = set_attr_ks<14>();
     if (e != cudaSuccess) return set_cuda_error(e, "matvec split-K prepare");
     done[dev & 63] = true;
     return ARC_OK;
 }
 
-// Single matrix, K > 3584 with an even number of super-blocks (Q6_K pairing;
-// Q4_K too, so that both formats take the same path), the x image in smem.
+// Single matrix, K > 3584; Q6_K: an even number of super-blocks and a
+// multiple of 4 rows (the tensor-map super-rows).
 bool matvec_splitk_supported(int fmt, bool dual, uint32_t rows, uint32_t k) {
-    if ((fmt != 12 && fmt != 14) || dual || rows == 0 || k % 512u) return false;
+    if ((fmt != 12 && fmt != 14) || dual || rows == 0 || k % 256u) return false;
     const uint32_t nb = k / 256u;
-    if (nb <= 14) return false;
-    return sk_config(fmt, rows, k, 148).smem <= 227u * 1024u;
+    if (nb <= 14 || (fmt == 14 && ((nb & 1u) || (rows & 3u)))) return false;
+    if (nb > kNW * kMaxSlices) return false;
+    return ks_plan_cached(fmt, rows, k, 148).ok;
 }
 
 int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, const float* x, const float* gamma,
@@ -418,14 +600,30 @@ int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, cons
     int st = matvec_splitk_prepare();
     if (st == ARC_OK) st = matvec_splitk_reserve(fmt, rows, k);
     if (st != ARC_OK) return st;
-    const SkConfig c = sk_config(fmt, rows, k, sk_sm_count());
+    KsPlan pl = ks_plan_cached(fmt, rows, k, (uint32_t)ks_sm_count());
+    if (!pl.ok) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec split-K: no plan fits shared memory");
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return set_error(ARC_E_CUDA, "matvec split-K: cuTensorMapEncodeTiled unavailable");
+    // the matrix as u64 words in super-rows of Rs rows (Rs * row bytes is a multiple of 16)
+    const uint32_t nb = k / 256u, rb = nb * (fmt == 12 ? 144u : 210u), Rs = fmt == 12 ? 1u : 4u;
+    KMaps maps;
+    std::memset(&maps, 0, sizeof maps);
+    for (uint32_t i = 0; i < pl.nmaps; ++i) {
+        const cuuint64_t dims[2] = {(cuuint64_t)Rs * rb / 8u, (cuuint64_t)(rows / Rs)};
+        const cuuint64_t strides[1] = {(cuuint64_t)Rs * rb};
+        const cuuint32_t box[2] = {pl.map_bw[i] / 8u, kG / Rs};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUresult r = enc(&maps.m[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return set_error(ARC_E_INVALID_ARGUMENT, "matvec split-K: tensor map rejected");
+    }
     int dev = 0;
     cudaGetDevice(&dev);
-    SplitK sk = c.k;
     {
-        std::lock_guard<std::mutex> lock(g_sk_mutex);
-        sk.part = g_sk[dev & 63].part;
-        sk.cnt = g_sk[dev & 63].cnt;
+        std::lock_guard<std::mutex> lock(g_ks_mutex);
+        pl.q.part = g_ks[dev & 63].part;
+        pl.q.cnt = g_ks[dev & 63].cnt;
     }
     MvParams p{};
     p.w0 = static_cast<const uint8_t*>(w);
@@ -438,16 +636,17 @@ int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, cons
     p.err = dev_error_word();
     p.rows = rows;
     p.k = k;
-    p.nb = k / 256u;
-    p.rb = p.nb * (fmt == 12 ? 144u : 210u);
-    p.G = kRowsU;
-    p.n_groups = c.k.n_rg;
-    p.stages = c.S;
-    p.stage_smem = c.stage_smem;
+    p.nb = nb;
+    p.rb = rb;
+    p.G = kG;
+    p.n_groups = pl.n_groups;
+    p.stages = pl.S;
+    p.stage_smem = pl.stage_smem;
     p.early = pdl_enabled() ? 1u : 0u;
+    const dim3 block((kNW + 1) * 32);
     const cudaError_t e =
-        fmt == 12 ? launch_kernel(matvec_imma_splitk_kernel<12>, dim3(c.grid), dim3((kNW + 1) * 32), c.smem, stream, p, sk)
-                  : launch_kernel(matvec_imma_splitk_kernel<14>, dim3(c.grid), dim3((kNW + 1) * 32), c.smem, stream, p, sk);
+        fmt == 12 ? launch_kernel(matvec_imma_kslice_kernel<12>, dim3(pl.grid), block, pl.smem, stream, p, pl.q, maps)
+                  : launch_kernel(matvec_imma_kslice_kernel<14>, dim3(pl.grid), block, pl.smem, stream, p, pl.q, maps);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "matvec split-K launch");
 }
 

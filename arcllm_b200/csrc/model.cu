@@ -177,7 +177,9 @@ int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
     ARC_TRY(matvec_prepare());
     ARC_TRY(matvec_imma_prepare());
     ARC_TRY(matvec_splitk_prepare());
-    ARC_TRY(matvec_splitk_reserve(ARC_GGML_Q4_K, cfg->hidden, cfg->ffn));  // FFN down, before any graph capture
+    // FFN down scratch for the K-slice kernel, before any graph capture (either format)
+    ARC_TRY(matvec_splitk_reserve(ARC_GGML_Q4_K, cfg->hidden, cfg->ffn));
+    ARC_TRY(matvec_splitk_reserve(ARC_GGML_Q6_K, cfg->hidden, cfg->ffn));
     ARC_TRY(decode_ops_prepare());
     if (!dev_error_word()) return set_error(ARC_E_CUDA, "model_create: device error word unavailable");
     auto* m = new (std::nothrow) arcllm_cuda_model();

@@ -137,8 +137,11 @@ CASES = [
 # split-K tensor-core kernel (opt-in for K > 3584): single row, several 32-row
 # groups, ragged last group, K not a multiple of the 6-super-block chunk, more
 # work units than SMs, a 13-row matrix whose last row ends inside a 16-byte word
+# Q6_K rows must be a multiple of 4 for the long-K tensor-core kernel; the
+# other Q6_K cases check that those shapes fall back to the CUDA-core kernel.
 SPLITK_CASES = [("q4k", 1, 18944), ("q6k", 2, 4096), ("q4k", 40, 4608), ("q6k", 700, 18944), ("q6k", 13, 18944),
-                ("q4k", 3584, 18944), ("q6k", 3584, 18944)]
+                ("q4k", 3584, 18944), ("q6k", 3584, 18944), ("q6k", 12, 18944), ("q6k", 4, 4096), ("q4k", 3, 18944),
+                ("q4k", 1000, 32768)]
 
 
 @pytest.mark.parametrize("fmt,rows,k", CASES)
@@ -157,6 +160,20 @@ def test_matvec_parity(fmt, rows, k):
 def test_matvec_splitk_parity(fmt, rows, k, monkeypatch):
     monkeypatch.setenv("ARCLLM_MATVEC_IMPL", "splitk")
     test_matvec_parity(fmt, rows, k)
+
+
+@pytest.mark.parametrize("fmt", ["q4k", "q6k"])
+def test_matvec_splitk_repeat_bit_identical(fmt, monkeypatch):
+    """The cross-CTA reduction re-arms its counters and adds slice partials in
+    a fixed order: back-to-back launches give bit-identical rows."""
+    monkeypatch.setenv("ARCLLM_MATVEC_IMPL", "splitk")
+    rows, k, seed = 3584, 18944, 5151
+    w = gpu_fill(fmt, rows, k, seed)
+    x = O.normal_f32(k, seed + 1)
+    ys = [run_matvec(fmt, w, rows, k, x) for _ in range(3)]
+    assert np.array_equal(ys[0].view(np.uint32), ys[1].view(np.uint32))
+    assert np.array_equal(ys[0].view(np.uint32), ys[2].view(np.uint32))
+    G.check_device_error()
 
 
 @pytest.mark.parametrize("fmt", ["q4k", "q6k"])
