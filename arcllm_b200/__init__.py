@@ -35,6 +35,10 @@ SIGNATURES = {
     "arcllm_cuda_matvec_q6k": [_vp, _u32, _u32, _vp, _vp, _vp, _vp],
     "arcllm_cuda_gateup_silu_q4k": [_vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp],
     "arcllm_cuda_gemm_q4k_bf16": [_vp, _u32, _u32, _vp, _u32, _vp, _vp],
+    "arcllm_cuda_gemm_bf16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],
+    "arcllm_cuda_rope_kv_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
+                                 _vp],
+    "arcllm_cuda_attention_prefill": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _vp],
     "arcllm_cuda_exec148_materialize": [_vp, _u64, _vp, _vp],
     "arcllm_cuda_exec148_validate": [_vp, _vp, _u64, C.POINTER(C.c_uint64), _vp],
     "arcllm_cuda_fill_q4k": [_vp, _u64, _u64, _u64, _vp],
@@ -63,6 +67,8 @@ SIGNATURES = {
     "arcllm_cuda_model_generate": [_vp, _vp, _u32, _u32, _vp, _vp, _vp],
     "arcllm_cuda_model_begin": [_vp, _vp, _u32, _u32, _vp],
     "arcllm_cuda_model_step": [_vp, _i32, _i32, _vp],
+    "arcllm_cuda_model_set_prefill_mode": [_vp, _i32],
+    "arcllm_cuda_model_set_prefill_down": [_vp, _u32, _vp, _i32],
     "arcllm_cuda_model_logits": [_vp, C.POINTER(_vp)],
     "arcllm_cuda_model_kv_cache": [_vp, C.POINTER(_vp), C.POINTER(_vp)],
     "arcllm_cuda_model_shard_lm_head": [_vp, _u32, _u32],

@@ -110,6 +110,9 @@ int exec148_matvec(const void* w, uint32_t rows, uint32_t k, const float* x, con
 int gemm_q4k_bf16_prepare();
 int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,
                   cudaStream_t stream);
+// Q4_K (12) or Q6_K (14) weights; y = residual + x W^T when residual is non-null.
+int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
+                 const float* residual, float* y, cudaStream_t stream);
 
 std::vector<float> rope_table(uint32_t max_ctx, uint32_t head_dim, float theta);
 int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out);
@@ -123,6 +126,8 @@ int model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_pr
 int model_step(arcllm_cuda_model* m, int with_head, int use_graph, cudaStream_t st);
 int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
                    uint32_t* out_host, arcllm_cuda_gen_stats* stats, cudaStream_t st);
+int model_set_prefill_mode(arcllm_cuda_model* m, int mode);
+int model_set_prefill_down(arcllm_cuda_model* m, uint32_t layer, const void* w, int type);
 int model_logits(arcllm_cuda_model* m, const float** out);
 int model_kv_cache(arcllm_cuda_model* m, const uint16_t** k, const uint16_t** v);
 

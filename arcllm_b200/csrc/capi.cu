@@ -9,6 +9,7 @@
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
 #include "decode_ops.h"
+#include "prefill_ops.h"
 
 namespace arc {
 
@@ -185,6 +186,13 @@ int arcllm_cuda_gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint1
     ARC_GUARD_END
 }
 
+int arcllm_cuda_gemm_bf16(int type, const void* w, uint32_t n, uint32_t k, const uint16_t* x_bf16, uint32_t m,
+                          const float* residual, float* y, void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::gemm_kq_bf16(type, w, n, k, x_bf16, m, residual, y, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_fill_q4k(void* w, uint64_t block_begin, uint64_t n_blocks, uint64_t seed, void* stream) {
     ARC_GUARD_BEGIN
     return arc::fill_blocks(12, w, block_begin, n_blocks, seed, static_cast<cudaStream_t>(stream));
@@ -246,6 +254,31 @@ int arcllm_cuda_attention_decode(const float* q, const uint16_t* k_cache, const 
         return set_error(ARC_E_INVALID_ARGUMENT, "attention: bad shape");
     arc::AttnShape s{q_heads, kv_heads, head_dim, max_ctx, layer, n_splits, 1.0f / std::sqrt((float)head_dim)};
     return arc::launch_attention(q, k_cache, v_cache, pos_dev, s, scratch, out, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_rope_kv_rows(float* q, float* k, const float* v, const float* bq, const float* bk, const float* bv,
+                             const float* table, uint32_t pos0, uint32_t rows, uint16_t* k_cache, uint16_t* v_cache,
+                             uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, uint32_t max_ctx, uint32_t layer,
+                             void* stream) {
+    ARC_GUARD_BEGIN
+    if (!q || !k || !v || !table || !k_cache || !v_cache) return set_error(ARC_E_INVALID_ARGUMENT, "rope rows: null");
+    if (head_dim == 0 || head_dim % 2u || kv_heads == 0 || q_heads == 0 || max_ctx == 0)
+        return set_error(ARC_E_INVALID_ARGUMENT, "rope rows: bad shape");
+    arc::RopeKvShape s{q_heads, kv_heads, head_dim, max_ctx, layer};
+    return arc::launch_rope_kv_rows(q, k, v, bq, bk, bv, reinterpret_cast<const float2*>(table), pos0, rows, k_cache,
+                                    v_cache, s, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_attention_prefill(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, uint32_t pos0,
+                                  uint32_t rows, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                                  uint32_t max_ctx, uint32_t layer, uint16_t* out_bf16, void* stream) {
+    ARC_GUARD_BEGIN
+    if (!q || !k_cache || !v_cache || !out_bf16) return set_error(ARC_E_INVALID_ARGUMENT, "attention prefill: null");
+    if (kv_heads == 0 || max_ctx == 0 || rows > 65535u) return set_error(ARC_E_INVALID_ARGUMENT, "attention prefill: bad shape");
+    arc::AttnShape s{q_heads, kv_heads, head_dim, max_ctx, layer, 1, 1.0f / std::sqrt((float)head_dim)};
+    return arc::launch_attention_prefill(q, k_cache, v_cache, pos0, rows, s, out_bf16, static_cast<cudaStream_t>(stream));
     ARC_GUARD_END
 }
 
@@ -382,6 +415,18 @@ int arcllm_cuda_model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, u
 int arcllm_cuda_model_step(arcllm_cuda_model* m, int with_head, int use_graph, void* stream) {
     ARC_GUARD_BEGIN
     return arc::model_step(m, with_head, use_graph, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_set_prefill_mode(arcllm_cuda_model* m, int mode) {
+    ARC_GUARD_BEGIN
+    return arc::model_set_prefill_mode(m, mode);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_set_prefill_down(arcllm_cuda_model* m, uint32_t layer, const void* w, int type) {
+    ARC_GUARD_BEGIN
+    return arc::model_set_prefill_down(m, layer, w, type);
     ARC_GUARD_END
 }
 

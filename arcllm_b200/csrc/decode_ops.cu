@@ -33,7 +33,8 @@ __global__ void embed_f16_kernel(const uint16_t* __restrict__ table, const uint3
                                  uint32_t h, uint32_t vocab, float* __restrict__ out, unsigned int* err) {
     pdl_trigger();
     pdl_wait();  // inputs come from the preceding kernels
-    const uint32_t tok = *token_src;
+    const uint32_t tok = token_src[blockIdx.z];  // row z of a batch (one row for a decode step)
+    out += (uint64_t)blockIdx.z * h;
     if (tok >= vocab) {
         if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, ARC_DEV_ERR_BOUNDS);
         return;
@@ -47,7 +48,8 @@ __global__ void embed_q4k_kernel(const uint8_t* __restrict__ table, const uint32
                                  uint32_t h, uint32_t vocab, float* __restrict__ out, unsigned int* err) {
     pdl_trigger();
     pdl_wait();  // inputs come from the preceding kernels
-    const uint32_t tok = *token_src;
+    const uint32_t tok = token_src[blockIdx.z];  // row z of a batch (one row for a decode step)
+    out += (uint64_t)blockIdx.z * h;
     if (tok >= vocab) {
         if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, ARC_DEV_ERR_BOUNDS);
         return;
@@ -308,13 +310,19 @@ int launch_checked(cudaError_t e, const char* what) { return e == cudaSuccess ? 
 
 int launch_embed(int type, const void* table, const uint32_t* token_src, uint32_t h, uint32_t vocab, float* out,
                  cudaStream_t stream) {
+    return launch_embed_rows(type, table, token_src, 1, h, vocab, out, stream);
+}
+
+int launch_embed_rows(int type, const void* table, const uint32_t* token_src, uint32_t rows, uint32_t h,
+                      uint32_t vocab, float* out, cudaStream_t stream) {
+    if (rows == 0 || rows > 65535u) return set_error(ARC_E_INVALID_ARGUMENT, "embedding: 1..65535 rows");
     if (type == 1)
-        return launch_checked(launch_kernel(embed_f16_kernel, dim3((h + 255) / 256), dim3(256), 0, stream,
+        return launch_checked(launch_kernel(embed_f16_kernel, dim3((h + 255) / 256, 1, rows), dim3(256), 0, stream,
                                             static_cast<const uint16_t*>(table), token_src, h, vocab, out,
                                             dev_error_word()),
                               "embed launch");
     if (type == 12)
-        return launch_checked(launch_kernel(embed_q4k_kernel, dim3(h / 256), dim3(256), 0, stream,
+        return launch_checked(launch_kernel(embed_q4k_kernel, dim3(h / 256, 1, rows), dim3(256), 0, stream,
                                             static_cast<const uint8_t*>(table), token_src, h, vocab, out,
                                             dev_error_word()),
                               "embed launch");

@@ -29,8 +29,13 @@ struct AttnShape {
 
 // Load every decode-op kernel on the current device (before graph capture).
 int decode_ops_prepare();
+// ARC_OK, or the CUDA error of a launch recorded under `what`
+int launch_checked(cudaError_t e, const char* what);
 int launch_embed(int type, const void* table, const uint32_t* token_src, uint32_t h, uint32_t vocab, float* out,
                  cudaStream_t stream);
+// rows tokens token_src[0..rows) -> out[rows][h]
+int launch_embed_rows(int type, const void* table, const uint32_t* token_src, uint32_t rows, uint32_t h,
+                      uint32_t vocab, float* out, cudaStream_t stream);
 int launch_rope_kv_store(float* q, float* k, const float* v, const float2* table, const uint32_t* pos_src,
                          uint16_t* kc, uint16_t* vc, const RopeKvShape& s, cudaStream_t stream);
 // part: scratch of kv_heads * n_splits * (q_heads/kv_heads) * (head_dim + 2) floats

@@ -192,9 +192,55 @@ __device__ __forceinline__ void dequant_subblock(uint4 q0, uint4 q1, uint32_t fb
     }
 }
 
+// 8 little-endian words of the 32 bytes at a 2-byte-aligned global address,
+// from 9 aligned word loads (the word past the end stays inside the Q6_K
+// block for every caller) and funnel shifts.
+struct Raw9 {
+    uint32_t r[9];
+};
+__device__ __forceinline__ void ld_raw9(const uint8_t* p, Raw9& o) {
+    const uint32_t* a = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
+#pragma unroll
+    for (int i = 0; i < 9; ++i) o.r[i] = __ldg(a + i);
+}
+__device__ __forceinline__ uint32_t raw9_word(const Raw9& o, int i, uint32_t sh) {
+    return __funnelshift_r(o.r[i], o.r[i + 1], sh);
+}
+
+// Dequantise quarter q of half h of one Q6_K super-block row -- 32 weights,
+// elements 32*hi .. +31 of the 64-element stage row -- to bf16: the 6-bit code
+// c = low nibble of ql | 2 bits of qh << 4 (src/p8c_segmented_access_correctness.cpp:905-956),
+// c - 32 as bf16 via (128 + c) - 160 (exact), times f = bf16(d * sc) with one
+// rounding; scales sc[8h + 2q] (elements 0..15) and sc[8h + 2q + 1] (16..31).
+__device__ __forceinline__ void dequant_q6_quarter(const Raw9& ql, uint32_t shl, const Raw9& qh, uint32_t shh,
+                                                   uint32_t lo_shift, uint32_t qh_shift, uint32_t f0, uint32_t f1,
+                                                   uint32_t n, uint32_t hi, uint8_t* btile) {
+    uint8_t* rowbase = btile + (n >> 3) * 1024u + (n & 7u) * 128u;
+    constexpr uint32_t k128 = 0x43004300u, k160 = 0x43204320u, kNegZero = 0x80008000u;
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {  // output chunk: elements 8*ch .. +7
+        uint32_t out[4];
+#pragma unroll
+        for (int wi = 0; wi < 2; ++wi) {
+            const int i = 2 * ch + wi;
+            const uint32_t c = ((raw9_word(ql, i, shl) >> lo_shift) & 0x0F0F0F0Fu) |
+                               (((raw9_word(qh, i, shh) >> qh_shift) & 0x03030303u) << 4);
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {
+                const uint32_t spread = __byte_perm(c, 0u, pr ? 0x4342u : 0x4140u);
+                out[2 * wi + pr] = bfma2(bsub2(spread | k128, k160), ch < 2 ? f0 : f1, kNegZero);
+            }
+        }
+        const uint32_t chunk = 4u * hi + ch;
+        *reinterpret_cast<uint4*>(rowbase + ((chunk ^ (n & 7u)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+}
+
+template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_q4k_bf16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w, uint32_t n_total,
-                         uint32_t k, uint32_t m, float* __restrict__ y, unsigned int* err, const SplitKWs sk) {
+    gemm_kq_bf16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w, uint32_t n_total,
+                        uint32_t k, uint32_t m, const float* __restrict__ residual, float* __restrict__ y,
+                        unsigned int* err, const SplitKWs sk) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + kStages * kStageBytes);
@@ -204,7 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sb_begin = nsb * split / sk.ks, sb_end = nsb * (split + 1u) / sk.ks;
     const uint32_t kbase = 4u * sb_begin;          // first 64-wide K block of this CTA
     const uint32_t nkb = 4u * (sb_end - sb_begin);  // K blocks of this CTA
-    const uint32_t rb = (k / 256u) * 144u;
+    constexpr uint32_t bsz = FMT == 12 ? 144u : 210u;
+    const uint32_t rb = (k / 256u) * bsz;
 
     if (tid == 0) {
         for (uint32_t s = 0; s < kStages; ++s) {
@@ -272,32 +319,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- dequant producers, then epilogue ----------------
         const uint32_t dt = tid - 64u;  // 0..255: W row dt >> 1 of this CTA, sub-block half dt & 1 of the stage
         const uint32_t nrow = dt >> 1, hi = dt & 1u;
-        const uint8_t* row = w + (uint64_t)(n0 + nrow) * rb + (uint64_t)sb_begin * 144u;  // this split's K range
-        // the code bytes of stage kb are loaded kPrefetch stages ahead, so
-        // global-memory latency overlaps the dequantisation of earlier stages;
-        // scales are unpacked once per super-block (every 4 stages)
-        constexpr uint32_t kPrefetch = 4;
-        uint4 pq0[kPrefetch], pq1[kPrefetch];
-        auto load_codes = [&](uint32_t kb, uint4& a, uint4& b) {
-            const uint8_t* blk = row + (kb >> 2) * 144u + 16u + 32u * (kb & 3u);
-            a = ld_nc_v4(blk);
-            b = ld_nc_v4(blk + 16u);
-        };
+        const uint8_t* row = w + (uint64_t)(n0 + nrow) * rb + (uint64_t)sb_begin * bsz;  // this split's K range
+        if (FMT == 14) {
+            // Q6_K: thread (nrow, hi) dequantises quarter 2*(sub & 1) + hi of half sub >> 1 of each
+            // super-block (sub = stage index within the super-block); raw words prefetched 2 stages ahead
+            constexpr uint32_t kPf = 2;
+            Raw9 pql[kPf], pqh[kPf];
+            uint32_t psc[kPf];
+            auto load6 = [&](uint32_t kb, Raw9& a, Raw9& b, uint32_t& scd) {
+                const uint8_t* blk = row + (kb >> 2) * 210u;
+                const uint32_t sub = kb & 3u, h = sub >> 1, q = 2u * (sub & 1u) + hi;
+                ld_raw9(blk + 64u * h + 32u * hi, a);
+                ld_raw9(blk + 128u + 32u * h, b);
+                const uint32_t sc2 = *reinterpret_cast<const unsigned short*>(blk + 192u + 8u * h + 2u * q);
+                const uint32_t dd = *reinterpret_cast<const unsigned short*>(blk + 208u);
+                scd = sc2 | (dd << 16);
+            };
 #pragma unroll
-        for (uint32_t i = 0; i < kPrefetch; ++i)
-            if (i < nkb) load_codes(i, pq0[i], pq1[i]);
-        uint4 hd_next = ld_nc_v4(row);
-        uint32_t fb[4], ob[4];
-        bool stop = false;
-        for (uint32_t kb0 = 0; kb0 < nkb && !stop; kb0 += kPrefetch) {  // kPrefetch == 4: one super-block
-            subblock_consts(hd_next, hi, fb, ob);
-            if (kb0 + 4u < nkb) hd_next = ld_nc_v4(row + ((kb0 >> 2) + 1u) * 144u);
+            for (uint32_t i = 0; i < kPf; ++i)
+                if (i < nkb) load6(i, pql[i], pqh[i], psc[i]);
+            bool stop6 = false;
+            for (uint32_t kb0 = 0; kb0 < nkb && !stop6; kb0 += kPf) {
 #pragma unroll
-            for (uint32_t i = 0; i < kPrefetch; ++i) {
-                const uint32_t kb = kb0 + i;
+              for (uint32_t slot = 0; slot < kPf; ++slot) {
+                const uint32_t kb = kb0 + slot;
                 if (kb >= nkb) break;
-                const uint4 c0 = pq0[i], c1 = pq1[i];
-                if (kb + kPrefetch < nkb) load_codes(kb + kPrefetch, pq0[i], pq1[i]);
+                const Raw9 ql = pql[slot], qh = pqh[slot];
+                const uint32_t scd = psc[slot];
+                const uint8_t* blk = row + (kb >> 2) * 210u;
+                const uint32_t sub = kb & 3u, h = sub >> 1, q = 2u * (sub & 1u) + hi;
+                const uint32_t shl = (uint32_t)((reinterpret_cast<uintptr_t>(blk + 64u * h + 32u * hi)) & 3u) * 8u;
+                const uint32_t shh = (uint32_t)((reinterpret_cast<uintptr_t>(blk + 128u + 32u * h)) & 3u) * 8u;
+                if (kb + kPf < nkb) load6(kb + kPf, pql[slot], pqh[slot], psc[slot]);
+                const float d = __half2float(__ushort_as_half((unsigned short)(scd >> 16)));
+                const float s0 = d * (float)(int8_t)(scd & 0xFFu), s1 = d * (float)(int8_t)((scd >> 8) & 0xFFu);
+                const uint32_t f0 = bf16x2(s0, s0), f1 = bf16x2(s1, s1);
                 const uint32_t s = kb % kStages;
                 bool ok = true;
                 if (kb >= kStages) {
@@ -306,13 +362,58 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok) *abort_flag = 1;
                 if (*abort_flag) {
-                    stop = true;
+                    stop6 = true;
                     break;
                 }
-                dequant_subblock(c0, c1, fb[i], ob[i], nrow, hi, smem + s * kStageBytes + 2 * kAHalf);
+                dequant_q6_quarter(ql, shl, qh, shh, 4u * (sub & 1u), 2u * q, f0, f1, nrow, hi,
+                                   smem + s * kStageBytes + 2 * kAHalf);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tail->full_b[s]);
+              }
+            }
+        } else {
+            // the code bytes of stage kb are loaded kPrefetch stages ahead, so
+            // global-memory latency overlaps the dequantisation of earlier stages;
+            // scales are unpacked once per super-block (every 4 stages)
+            constexpr uint32_t kPrefetch = 4;
+            uint4 pq0[kPrefetch], pq1[kPrefetch];
+            auto load_codes = [&](uint32_t kb, uint4& a, uint4& b) {
+                const uint8_t* blk = row + (kb >> 2) * 144u + 16u + 32u * (kb & 3u);
+                a = ld_nc_v4(blk);
+                b = ld_nc_v4(blk + 16u);
+            };
+    #pragma unroll
+            for (uint32_t i = 0; i < kPrefetch; ++i)
+                if (i < nkb) load_codes(i, pq0[i], pq1[i]);
+            uint4 hd_next = ld_nc_v4(row);
+            uint32_t fb[4], ob[4];
+            bool stop = false;
+            for (uint32_t kb0 = 0; kb0 < nkb && !stop; kb0 += kPrefetch) {  // kPrefetch == 4: one super-block
+                subblock_consts(hd_next, hi, fb, ob);
+                if (kb0 + 4u < nkb) hd_next = ld_nc_v4(row + ((kb0 >> 2) + 1u) * 144u);
+    #pragma unroll
+                for (uint32_t i = 0; i < kPrefetch; ++i) {
+                    const uint32_t kb = kb0 + i;
+                    if (kb >= nkb) break;
+                    const uint4 c0 = pq0[i], c1 = pq1[i];
+                    if (kb + kPrefetch < nkb) load_codes(kb + kPrefetch, pq0[i], pq1[i]);
+                    const uint32_t s = kb % kStages;
+                    bool ok = true;
+                    if (kb >= kStages) {
+                        if (lane == 0) ok = mbar_wait(&tail->empty[s], ((kb / kStages) - 1u) & 1u, err);
+                        ok = __shfl_sync(0xffffffffu, ok, 0);
+                    }
+                    if (!ok) *abort_flag = 1;
+                    if (*abort_flag) {
+                        stop = true;
+                        break;
+                    }
+                    dequant_subblock(c0, c1, fb[i], ob[i], nrow, hi, smem + s * kStageBytes + 2 * kAHalf);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tail->full_b[s]);
+                }
             }
         }
         // epilogue: warp (2..5) % 4 owns TMEM lanes 32*q .. 32*q+31
@@ -330,11 +431,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(tmem + ((32u * q) << 16) + acc * 128u + cb * 32u, r);
             const uint32_t mrow = acc * 128u + 32u * q + lane;
             if (store && mrow < m) {
-                float4* dst = reinterpret_cast<float4*>(dst_base + (uint64_t)mrow * n_total + n0 + cb * 32u);
+                const uint64_t off = (uint64_t)mrow * n_total + n0 + cb * 32u;
+                float4* dst = reinterpret_cast<float4*>(dst_base + off);
+                const bool add_res = residual && sk.ks == 1u;  // y = residual + x W^T (split: after the sum)
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                         __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                for (int i = 0; i < 8; ++i) {
+                    float4 v = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                           __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                    if (add_res) {
+                        const float4 rr = reinterpret_cast<const float4*>(residual + off)[i];
+                        v = make_float4(rr.x + v.x, rr.y + v.y, rr.z + v.z, rr.w + v.w);
+                    }
+                    dst[i] = v;
+                }
             }
         }
         if (sk.ks > 1u) {
@@ -359,6 +468,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int i = 0; i < 8; ++i) {
                             const float4 v = __ldcg(src + i);
                             t[i].x += v.x, t[i].y += v.y, t[i].z += v.z, t[i].w += v.w;
+                        }
+                    }
+                    if (residual) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 rr = reinterpret_cast<const float4*>(residual + off)[i];
+                            t[i] = make_float4(rr.x + t[i].x, rr.y + t[i].y, rr.z + t[i].z, rr.w + t[i].w);
                         }
                     }
                     float4* dst = reinterpret_cast<float4*>(y + off);
@@ -424,20 +540,24 @@ int gemm_q4k_bf16_prepare() {
     int dev = 0;
     cudaGetDevice(&dev);
     if (done[dev & 63]) return ARC_OK;
-    const cudaError_t e =
-        cudaFuncSetAttribute(gemm_q4k_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_kq_bf16_kernel<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<14>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e != cudaSuccess) return set_cuda_error(e, "gemm prepare");
     done[dev & 63] = true;
     return ARC_OK;
 }
 
-int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,
-                  cudaStream_t stream) {
+int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
+                 const float* residual, float* y, cudaStream_t stream) {
+    if (fmt != 12 && fmt != 14) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: weights must be Q4_K or Q6_K");
     if (!w || !x || !y) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: null pointer");
     if (m == 0 || m > 256 || n == 0 || n % kBN || k == 0 || k % 256u)
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "gemm: needs 1 <= M <= 256, N % 128 == 0, K % 256 == 0");
-    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u)
-        return set_error(ARC_E_ALIGNMENT, "gemm: W, X and Y must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+         reinterpret_cast<uintptr_t>(residual)) & 15u)
+        return set_error(ARC_E_ALIGNMENT, "gemm: W, X, residual and Y must be 16-byte aligned");
     int st = gemm_q4k_bf16_prepare();
     if (st != ARC_OK) return st;
     EncodeTiledFn enc = encode_tiled_fn();
@@ -463,9 +583,17 @@ int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint
         st = gemm_splitk_reserve((size_t)ks * m * n, tiles, &sk.ws, &sk.cnt);
         if (st != ARC_OK) return st;
     }
-    const cudaError_t e = launch_kernel(gemm_q4k_bf16_kernel, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
-                                        static_cast<const uint8_t*>(w), n, k, m, y, dev_error_word(), sk);
+    const cudaError_t e =
+        fmt == 12 ? launch_kernel(gemm_kq_bf16_kernel<12>, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
+                                  static_cast<const uint8_t*>(w), n, k, m, residual, y, dev_error_word(), sk)
+                  : launch_kernel(gemm_kq_bf16_kernel<14>, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
+                                  static_cast<const uint8_t*>(w), n, k, m, residual, y, dev_error_word(), sk);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "gemm launch");
+}
+
+int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,
+                  cudaStream_t stream) {
+    return gemm_kq_bf16(12, w, n, k, x, m, nullptr, y, stream);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda

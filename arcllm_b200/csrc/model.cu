@@ -11,15 +11,22 @@
 // RoPE + fp16 KV store, split-KV GQA attention, O projection + residual,
 // RMSNorm fused into the dual gate/up matvec with silu(g)*u, down projection
 // + residual.  Then output RMSNorm fused into the LM head, argmax, finalize.
-// The prompt is consumed token by token through the same layer chain without
-// the LM head (the prefill graph).
+// The prompt (all but its last token) is consumed in batches of up to 256
+// rows on the tensor cores (enqueue_prefill_chunk: bf16 tcgen05 GEMMs for
+// every projection, batched RMSNorm / RoPE + KV store / causal attention /
+// SiLU kernels -- the reference's prefill chain, src/arcllm_v1_runtime.cpp:
+// 340-369), or, in prefill mode 0, token by token through the decode layer
+// chain without the LM head (the prefill graph, fp32 throughout).
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
 
 #include "arcllm_cuda_internal.h"
 #include "decode_ops.h"
+#include "prefill_ops.h"
 
 struct arcllm_cuda_model {
     int device = 0;
@@ -48,6 +55,16 @@ struct arcllm_cuda_model {
 
     cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
     uint32_t launches_prefill_step = 0, launches_decode_step = 0;
+
+    // batched prefill (allocated on first use): rows of up to kPrefillRows prompt tokens
+    int prefill_mode = 1;  // 1: tensor-core batches; 0: token by token
+    std::vector<const void*> prefill_down;  // Q4_K/Q6_K down weights when w_down is an EXEC148 image
+    std::vector<int> prefill_down_type;
+    void* pf_arena = nullptr;
+    float *pf_h = nullptr, *pf_h2 = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_g = nullptr,
+          *pf_u = nullptr;
+    uint16_t *pf_xb = nullptr, *pf_attn = nullptr, *pf_s = nullptr;
+    uint32_t launches_prefill_batched = 0;
 };
 
 namespace arc {
@@ -146,6 +163,96 @@ int capture(arcllm_cuda_model* m, bool with_head, cudaGraphExec_t* out, uint32_t
     return ARC_OK;
 }
 
+constexpr uint32_t kPrefillRows = 256;  // the GEMMs' M limit
+
+// Down weights of layer l for the batched prefill (the GEMM reads Q4_K/Q6_K,
+// not the EXEC148 image); null when none is available.
+const void* prefill_down_w(const arcllm_cuda_model* m, uint32_t l, int* type) {
+    const arcllm_cuda_layer& L = m->layers[l];
+    if (L.type_down != ARC_TYPE_EXEC148) {
+        *type = L.type_down;
+        return L.w_down;
+    }
+    *type = m->prefill_down_type[l];
+    return m->prefill_down[l];
+}
+
+bool prefill_batched_ok(const arcllm_cuda_model* m) {
+    if (m->prefill_mode != 1) return false;
+    if (const char* e = std::getenv("ARCLLM_PREFILL"))
+        if (std::strcmp(e, "token") == 0) return false;
+    for (uint32_t l = 0; l < m->cfg.n_layers; ++l) {
+        int t = 0;
+        if (!prefill_down_w(m, l, &t) || !quant_ok(t)) return false;
+    }
+    return true;
+}
+
+int prefill_alloc(arcllm_cuda_model* m) {
+    if (m->pf_arena) return ARC_OK;
+    const arcllm_cuda_model_config& c = m->cfg;
+    const size_t T = kPrefillRows, H = c.hidden, KV = (size_t)c.n_kv_heads * c.head_dim, F = c.ffn;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const size_t o_h = take(4 * T * H), o_h2 = take(4 * T * H), o_q = take(4 * T * H), o_k = take(4 * T * KV),
+                 o_v = take(4 * T * KV), o_g = take(4 * T * F), o_u = take(4 * T * F), o_xb = take(2 * T * H),
+                 o_attn = take(2 * T * H), o_s = take(2 * T * F);
+    const cudaError_t e = cudaMalloc(&m->pf_arena, off);
+    if (e != cudaSuccess) {
+        m->pf_arena = nullptr;
+        return set_cuda_error(e, "prefill buffers");
+    }
+    uint8_t* a = static_cast<uint8_t*>(m->pf_arena);
+    m->pf_h = reinterpret_cast<float*>(a + o_h);
+    m->pf_h2 = reinterpret_cast<float*>(a + o_h2);
+    m->pf_q = reinterpret_cast<float*>(a + o_q);
+    m->pf_k = reinterpret_cast<float*>(a + o_k);
+    m->pf_v = reinterpret_cast<float*>(a + o_v);
+    m->pf_g = reinterpret_cast<float*>(a + o_g);
+    m->pf_u = reinterpret_cast<float*>(a + o_u);
+    m->pf_xb = reinterpret_cast<uint16_t*>(a + o_xb);
+    m->pf_attn = reinterpret_cast<uint16_t*>(a + o_attn);
+    m->pf_s = reinterpret_cast<uint16_t*>(a + o_s);
+    return ARC_OK;
+}
+
+// Prompt rows pos0 .. pos0+T-1 through every layer: their K/V land in the
+// cache; the hidden states themselves are not kept (no LM head for them).
+int enqueue_prefill_chunk(arcllm_cuda_model* m, uint32_t pos0, uint32_t T, cudaStream_t st, uint32_t* n_launch) {
+    const arcllm_cuda_model_config& c = m->cfg;
+    const uint32_t H = c.hidden, KV = c.n_kv_heads * c.head_dim, F = c.ffn;
+    uint32_t n = 0;
+    ARC_TRY(launch_embed_rows(m->tok_embd_type, m->tok_embd, m->prompt + pos0, T, H, c.vocab, m->pf_h, st));
+    ++n;
+    for (uint32_t l = 0; l < c.n_layers; ++l) {
+        const arcllm_cuda_layer& L = m->layers[l];
+        int type_down = 0;
+        const void* w_down = prefill_down_w(m, l, &type_down);
+        ARC_TRY(launch_rmsnorm_rows_bf16(m->pf_h, L.attn_norm, c.rms_eps, T, H, m->pf_xb, st));
+        ARC_TRY(gemm_kq_bf16(L.type_q, L.wq, H, H, m->pf_xb, T, nullptr, m->pf_q, st));
+        ARC_TRY(gemm_kq_bf16(L.type_k, L.wk, KV, H, m->pf_xb, T, nullptr, m->pf_k, st));
+        ARC_TRY(gemm_kq_bf16(L.type_v, L.wv, KV, H, m->pf_xb, T, nullptr, m->pf_v, st));
+        RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
+        ARC_TRY(launch_rope_kv_rows(m->pf_q, m->pf_k, m->pf_v, L.bq, L.bk, L.bv, m->rope, pos0, T, m->kc, m->vc, rs,
+                                    st));
+        AttnShape as{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l, 1, 1.0f / std::sqrt((float)c.head_dim)};
+        ARC_TRY(launch_attention_prefill(m->pf_q, m->kc, m->vc, pos0, T, as, m->pf_attn, st));
+        ARC_TRY(gemm_kq_bf16(L.type_o, L.wo, H, H, m->pf_attn, T, m->pf_h, m->pf_h2, st));  // h2 = h + O
+        ARC_TRY(launch_rmsnorm_rows_bf16(m->pf_h2, L.ffn_norm, c.rms_eps, T, H, m->pf_xb, st));
+        ARC_TRY(gemm_kq_bf16(ARC_GGML_Q4_K, L.w_gate, F, H, m->pf_xb, T, nullptr, m->pf_g, st));
+        ARC_TRY(gemm_kq_bf16(ARC_GGML_Q4_K, L.w_up, F, H, m->pf_xb, T, nullptr, m->pf_u, st));
+        ARC_TRY(launch_silu_mul_rows_bf16(m->pf_g, m->pf_u, (uint64_t)T * F, m->pf_s, st));
+        ARC_TRY(gemm_kq_bf16(type_down, w_down, H, F, m->pf_s, T, m->pf_h2, m->pf_h, st));  // h = h2 + down
+        n += 12;
+    }
+    if (n_launch) *n_launch += n;
+    return ARC_OK;
+}
+
 }  // namespace
 
 // RoPE table: cos/sin of pos * theta^(-2p/d) computed with the reference's
@@ -188,6 +295,8 @@ int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
     m->cfg = c;
     m->layers.resize(c.n_layers);
     m->layer_set.assign(c.n_layers, 0);
+    m->prefill_down.assign(c.n_layers, nullptr);
+    m->prefill_down_type.assign(c.n_layers, 0);
     m->lm_row0 = 0;
     m->lm_rows = c.vocab;
     const uint32_t gq = c.n_heads / c.n_kv_heads;
@@ -332,8 +441,19 @@ int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventCreate(&e2);
+    const bool batched = n_prompt > 1 && prefill_batched_ok(m);
+    if (batched) ARC_TRY(prefill_alloc(m));
+    m->launches_prefill_batched = 0;
     cudaEventRecord(e0, st);
-    for (uint32_t i = 0; i + 1 < n_prompt; ++i) ARC_TRY(model_step(m, 0, 1, st));
+    if (batched) {
+        for (uint32_t p0 = 0; p0 + 1 < n_prompt; p0 += kPrefillRows)
+            ARC_TRY(enqueue_prefill_chunk(m, p0, std::min(kPrefillRows, n_prompt - 1u - p0), st,
+                                          &m->launches_prefill_batched));
+        ARC_TRY(launch_prefill_done(m->state, m->prompt, n_prompt, st));
+        ++m->launches_prefill_batched;
+    } else {
+        for (uint32_t i = 0; i + 1 < n_prompt; ++i) ARC_TRY(model_step(m, 0, 1, st));
+    }
     ARC_TRY(model_step(m, 1, 1, st));  // last prompt token: first generated token
     cudaEventRecord(e1, st);
     for (uint32_t i = 1; i < max_new; ++i) ARC_TRY(model_step(m, 1, 1, st));
@@ -352,8 +472,13 @@ int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n
     cudaEventDestroy(e2);
     if (e != cudaSuccess) return set_cuda_error(e, "generate: readback");
     if (stats) {
-        stats->prefill_launches = m->launches_prefill_step * (n_prompt - 1u) + m->launches_decode_step;
-        stats->prefill_graph_launches = n_prompt;
+        if (batched) {
+            stats->prefill_launches = m->launches_prefill_batched + m->launches_decode_step;
+            stats->prefill_graph_launches = 1;
+        } else {
+            stats->prefill_launches = m->launches_prefill_step * (n_prompt - 1u) + m->launches_decode_step;
+            stats->prefill_graph_launches = n_prompt;
+        }
         stats->decode_launches_per_step = m->launches_decode_step;
         stats->decode_graph_launches_per_step = 1;
         stats->decode_steps = max_new - 1u;
@@ -363,6 +488,21 @@ int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n
     }
     if (s.n_generated != max_new) return set_error(ARC_E_INVALID_ARGUMENT, "generate: generated-token count mismatch");
     if (s.nonfinite) return set_error(ARC_E_NONFINITE, "generate: non-finite logits");
+    return ARC_OK;
+}
+
+int model_set_prefill_mode(arcllm_cuda_model* m, int mode) {
+    if (!m || (mode != 0 && mode != 1)) return set_error(ARC_E_INVALID_ARGUMENT, "prefill mode: 0 or 1");
+    m->prefill_mode = mode;
+    return ARC_OK;
+}
+
+int model_set_prefill_down(arcllm_cuda_model* m, uint32_t layer, const void* w, int type) {
+    if (!m || !w) return set_error(ARC_E_INVALID_ARGUMENT, "prefill down: null pointer");
+    if (layer >= m->cfg.n_layers) return set_error(ARC_E_INVALID_ARGUMENT, "prefill down: layer out of range");
+    if (!quant_ok(type)) return set_error(ARC_E_UNSUPPORTED_SHAPE, "prefill down: Q4_K or Q6_K");
+    m->prefill_down[layer] = w;
+    m->prefill_down_type[layer] = type;
     return ARC_OK;
 }
 
@@ -384,6 +524,7 @@ int model_destroy(arcllm_cuda_model* m) {
     if (m->g_prefill) cudaGraphExecDestroy(m->g_prefill);
     if (m->g_decode) cudaGraphExecDestroy(m->g_decode);
     if (m->arena) cudaFree(m->arena);
+    if (m->pf_arena) cudaFree(m->pf_arena);
     delete m;
     return ARC_OK;
 }

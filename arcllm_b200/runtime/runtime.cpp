@@ -264,6 +264,9 @@ RunResult generate(const RunRequest& request) {
                                   int(z.ow->ggml_type), devf(z.fn), dev(z.gw), dev(z.uw), int(z.gw->ggml_type),
                                   q4_backend.exec_image(src.layer), ARC_TYPE_EXEC148};
             check(arcllm_cuda_model_set_layer(model.m, src.layer, &lay), "route B binding");
+            // the batched prefill GEMMs keep reading the GGUF Q4_K packing of this layer
+            check(arcllm_cuda_model_set_prefill_down(model.m, src.layer, dev(z.dw), int(z.dw->ggml_type)),
+                  "route B prefill binding");
         }
     }
 

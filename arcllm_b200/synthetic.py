@@ -142,6 +142,26 @@ class SyntheticModel:
         call("arcllm_cuda_model_generate", self.h, pa, n, max_new, out, C.byref(st), self.stream)
         return list(out), st
 
+    def set_prefill_mode(self, mode):
+        """1: batched tensor-core prefill (default); 0: token by token"""
+        call("arcllm_cuda_model_set_prefill_mode", self.h, int(mode))
+
+    def kv_cache(self, layer, n_pos):
+        """fp16 K and V cache rows [n_pos][kv_dim] of one layer (numpy)"""
+        import numpy as np
+        c = self.cfg
+        kv = c["n_kv_heads"] * c["head_dim"]
+        kp, vp = C.c_void_p(), C.c_void_p()
+        call("arcllm_cuda_model_kv_cache", self.h, C.byref(kp), C.byref(vp))
+        out = []
+        for p in (kp, vp):
+            a = np.empty((n_pos, kv), np.float16)
+            src = C.c_void_p(p.value + 2 * layer * c["max_ctx"] * kv)
+            call("arcllm_cuda_memcpy_d2h", a.ctypes.data_as(C.c_void_p), src, a.nbytes, self.stream)
+            out.append(a)
+        call("arcllm_cuda_stream_synchronize", self.stream)
+        return out
+
     def begin(self, prompt, max_new):
         pa = (C.c_uint32 * len(prompt))(*prompt)
         call("arcllm_cuda_model_begin", self.h, pa, len(prompt), max_new, self.stream)

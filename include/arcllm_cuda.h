@@ -139,6 +139,13 @@ ARCLLM_CUDA_API int arcllm_cuda_exec148_validate(const void *q4k, const void *ex
 ARCLLM_CUDA_API int arcllm_cuda_gemm_q4k_bf16(const void *w, uint32_t n, uint32_t k, const uint16_t *x_bf16,
                                               uint32_t m, float *y, void *stream);
 
+/* The same GEMM for Q4_K (type 12) or Q6_K (type 14) weights, with an
+ * optional fp32 residual: y = residual + x * W^T when residual is non-null
+ * (the residual adds of the prefill chain, src/arcllm_v1_runtime.cpp:343-366,
+ * fused into the epilogue).  Q6_K rows need only be 2-byte aligned. */
+ARCLLM_CUDA_API int arcllm_cuda_gemm_bf16(int type, const void *w, uint32_t n, uint32_t k, const uint16_t *x_bf16,
+                                          uint32_t m, const float *residual, float *y, void *stream);
+
 /* ---- synthetic fixture streams -------------------------------------------
  * Deterministic, counter-based generators (element n of a splitmix64
  * sequence), identical bit for bit to the CPU test oracle, so multi-GB
@@ -175,6 +182,22 @@ ARCLLM_CUDA_API int arcllm_cuda_attention_decode(const float *q, const uint16_t 
                                                  const uint32_t *pos_dev, uint32_t q_heads, uint32_t kv_heads,
                                                  uint32_t head_dim, uint32_t max_ctx, uint32_t layer,
                                                  uint32_t n_splits, float *scratch, float *out, void *stream);
+/* Batched prefill forms (the model's prefill chain; also for tests): rows t =
+ * 0..rows-1 of q [rows][q_heads*head_dim], k and v [rows][kv_heads*head_dim]
+ * get their biases (nullable) added, q and k the RoPE rotation of position
+ * pos0+t (in place), and k, v are stored as fp16 at that position of `layer`;
+ * then causal attention of query row t over cache positions 0..pos0+t, the
+ * result written as bf16 [rows][q_heads*head_dim] (the O-projection GEMM's
+ * operand).  head_dim must be 128; pos0+rows <= max_ctx. */
+ARCLLM_CUDA_API int arcllm_cuda_rope_kv_rows(float *q, float *k, const float *v, const float *bq, const float *bk,
+                                             const float *bv, const float *table, uint32_t pos0, uint32_t rows,
+                                             uint16_t *k_cache, uint16_t *v_cache, uint32_t q_heads,
+                                             uint32_t kv_heads, uint32_t head_dim, uint32_t max_ctx, uint32_t layer,
+                                             void *stream);
+ARCLLM_CUDA_API int arcllm_cuda_attention_prefill(const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                                  uint32_t pos0, uint32_t rows, uint32_t q_heads, uint32_t kv_heads,
+                                                  uint32_t head_dim, uint32_t max_ctx, uint32_t layer,
+                                                  uint16_t *out_bf16, void *stream);
 /* Same computation as arcllm_cuda_attention_decode, for callers that cannot
  * allocate device memory when they run a step (a host that fixes its device
  * memory plan in advance, a latency-critical loop that must not risk the
@@ -257,9 +280,13 @@ ARCLLM_CUDA_API int arcllm_cuda_model_set_layer(arcllm_cuda_model *m, uint32_t l
 /* tok_embd_type: F16 (1, [vocab][hidden] halves) or Q4_K (12); output_type Q4_K/Q6_K */
 ARCLLM_CUDA_API int arcllm_cuda_model_set_endpoints(arcllm_cuda_model *m, const void *tok_embd, int tok_embd_type,
                                                     const float *output_norm, const void *output, int output_type);
-/* Greedy generation: consumes the prompt (one step per token), then produces
- * max_new tokens into out_tokens_host.  Synchronous on `stream`.  Fails with
- * ARC_E_NONFINITE on non-finite logits (runtime.cpp:446,501). */
+/* Greedy generation: consumes the prompt, then produces max_new tokens into
+ * out_tokens_host.  Synchronous on `stream`.  Fails with ARC_E_NONFINITE on
+ * non-finite logits (runtime.cpp:446,501).  In prefill mode 1 (the default)
+ * all prompt tokens but the last go through the layers in batches of up to
+ * 256 rows on the tcgen05 GEMMs (bf16 operands, fp32 accumulation; the
+ * reference's prefill chain, runtime.cpp:340-369); in mode 0 (or with the
+ * environment variable ARCLLM_PREFILL=token) one fp32 step per token. */
 ARCLLM_CUDA_API int arcllm_cuda_model_generate(arcllm_cuda_model *m, const uint32_t *prompt_host, uint32_t n_prompt,
                                                uint32_t max_new, uint32_t *out_tokens_host,
                                                arcllm_cuda_gen_stats *stats, void *stream);
@@ -269,6 +296,13 @@ ARCLLM_CUDA_API int arcllm_cuda_model_generate(arcllm_cuda_model *m, const uint3
 ARCLLM_CUDA_API int arcllm_cuda_model_begin(arcllm_cuda_model *m, const uint32_t *prompt_host, uint32_t n_prompt,
                                             uint32_t max_new, void *stream);
 ARCLLM_CUDA_API int arcllm_cuda_model_step(arcllm_cuda_model *m, int with_head, int use_graph, void *stream);
+/* Prefill mode: 1 = batched on the tensor cores (default), 0 = token by token. */
+ARCLLM_CUDA_API int arcllm_cuda_model_set_prefill_mode(arcllm_cuda_model *m, int mode);
+/* Q4_K/Q6_K down weights of `layer` for the batched prefill, needed when the
+ * layer's decode down projection is bound to an EXEC148 image (type 148):
+ * the prefill GEMMs read the GGUF packing.  Without it such a model prefills
+ * token by token. */
+ARCLLM_CUDA_API int arcllm_cuda_model_set_prefill_down(arcllm_cuda_model *m, uint32_t layer, const void *w, int type);
 /* Device pointers to the last logits [vocab] and to the K / V caches. */
 ARCLLM_CUDA_API int arcllm_cuda_model_logits(arcllm_cuda_model *m, const float **out);
 ARCLLM_CUDA_API int arcllm_cuda_model_kv_cache(arcllm_cuda_model *m, const uint16_t **k, const uint16_t **v);

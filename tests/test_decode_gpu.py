@@ -156,6 +156,7 @@ def test_decode_small_q4_everywhere():
 def test_generate_matches_stepwise_and_reports_stats():
     from arcllm_b200.synthetic import SyntheticModel
     m = SyntheticModel(SMALL, seed=0x5EED + 2)
+    m.set_prefill_mode(0)  # token by token: the same fp32 chain as the eager steps below
     prompt = [int(t) for t in O.tokens(8, 0x77, SMALL["vocab"])]
     toks, st = m.generate(prompt, 8)
     toks2, st2 = m.generate(prompt, 8)  # request-scoped: a second request repeats exactly

@@ -1,5 +1,6 @@
-"""Prefill GEMM on tcgen05 (arcllm_cuda_gemm_q4k_bf16): y = x * W^T with x bf16
-[m x k], W Q4_K [n x k], fp32 accumulation.  Checked tightly against the same
+"""Prefill GEMM on tcgen05 (arcllm_cuda_gemm_q4k_bf16 / arcllm_cuda_gemm_bf16):
+y = (residual +) x * W^T with x bf16 [m x k], W Q4_K or Q6_K [n x k], fp32
+accumulation.  Checked tightly against the same
 product with W dequantised the way the kernel does it (bf16 scale and offset
 per sub-block, one bf16 rounding of q*f - o), and at the stated 1e-2 rel-L2
 against the CPU oracle's bit-exact fp32 dequantisation."""
@@ -44,6 +45,57 @@ def q4k_bf16_weights(w_host, n, k):
     q = np.where((kk & 63) < 32, byte & 15, byte >> 4).astype(np.float64)
     w = q * f[:, kk >> 5] - o[:, kk >> 5]
     return bf16_round(w.astype(np.float32)).reshape(n, k)
+
+
+def q6k_bf16_weights(w_host, n, k):
+    """The kernel's bf16 Q6_K weights: f = bf16(d*sc) per 16-element group,
+    w = bf16((c - 32) * f) with one rounding."""
+    nb = k // 256
+    blk = w_host.reshape(n * nb, 210)
+    d = blk[:, 208:210].copy().view(np.float16).astype(np.float32)[:, 0]
+    sc = blk[:, 192:208].astype(np.int8).astype(np.float32)
+    f = bf16_round((d[:, None] * sc).astype(np.float32)).astype(np.float64)
+    kk = np.arange(256)
+    h, q, l = kk >> 7, (kk & 127) >> 5, kk & 31
+    low = (blk[:, 64 * h + 32 * (q & 1) + l].astype(np.int32) >> (4 * (q >> 1))) & 15
+    high = (blk[:, 128 + 32 * h + l].astype(np.int32) >> (2 * q)) & 3
+    c = (low | (high << 4)).astype(np.float64) - 32.0
+    w = c * f[:, 8 * h + 2 * q + (l >> 4)]
+    return bf16_round(w.astype(np.float32)).reshape(n, k)
+
+
+def run_gemm_t(fmt, m, n, k, seed, residual=False):
+    w_host = O.fill_weights(fmt, n, k, seed)
+    w = G.to_dev(w_host)
+    x32 = O.normal_f32(m * k, seed + 1).reshape(m, k)
+    xb = torch.from_numpy(x32).to(torch.bfloat16).to(G.dev())
+    r = torch.from_numpy(O.normal_f32(m * n, seed + 2).reshape(m, n)).to(G.dev()) if residual else None
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device=G.dev())
+    A.call("arcllm_cuda_gemm_bf16", 12 if fmt == "q4k" else 14, G.ptr(w), n, k, C.c_void_p(xb.data_ptr()), m,
+           C.c_void_p(r.data_ptr()) if residual else None, C.c_void_p(y.data_ptr()), G.stream())
+    torch.cuda.synchronize()
+    G.check_device_error()
+    wd = O.dequant(fmt, w_host, n, k).reshape(n, k)
+    wb = q4k_bf16_weights(w_host, n, k) if fmt == "q4k" else q6k_bf16_weights(w_host, n, k)
+    xf = xb.float().cpu().numpy().astype(np.float64)
+    rr = r.cpu().numpy().astype(np.float64) if residual else 0.0
+    return y.cpu().numpy().astype(np.float64), xf, wd, wb, rr
+
+
+@pytest.mark.parametrize("fmt,m,n,k,res", [("q6k", 256, 128, 256, False), ("q6k", 255, 512, 3584, True),
+                                           ("q6k", 100, 384, 1024, False), ("q6k", 256, 3584, 18944, True),
+                                           ("q6k", 1, 128, 512, True), ("q4k", 255, 3584, 3584, True),
+                                           ("q4k", 64, 3584, 18944, True)])
+def test_gemm_bf16_formats_and_residual(fmt, m, n, k, res):
+    y, xf, wd, wb, rr = run_gemm_t(fmt, m, n, k, 1300 + m + n + k, res)
+    assert np.isfinite(y).all()
+    y_b = rr + xf @ wb.astype(np.float64).T
+    y_f = rr + xf @ wd.astype(np.float64).T
+    rel_b = np.linalg.norm(y - y_b) / np.linalg.norm(y_b)
+    rel_f = np.linalg.norm(y - y_f) / np.linalg.norm(y_f)
+    print("gemm %s %dx%dx%d res=%d: rel-L2 %.2e (kernel's bf16 W), %.2e (fp32 W)" % (fmt, m, n, k, res, rel_b, rel_f))
+    assert rel_b <= 1e-5
+    assert rel_f <= 1e-2
 
 
 def run_gemm(m, n, k, seed):

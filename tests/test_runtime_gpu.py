@@ -2,7 +2,10 @@
 reference-compatible CLI (src/arcllm_v1_runtime_cli.cpp interface): a
 synthetic Qwen2 GGUF is read, checked, uploaded and decoded greedily; the
 tokens must equal the CPU oracle's greedy decode of the same weights and the
-device-filled SyntheticModel's."""
+device-filled SyntheticModel's.  Exact token comparisons run the prompt token
+by token (ARCLLM_PREFILL=token: the fp32 decode chain); the default batched
+tensor-core prefill (bf16 GEMMs) is checked numerically in test_prefill_gpu.py
+and for its bookkeeping here."""
 import json
 import os
 import subprocess
@@ -23,10 +26,11 @@ SMALL = dict(n_layers=2, hidden=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn=
              rms_eps=1e-6, rope_theta=1.0e6)
 
 
-def run_cli(path, prompt, max_new, profile=0, scope=0):
+def run_cli(path, prompt, max_new, profile=0, scope=0, prefill="token"):
+    env = dict(os.environ, ARCLLM_PREFILL=prefill)
     r = subprocess.run([CLI, "--model", path, "--shader-dir", "unused", "--tokens", ",".join(map(str, prompt)),
                         "--max-new", str(max_new), "--profile", str(profile), "--within-validated-domain",
-                        str(scope)], capture_output=True, text=True, timeout=600)
+                        str(scope)], capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stderr
     return json.loads(r.stdout)
 
@@ -62,6 +66,7 @@ def test_generate_cli_matches_oracle(tmp_path, emb):
     # the same weights filled on the device through the C ABI decode to the same tokens
     from arcllm_b200.synthetic import SyntheticModel
     m = SyntheticModel(SMALL, types=types, seed=seed)
+    m.set_prefill_mode(0)
     dev_toks, _ = m.generate(prompt, 6)
     m.close()
     assert toks == dev_toks
@@ -105,3 +110,24 @@ def test_generate_route_b_inside_validated_domain(tmp_path):
     # profile 1 needs 4 tokens of reuse: 3 new tokens (reuse 2 at the first decode step) stay on A
     c = run_cli(path, prompt, 3, profile=1, scope=1)
     assert c["stats"]["route_a_steps"] == 2 and c["stats"]["route_b_steps"] == 0 and c["stats"]["acquire_events"] == 0
+
+
+def test_generate_cli_batched_prefill(tmp_path):
+    """Default prefill: all prompt tokens but the last in one batch through the
+    tensor-core GEMMs (1 embedding + 12 launches per layer + the state hand-off),
+    then the decode graph; also under route B, where the prefill GEMMs read the
+    Q4_K down weights while decode reads the EXEC148 image."""
+    types = dict(w_down=GGML_Q4_K)
+    path = str(tmp_path / "m.gguf")
+    write_synthetic_gguf(path, SMALL, types=types, seed=0x5EED + 10)
+    prompt = [int(t) for t in O.tokens(40, 0x7A, SMALL["vocab"])]
+    t = run_cli(path, prompt, 6, prefill="token")
+    for scope in (0, 1):
+        b = run_cli(path, prompt, 6, scope=scope, prefill="gemm")
+        s = b["stats"]
+        assert s["finite"] is True and s["decode_steps"] == 5
+        assert s["prefill_submits"] == 1
+        assert s["prefill_dispatches"] == 1 + 12 * SMALL["n_layers"] + 1 + s["decode_dispatches_per_step"]
+        assert s["route_b_steps"] == (5 if scope else 0)
+        # bf16 prefill vs the fp32 token path: the first generated token agrees on this model
+        assert b["generated_token_ids"][0] == t["generated_token_ids"][0]
