@@ -453,33 +453,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar_sync(1, kDqWarps * 32u);
             if (tail->last_split) {
                 __threadfence();
+                // all 256 threads add the tile's split partials, coalesced float4 by float4
+                // (four positions per thread at a time, every split's loads in flight together),
+                // in split order (deterministic)
+                if (store) {
+                    const uint32_t nf4 = m * (kBN / 4u), n4 = n_total / 4u;
 #pragma unroll 1
-                for (uint32_t pair = sub; pair < kPairs; pair += kPerQuarter) {
-                    const uint32_t acc = pair / (kBN / 32u), cb = pair % (kBN / 32u);
-                    const uint32_t mrow = acc * 128u + 32u * q + lane;
-                    if (!(store && mrow < m)) continue;
-                    const uint64_t off = (uint64_t)mrow * n_total + n0 + cb * 32u;
-                    float4 t[8];
+                    for (uint32_t p0 = dt; p0 < nf4; p0 += 4u * 256u) {
+                        float4 t[4];
+                        uint64_t off4[4];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) t[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (uint32_t sp = 0; sp < sk.ks; ++sp) {
-                        const float4* src = reinterpret_cast<const float4*>(sk.ws + (uint64_t)sp * m * n_total + off);
+                        for (int u = 0; u < 4; ++u) {
+                            const uint32_t pp = min(p0 + 256u * u, nf4 - 1u);  // clamped: duplicates are not stored
+                            off4[u] = (uint64_t)(pp >> 5) * n4 + n0 / 4u + (pp & 31u);
+                            t[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll 4
+                        for (uint32_t sp = 0; sp < sk.ks; ++sp) {
+                            const float4* src = reinterpret_cast<const float4*>(sk.ws + (uint64_t)sp * m * n_total);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const float4 v = __ldcg(src + i);
-                            t[i].x += v.x, t[i].y += v.y, t[i].z += v.z, t[i].w += v.w;
+                            for (int u = 0; u < 4; ++u) {
+                                const float4 v = __ldcg(src + off4[u]);
+                                t[u].x += v.x, t[u].y += v.y, t[u].z += v.z, t[u].w += v.w;
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            if (p0 + 256u * u >= nf4) break;
+                            if (residual) {
+                                const float4 rr = reinterpret_cast<const float4*>(residual)[off4[u]];
+                                t[u] = make_float4(rr.x + t[u].x, rr.y + t[u].y, rr.z + t[u].z, rr.w + t[u].w);
+                            }
+                            reinterpret_cast<float4*>(y)[off4[u]] = t[u];
                         }
                     }
-                    if (residual) {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const float4 rr = reinterpret_cast<const float4*>(residual + off)[i];
-                            t[i] = make_float4(rr.x + t[i].x, rr.y + t[i].y, rr.z + t[i].z, rr.w + t[i].w);
-                        }
-                    }
-                    float4* dst = reinterpret_cast<float4*>(y + off);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) dst[i] = t[i];
                 }
                 if (dt == 0) atomicExch(&sk.cnt[blockIdx.x], 0u);
             }
