@@ -206,24 +206,44 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     }
 }
 
+// Merge the slices of one q head: an online merge over chunks of 8 slices
+// whose (max, sum, acc) loads are all issued before any is used.
 __global__ void attn_merge_kernel(const float* __restrict__ part, const uint32_t* __restrict__ pos_src, AttnShape s,
                                   uint32_t gq, float* __restrict__ out) {
     pdl_trigger();
     pdl_wait();  // inputs come from the preceding kernels
-    constexpr int D = 128;
+    constexpr int D = 128, CH = 8;
     const uint32_t qh = blockIdx.x, d = threadIdx.x;
     const uint32_t kvh = qh / gq, g = qh - kvh * gq;
     const uint32_t n = min(*pos_src, s.max_ctx - 1u) + 1u;
     const uint32_t chunk = (n + s.n_splits - 1u) / s.n_splits;
     const uint32_t used = (n + chunk - 1u) / chunk;
-    float M = -FLT_MAX;
-    for (uint32_t sp = 0; sp < used; ++sp) M = fmaxf(M, part[(((uint64_t)kvh * s.n_splits + sp) * gq + g) * (D + 2u)]);
-    float L = 0.f, A = 0.f;
-    for (uint32_t sp = 0; sp < used; ++sp) {
-        const float* pp = part + (((uint64_t)kvh * s.n_splits + sp) * gq + g) * (D + 2u);
-        const float f = __expf(pp[0] - M);
-        L = fmaf(pp[1], f, L);
-        A = fmaf(pp[2 + d], f, A);
+    float M = -FLT_MAX, L = 0.f, A = 0.f;
+    for (uint32_t sp0 = 0; sp0 < used; sp0 += CH) {
+        float mm[CH], ll[CH], aa[CH];
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+            const uint32_t sp = sp0 + j;
+            if (sp < used) {
+                const float* pp = part + (((uint64_t)kvh * s.n_splits + sp) * gq + g) * (D + 2u);
+                mm[j] = pp[0], ll[j] = pp[1], aa[j] = pp[2 + d];
+            } else {
+                mm[j] = -FLT_MAX, ll[j] = 0.f, aa[j] = 0.f;
+            }
+        }
+        float cm = M;
+#pragma unroll
+        for (int j = 0; j < CH; ++j) cm = fmaxf(cm, mm[j]);
+        const float r = __expf(M - cm);
+        L *= r;
+        A *= r;
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+            const float f = __expf(mm[j] - cm);
+            L = fmaf(ll[j], f, L);
+            A = fmaf(aa[j], f, A);
+        }
+        M = cm;
     }
     out[qh * D + d] = A / L;
 }

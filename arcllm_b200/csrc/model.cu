@@ -55,6 +55,9 @@ struct arcllm_cuda_model {
 
     cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
     uint32_t launches_prefill_step = 0, launches_decode_step = 0;
+    // K and V projections run beside Q on two side streams (forked and joined with events)
+    cudaStream_t side[2] = {nullptr, nullptr};
+    cudaEvent_t ev_fork = nullptr, ev_join[2] = {nullptr, nullptr};
 
     // batched prefill (allocated on first use): rows of up to kPrefillRows prompt tokens
     int prefill_mode = 1;  // 1: tensor-core batches; 0: token by token
@@ -109,9 +112,20 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
     float* hm = m->h1;
     for (uint32_t l = 0; l < c.n_layers; ++l) {
         const arcllm_cuda_layer& L = m->layers[l];
+        // Q, K and V read the same input: K and V go to side streams so the three
+        // matvecs (112 + 16 + 16 CTAs at the Qwen2.5-7B shape) share the GPU
+        ARC_TRY(launch_checked(cudaEventRecord(m->ev_fork, st), "fork"));
+        for (int i = 0; i < 2; ++i) ARC_TRY(launch_checked(cudaStreamWaitEvent(m->side[i], m->ev_fork, 0), "fork"));
         ARC_TRY(mv(L.type_q, L.wq, H, H, hc, L.attn_norm, c.rms_eps, L.bq, nullptr, m->q, st));
-        ARC_TRY(mv(L.type_k, L.wk, KV, H, hc, L.attn_norm, c.rms_eps, L.bk, nullptr, m->k, st));
-        ARC_TRY(mv(L.type_v, L.wv, KV, H, hc, L.attn_norm, c.rms_eps, L.bv, nullptr, m->v, st));
+        {
+            PdlScope plain(false);  // a side stream's predecessor is an event, not a kernel
+            ARC_TRY(mv(L.type_k, L.wk, KV, H, hc, L.attn_norm, c.rms_eps, L.bk, nullptr, m->k, m->side[0]));
+            ARC_TRY(mv(L.type_v, L.wv, KV, H, hc, L.attn_norm, c.rms_eps, L.bv, nullptr, m->v, m->side[1]));
+        }
+        for (int i = 0; i < 2; ++i) {
+            ARC_TRY(launch_checked(cudaEventRecord(m->ev_join[i], m->side[i]), "join"));
+            ARC_TRY(launch_checked(cudaStreamWaitEvent(st, m->ev_join[i], 0), "join"));
+        }
         RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
         ARC_TRY(launch_rope_kv_store(m->q, m->k, m->v, m->rope, &m->state->pos, m->kc, m->vc, rs, st));
         AttnShape as{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l, m->attn_splits,
@@ -344,6 +358,13 @@ int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
         delete m;
         return set_cuda_error(e, "model_create: init");
     }
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaStreamCreateWithFlags(&m->side[i], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming);
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&m->ev_join[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        model_destroy(m);
+        return set_cuda_error(e, "model_create: streams");
+    }
     *out = m;
     return ARC_OK;
 }
@@ -525,6 +546,11 @@ int model_destroy(arcllm_cuda_model* m) {
     if (m->g_decode) cudaGraphExecDestroy(m->g_decode);
     if (m->arena) cudaFree(m->arena);
     if (m->pf_arena) cudaFree(m->pf_arena);
+    for (int i = 0; i < 2; ++i) {
+        if (m->side[i]) cudaStreamDestroy(m->side[i]);
+        if (m->ev_join[i]) cudaEventDestroy(m->ev_join[i]);
+    }
+    if (m->ev_fork) cudaEventDestroy(m->ev_fork);
     delete m;
     return ARC_OK;
 }
