@@ -71,9 +71,17 @@ int matvec_plan(int fmt, bool dual, uint32_t rows, uint32_t k, MatvecPlan* out);
 // Integer tensor-core variant (matvec_imma.cu), K/256 <= 14 (even for Q6_K).
 int matvec_imma_prepare();
 bool matvec_imma_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
+// Fused RoPE / KV-store epilogue of the whole-row kernel (mode 1: rotate rows in pairs at
+// position *pos and write y; 2: also store fp16 to cache row *pos; 3: store fp16 unrotated).
+struct RopeEpilogue {
+    uint32_t mode, half, max_ctx;
+    const float2* table;
+    const uint32_t* pos;
+    uint16_t* cache;  // this layer's cache: row p at p * rows
+};
 int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                        const float* gamma, float eps, const float* bias, const float* residual, float* y,
-                       cudaStream_t stream);
+                       cudaStream_t stream, const RopeEpilogue* rope = nullptr);
 // Integer tensor-core K-slice variant (matvec_imma_splitk.cu) for K > 3584.
 // It adds CTA partials through a per-device scratch: launches of it on one
 // device must not overlap in time (one stream, or ordered streams).

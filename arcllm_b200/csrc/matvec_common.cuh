@@ -30,6 +30,14 @@ struct MvParams {
     uint32_t stage_smem;  // bytes of one stage in smem (both matrices + pad)
     uint32_t x_floats;    // padded x length in smem
     uint32_t early;       // 1: weights may be streamed before the PDL wait (they are not written upstream)
+    // fused RoPE / KV-store epilogue (whole-row integer-MMA kernel only; rope_mode 0 = none):
+    // 1 rotate adjacent row pairs (2p, 2p+1) of each head_dim-row head at position *pos -> y;
+    // 2 rotate, then store fp16 into cache row *pos; 3 store fp16 into cache row *pos
+    uint32_t rope_mode, rope_half;  // rope_half = head_dim / 2
+    const float2* rope_table;       // [max_ctx][head_dim/2] (cos, sin)
+    const uint32_t* rope_pos;       // device position
+    uint16_t* cache;                // cache base + layer offset; row `pos` starts at pos * rows
+    uint32_t max_ctx;
 };
 
 // Fold N per-row partial sums over the warp: afterwards lane L holds the full

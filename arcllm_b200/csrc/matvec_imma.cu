@@ -106,7 +106,7 @@ __device__ __forceinline__ void finish_rows(const MvParams& p, const float* red,
     const uint32_t grp = blockIdx.x + itr * gridDim.x;
     const uint32_t rows_g = min(p.G, p.rows - grp * p.G);
     const float* rs = red + (par * S + s) * nwc * NV;
-    for (uint32_t r = lane; r < rows_g; r += 32u) {
+    for (uint32_t r = lane; (DUAL || p.rope_mode == 0) && r < rows_g; r += 32u) {
         const uint32_t row = grp * p.G + r;
         float a = 0.f;
         for (uint32_t w = 0; w < nwc; ++w) a += rs[w * NV + r];
@@ -115,10 +115,36 @@ __device__ __forceinline__ void finish_rows(const MvParams& p, const float* red,
             for (uint32_t w = 0; w < nwc; ++w) u += rs[w * NV + G + r];
             // src/p8c_segmented_access_correctness.cpp:1064-1073 (silu(g)*u)
             p.y[row] = (a / (1.0f + expf(-a))) * u;
-        } else {
+        } else if (p.rope_mode == 0) {
             if (p.bias) a += p.bias[row];
             if (p.residual) a = p.residual[row] + a;
             p.y[row] = a;
+        }
+    }
+    if (!DUAL && p.rope_mode != 0) {
+        // fused RoPE / fp16 KV store: one row per lane (G <= 32), rotation pairs (2p, 2p+1) in
+        // neighbouring lanes; the same operations as the standalone rope_kv_store kernel
+        const uint32_t row = grp * p.G + lane;
+        const bool act = lane < rows_g;
+        float a = 0.f;
+        if (act) {
+            for (uint32_t w = 0; w < nwc; ++w) a += rs[w * NV + lane];
+            if (p.bias) a += p.bias[row];
+        }
+        const uint32_t pos = *p.rope_pos;
+        const bool pos_ok = pos < p.max_ctx;
+        if (!pos_ok && lane == 0) raise_error(p.err, ARC_DEV_ERR_BOUNDS);
+        float v = a;
+        if (p.rope_mode <= 2u) {
+            const float b = __shfl_xor_sync(0xffffffffu, a, 1);
+            const float2 cs = pos_ok ? p.rope_table[(uint64_t)pos * p.rope_half + (row >> 1) % p.rope_half]
+                                     : make_float2(1.f, 0.f);
+            v = (row & 1u) ? __fadd_rn(__fmul_rn(b, cs.y), __fmul_rn(a, cs.x))
+                           : __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+        }
+        if (act) {
+            p.y[row] = v;
+            if (p.rope_mode >= 2u && pos_ok) p.cache[(uint64_t)pos * p.rows + row] = __half_as_ushort(__float2half_rn(v));
         }
     }
 }
@@ -175,9 +201,11 @@ __device__ __forceinline__ void produce_and_finish(const MvParams& p, uint8_t* s
                 if (DUAL) bulk_g2s(dst + mat_off + o, p.w1 + goff + o, n, &full[s], pol);
             }
         }
+        if (it == S && p.early) pdl_wait();  // the epilogue reads predecessors' outputs (bias, residual, position)
         if (it >= S) finish_rows<G, DUAL>(p, red, nwc, it - S, lane);
     }
     if (ok) {
+        if (it <= S && p.early) pdl_wait();
         for (uint32_t j = it > S ? it - S : 0; j < it; ++j) {
             if (!released(j)) {
                 ok = false;
@@ -363,7 +391,7 @@ bool matvec_imma_supported(int fmt, bool dual, uint32_t rows, uint32_t k) {
 
 int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                        const float* gamma, float eps, const float* bias, const float* residual, float* y,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const RopeEpilogue* rope) {
     if (!matvec_imma_supported(fmt, dual, rows, k))
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec_imma: shape outside K/256 <= 14 (even for Q6_K)");
     if (!w0 || !x || !y || (dual && !w1)) return set_error(ARC_E_INVALID_ARGUMENT, "matvec: null pointer");
@@ -393,6 +421,17 @@ int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint3
     p.stage_smem = c.stage_smem;
     p.x_floats = 0;
     p.early = pdl_enabled() ? 1u : 0u;
+    if (rope && rope->mode != 0) {
+        if (dual || residual || rope->mode > 3u || rope->half == 0 || (rows % (2u * rope->half)) != 0u || !rope->pos ||
+            (rope->mode <= 2u && !rope->table) || (rope->mode >= 2u && !rope->cache))
+            return set_error(ARC_E_INVALID_ARGUMENT, "matvec_imma: bad fused RoPE epilogue");
+        p.rope_mode = rope->mode;
+        p.rope_half = rope->half;
+        p.rope_table = rope->table;
+        p.rope_pos = rope->pos;
+        p.cache = rope->cache;
+        p.max_ctx = rope->max_ctx;
+    }
     static int sm_count[64] = {};  // per device, queried once
     int dev = 0;
     cudaGetDevice(&dev);

@@ -101,6 +101,19 @@ int mv(int type, const void* w, uint32_t rows, uint32_t k, const float* x, const
         if (_st != ARC_OK) return _st; \
     } while (0)
 
+// RoPE + KV store can ride in the Q/K/V matvec epilogues: all three on the
+// whole-row integer-MMA kernel (K <= 3584, 16-byte aligned x and gamma).
+bool fuse_rope_ok(const arcllm_cuda_model* m, const arcllm_cuda_layer& L) {
+    if (const char* e = std::getenv("ARCLLM_FUSE_ROPE"))
+        if (std::strcmp(e, "0") == 0) return false;
+    if (std::getenv("ARCLLM_MATVEC_IMPL") && std::strcmp(std::getenv("ARCLLM_MATVEC_IMPL"), "cuda") == 0) return false;
+    const arcllm_cuda_model_config& c = m->cfg;
+    const uint32_t H = c.hidden, KV = c.n_kv_heads * c.head_dim;
+    if ((reinterpret_cast<uintptr_t>(L.attn_norm) & 15u) != 0u) return false;
+    return matvec_imma_supported(L.type_q, false, H, H) && matvec_imma_supported(L.type_k, false, KV, H) &&
+           matvec_imma_supported(L.type_v, false, KV, H);
+}
+
 // Enqueue one token step; `with_head` adds output norm + LM head + argmax.
 int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t* n_launch) {
     const arcllm_cuda_model_config& c = m->cfg;
@@ -116,18 +129,40 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
         // matvecs (112 + 16 + 16 CTAs at the Qwen2.5-7B shape) share the GPU
         ARC_TRY(launch_checked(cudaEventRecord(m->ev_fork, st), "fork"));
         for (int i = 0; i < 2; ++i) ARC_TRY(launch_checked(cudaStreamWaitEvent(m->side[i], m->ev_fork, 0), "fork"));
-        ARC_TRY(mv(L.type_q, L.wq, H, H, hc, L.attn_norm, c.rms_eps, L.bq, nullptr, m->q, st));
+        // RoPE and the fp16 KV store ride in the Q/K/V matvec epilogues when the whole-row
+        // integer-MMA kernel takes all three (ARCLLM_FUSE_ROPE=0 keeps the separate kernel)
+        const bool fuse = fuse_rope_ok(m, L);
+        const uint64_t lcache = (uint64_t)l * c.max_ctx * KV;
+        const uint32_t half = c.head_dim / 2u;
+        const RopeEpilogue rq{1u, half, c.max_ctx, m->rope, &m->state->pos, nullptr};
+        const RopeEpilogue rk{2u, half, c.max_ctx, m->rope, &m->state->pos, m->kc + lcache};
+        const RopeEpilogue rv{3u, half, c.max_ctx, m->rope, &m->state->pos, m->vc + lcache};
+        if (fuse)
+            ARC_TRY(matvec_imma_launch(L.type_q, false, L.wq, nullptr, H, H, hc, L.attn_norm, c.rms_eps, L.bq, nullptr,
+                                       m->q, st, &rq));
+        else
+            ARC_TRY(mv(L.type_q, L.wq, H, H, hc, L.attn_norm, c.rms_eps, L.bq, nullptr, m->q, st));
         {
             PdlScope plain(false);  // a side stream's predecessor is an event, not a kernel
-            ARC_TRY(mv(L.type_k, L.wk, KV, H, hc, L.attn_norm, c.rms_eps, L.bk, nullptr, m->k, m->side[0]));
-            ARC_TRY(mv(L.type_v, L.wv, KV, H, hc, L.attn_norm, c.rms_eps, L.bv, nullptr, m->v, m->side[1]));
+            if (fuse) {
+                ARC_TRY(matvec_imma_launch(L.type_k, false, L.wk, nullptr, KV, H, hc, L.attn_norm, c.rms_eps, L.bk,
+                                           nullptr, m->k, m->side[0], &rk));
+                ARC_TRY(matvec_imma_launch(L.type_v, false, L.wv, nullptr, KV, H, hc, L.attn_norm, c.rms_eps, L.bv,
+                                           nullptr, m->v, m->side[1], &rv));
+            } else {
+                ARC_TRY(mv(L.type_k, L.wk, KV, H, hc, L.attn_norm, c.rms_eps, L.bk, nullptr, m->k, m->side[0]));
+                ARC_TRY(mv(L.type_v, L.wv, KV, H, hc, L.attn_norm, c.rms_eps, L.bv, nullptr, m->v, m->side[1]));
+            }
         }
         for (int i = 0; i < 2; ++i) {
             ARC_TRY(launch_checked(cudaEventRecord(m->ev_join[i], m->side[i]), "join"));
             ARC_TRY(launch_checked(cudaStreamWaitEvent(st, m->ev_join[i], 0), "join"));
         }
-        RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
-        ARC_TRY(launch_rope_kv_store(m->q, m->k, m->v, m->rope, &m->state->pos, m->kc, m->vc, rs, st));
+        if (!fuse) {
+            RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
+            ARC_TRY(launch_rope_kv_store(m->q, m->k, m->v, m->rope, &m->state->pos, m->kc, m->vc, rs, st));
+            ++n;
+        }
         AttnShape as{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l, m->attn_splits,
                      1.0f / std::sqrt((float)c.head_dim)};
         ARC_TRY(launch_attention(m->q, m->kc, m->vc, &m->state->pos, as, m->part, m->attn, st));
@@ -135,7 +170,7 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
         ARC_TRY(matvec_any(ARC_GGML_Q4_K, true, L.w_gate, L.w_up, c.ffn, H, hm, L.ffn_norm, c.rms_eps, nullptr,
                            nullptr, m->s, st));
         ARC_TRY(mv(L.type_down, L.w_down, H, c.ffn, m->s, nullptr, 0.f, nullptr, hm, hc, st));
-        n += 9;
+        n += 8;
     }
     if (with_head) {
         ARC_TRY(mv(m->out_type, m->out_w, m->lm_rows, H, hc, m->out_norm, c.rms_eps, nullptr, nullptr,

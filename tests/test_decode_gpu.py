@@ -169,7 +169,7 @@ def test_generate_matches_stepwise_and_reports_stats():
             ref.append(O.argmax(m.logits())[0])
     assert toks == ref
     assert st.finite == 1 and st.decode_steps == 7 and st.prefill_graph_launches == 8
-    assert st.decode_launches_per_step == 1 + 9 * SMALL["n_layers"] + 3
+    assert st.decode_launches_per_step == 1 + 8 * SMALL["n_layers"] + 3  # RoPE + KV store fused into Q/K/V
     assert st.decode_graph_launches_per_step == 1
     m.close()
 
@@ -184,3 +184,27 @@ def test_decode_qwen7b_shape_parity():
     rels, rate, _ = run_parity(cfg, prompt, 3, threads=max(8, os.cpu_count() or 8))
     print("7B-shape: max rel-L2 %.2e, token match %.2f" % (max(rels), rate))
     assert max(rels) <= 1e-2 and rate == 1.0
+
+
+def test_fused_rope_kv_epilogue_bit_identical(monkeypatch):
+    """RoPE and the fp16 KV store in the Q/K/V matvec epilogues give the same
+    cache and logits, bit for bit, as the separate rope_kv_store kernel."""
+    from arcllm_b200.synthetic import SyntheticModel
+    prompt = [int(t) for t in O.tokens(9, 0x7E, SMALL["vocab"])]
+    out = {}
+    for fused in ("1", "0"):
+        monkeypatch.setenv("ARCLLM_FUSE_ROPE", fused)
+        m = SyntheticModel(SMALL, seed=0x5EED + 13)
+        m.set_prefill_mode(0)
+        toks, st = m.generate(prompt, 5)
+        n = len(prompt) + 4
+        out[fused] = (toks, st.decode_launches_per_step, m.logits(), [m.kv_cache(l, n) for l in range(2)])
+        m.close()
+    a, b = out["1"], out["0"]
+    assert a[0] == b[0]
+    assert a[1] == 1 + 8 * SMALL["n_layers"] + 3 and b[1] == 1 + 9 * SMALL["n_layers"] + 3
+    assert np.array_equal(a[2].view(np.uint32), b[2].view(np.uint32))
+    for l in range(2):
+        for j in range(2):
+            assert np.array_equal(a[3][l][j].view(np.uint16), b[3][l][j].view(np.uint16))
+    G.check_device_error()
