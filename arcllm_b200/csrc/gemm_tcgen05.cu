@@ -19,13 +19,16 @@
 //               (warp w serves TMEM lanes 32*(w%4)..) and store Y.
 // Both MMAs of a K step share the dequantised B tile, so each weight is
 // dequantised once per CTA.  When N/128 tiles leave SMs idle (the FFN-down
-// shape, N = 3584), K is split across CTAs and the partial tiles are added
-// in split order by the last CTA of each column tile.  All waits are bounded; on a timeout the kernel
+// shape, N = 3584), K is split across CTAs, the CTAs store partial tiles and
+// a grid-wide reduce kernel adds them in split order (deterministic; the
+// last CTA of each column tile adding them alone was the slowest part of the
+// small-N GEMMs).  All waits are bounded; on a timeout the kernel
 // sets the device error word, lets in-flight copies and MMAs finish (bounded),
 // frees its TMEM and returns.
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "arcllm_cuda_internal.h"
@@ -51,15 +54,13 @@ struct GemmSmemTail {
     uint64_t done;
     uint32_t tmem_base;
     int abort_flag;
-    int last_split;
 };
 
-// Split-K: CTAs (tile, split) cover K super-blocks [nsb*split/ks, nsb*(split+1)/ks).
-// Partial tiles go to ws[split][m][n]; the last CTA of a column tile to arrive
-// (per-tile counter) adds them in split order (deterministic) and writes y.
+// Split-K: CTAs (tile, split) cover K super-blocks [nsb*split/ks, nsb*(split+1)/ks)
+// and store their partial tiles to ws[split][m][n]; a grid-wide reduce kernel
+// then adds them in split order (deterministic) plus the residual into y.
 struct SplitKWs {
     float* ws;
-    uint32_t* cnt;  // per 128-column tile, zero between launches
     uint32_t ks;
 };
 
@@ -446,51 +447,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-        if (sk.ks > 1u) {
-            __threadfence();
-            named_bar_sync(1, kDqWarps * 32u);
-            if (dt == 0) tail->last_split = atomicAdd(&sk.cnt[blockIdx.x], 1u) == sk.ks - 1u;
-            named_bar_sync(1, kDqWarps * 32u);
-            if (tail->last_split) {
-                __threadfence();
-                // all 256 threads add the tile's split partials, coalesced float4 by float4
-                // (four positions per thread at a time, every split's loads in flight together),
-                // in split order (deterministic)
-                if (store) {
-                    const uint32_t nf4 = m * (kBN / 4u), n4 = n_total / 4u;
-#pragma unroll 1
-                    for (uint32_t p0 = dt; p0 < nf4; p0 += 4u * 256u) {
-                        float4 t[4];
-                        uint64_t off4[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const uint32_t pp = min(p0 + 256u * u, nf4 - 1u);  // clamped: duplicates are not stored
-                            off4[u] = (uint64_t)(pp >> 5) * n4 + n0 / 4u + (pp & 31u);
-                            t[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        }
-#pragma unroll 4
-                        for (uint32_t sp = 0; sp < sk.ks; ++sp) {
-                            const float4* src = reinterpret_cast<const float4*>(sk.ws + (uint64_t)sp * m * n_total);
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const float4 v = __ldcg(src + off4[u]);
-                                t[u].x += v.x, t[u].y += v.y, t[u].z += v.z, t[u].w += v.w;
-                            }
-                        }
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            if (p0 + 256u * u >= nf4) break;
-                            if (residual) {
-                                const float4 rr = reinterpret_cast<const float4*>(residual)[off4[u]];
-                                t[u] = make_float4(rr.x + t[u].x, rr.y + t[u].y, rr.z + t[u].z, rr.w + t[u].w);
-                            }
-                            reinterpret_cast<float4*>(y)[off4[u]] = t[u];
-                        }
-                    }
-                }
-                if (dt == 0) atomicExch(&sk.cnt[blockIdx.x], 0u);
-            }
-        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
@@ -500,43 +456,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// y = (residual +) sum over splits of ws[split] -- float4 by float4 over the
+// whole m x n output, splits added in order.
+__global__ void __launch_bounds__(256) gemm_splitk_reduce_kernel(const float4* __restrict__ ws, uint32_t ks,
+                                                                 uint64_t n4, const float4* __restrict__ residual,
+                                                                 float4* __restrict__ y) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (uint32_t sp = 0; sp < ks; ++sp) {
+            const float4 v = ws[(uint64_t)sp * n4 + i];
+            t.x += v.x, t.y += v.y, t.z += v.z, t.w += v.w;
+        }
+        if (residual) {
+            const float4 r = residual[i];
+            t = make_float4(r.x + t.x, r.y + t.y, r.z + t.z, r.w + t.w);
+        }
+        y[i] = t;
+    }
+}
+
 struct GemmScratch {
     float* ws = nullptr;
-    uint32_t* cnt = nullptr;
-    size_t ws_floats = 0, cnt_n = 0;
+    size_t ws_floats = 0;
 };
 std::mutex g_gemm_mutex;
 GemmScratch g_gemm_scratch[64];
 
 // Per-device split-K scratch, grown on demand (not while a graph is being
 // captured; split-K launches on one device must not overlap in time).
-int gemm_splitk_reserve(size_t ws_floats, size_t tiles, float** ws, uint32_t** cnt) {
+int gemm_splitk_reserve(size_t ws_floats, float** ws) {
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(g_gemm_mutex);
     GemmScratch& g = g_gemm_scratch[dev & 63];
-    if (g.ws_floats < ws_floats || g.cnt_n < tiles) {
-        const size_t nw = std::max(ws_floats, g.ws_floats), nc = std::max(tiles, g.cnt_n);
+    if (g.ws_floats < ws_floats) {
         float* nws = nullptr;
-        uint32_t* ncnt = nullptr;
-        cudaError_t e = cudaMalloc(&nws, nw * sizeof(float));
-        if (e == cudaSuccess) e = cudaMalloc(&ncnt, nc * sizeof(uint32_t));
-        if (e == cudaSuccess) e = cudaMemset(ncnt, 0, nc * sizeof(uint32_t));
+        cudaError_t e = cudaMalloc(&nws, ws_floats * sizeof(float));
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) {
             cudaFree(nws);
-            cudaFree(ncnt);
             return set_cuda_error(e, "gemm split-K scratch");
         }
         cudaFree(g.ws);
-        cudaFree(g.cnt);
         g.ws = nws;
-        g.cnt = ncnt;
-        g.ws_floats = nw;
-        g.cnt_n = nc;
+        g.ws_floats = ws_floats;
     }
     *ws = g.ws;
-    *cnt = g.cnt;
     return ARC_OK;
 }
 
@@ -584,17 +550,29 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const uint32_t tiles = n / kBN;
-    const uint32_t ks = std::max(1u, std::min((uint32_t)sms / tiles, k / 256u));
-    SplitKWs sk{nullptr, nullptr, ks};
+    uint32_t ks = std::max(1u, std::min((uint32_t)sms / tiles, k / 256u));
+    // tuning override for experiments: ARCLLM_GEMM_KS=<splits> (1 .. K/256)
+    if (const char* ev = std::getenv("ARCLLM_GEMM_KS")) {
+        const uint32_t f = (uint32_t)std::strtoul(ev, nullptr, 10);
+        if (f >= 1u && f <= k / 256u) ks = f;
+    }
+    SplitKWs sk{nullptr, ks};
     if (ks > 1) {
-        st = gemm_splitk_reserve((size_t)ks * m * n, tiles, &sk.ws, &sk.cnt);
+        st = gemm_splitk_reserve((size_t)ks * m * n, &sk.ws);
         if (st != ARC_OK) return st;
     }
-    const cudaError_t e =
+    cudaError_t e =
         fmt == 12 ? launch_kernel(gemm_kq_bf16_kernel<12>, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
                                   static_cast<const uint8_t*>(w), n, k, m, residual, y, dev_error_word(), sk)
                   : launch_kernel(gemm_kq_bf16_kernel<14>, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
                                   static_cast<const uint8_t*>(w), n, k, m, residual, y, dev_error_word(), sk);
+    if (e == cudaSuccess && ks > 1) {
+        const uint64_t n4 = (uint64_t)m * n / 4u;
+        const uint32_t blocks = (uint32_t)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)sms * 8u);
+        e = launch_kernel(gemm_splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream,
+                          reinterpret_cast<const float4*>(sk.ws), ks, n4, reinterpret_cast<const float4*>(residual),
+                          reinterpret_cast<float4*>(y));
+    }
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "gemm launch");
 }
 
