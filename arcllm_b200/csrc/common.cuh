@@ -42,6 +42,17 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// base + off rounded up to an A-byte boundary of the shared window.  The result
+// is derived from base (a pointer into a __shared__ array) by adding an offset,
+// so the compiler still knows it addresses shared memory; rounding the pointer
+// through an integer would turn every access through it into a generic one
+// (measured: the Q6_K LM-head matvec 91.9 -> 77.9 us).
+template <uint32_t A>
+__device__ __forceinline__ uint8_t* smem_align_up(uint8_t* base, uint32_t off) {
+    const uint32_t s = smem_addr(base);
+    return base + (((s + off + (A - 1u)) & ~(A - 1u)) - s);
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }

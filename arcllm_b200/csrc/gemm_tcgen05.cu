@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint32_t k, uint32_t m, const float* __restrict__ residual, float* __restrict__ y,
                         unsigned int* err, const SplitKWs sk) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem = smem_align_up<1024>(smem_raw, 0);
     GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + kStages * kStageBytes);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t n0 = blockIdx.x * kBN;

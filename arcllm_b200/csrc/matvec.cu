@@ -269,10 +269,9 @@ __global__ void __launch_bounds__((NWC + 1) * 32) matvec_stream_kernel(const MvP
     volatile int* abort_flag = cnt + kMaxStages;
     double* red_d = reinterpret_cast<double*>(smem + 2 * kMaxStages * 8 + 4 * kMaxStages + 16);  // [NWC]
     float* red = reinterpret_cast<float*>(red_d + NWC);  // [kMaxStages][NWC][NV]
-    float* xs = red + kMaxStages * NWC * NV;
-    xs = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(xs) + 15) & ~uintptr_t(15));
-    uint8_t* stages =
-        reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(xs + p.x_floats) + 127) & ~uintptr_t(127));
+    uint8_t* xsb = smem_align_up<16>(smem, (uint32_t)(reinterpret_cast<uint8_t*>(red + kMaxStages * NWC * NV) - smem));
+    float* xs = reinterpret_cast<float*>(xsb);
+    uint8_t* stages = smem_align_up<128>(smem, (uint32_t)(xsb - smem) + 4u * p.x_floats);
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t S = p.stages;

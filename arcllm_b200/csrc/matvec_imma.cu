@@ -233,8 +233,7 @@ __global__ void __launch_bounds__(15 * 32, 1) matvec_imma_kernel(const MvParams 
     double* red_d = reinterpret_cast<double*>(smem + kRedD);  // [32]
     float* red = reinterpret_cast<float*>(red_d + 32);        // [2][stages][nwc][NV]
     uint8_t* xscr = smem + imma_xscr_off(p.stages, nwc, NV);
-    uint8_t* stages = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem + imma_stage_off(p.stages, nwc, NV)) + 127) & ~uintptr_t(127));
+    uint8_t* stages = smem_align_up<128>(smem, imma_stage_off(p.stages, nwc, NV));
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t NT = nwc * 32u;

@@ -187,8 +187,7 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1)
     double* red_d = reinterpret_cast<double*>(smem + kHead);     // [32]
     float* red = reinterpret_cast<float*>(smem + ks_red_off());  // [2][S][kNW][kG]
     uint8_t* xscr = smem + ks_xscr_off(p.stages);
-    uint8_t* stages = reinterpret_cast<uint8_t*>(
-        (reinterpret_cast<uintptr_t>(smem + ks_stage_off(p.stages)) + 127) & ~uintptr_t(127));
+    uint8_t* stages = smem_align_up<128>(smem, ks_stage_off(p.stages));
 
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t S = p.stages;
