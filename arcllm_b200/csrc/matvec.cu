@@ -547,22 +547,20 @@ int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows
                cudaStream_t stream) {
     // Integer tensor-core kernels wherever their shape rules hold (16-byte
     // aligned x and gamma): whole rows for K <= 3584 (matvec_imma.cu), K
-    // slices for Q4_K with K > 3584 (matvec_imma_splitk.cu; FFN down 3584 x
-    // 18944: 16.4 us against 28 us on CUDA cores, measured on B200); the
-    // CUDA-core streaming kernel otherwise -- including Q6_K with K > 3584,
-    // where the K-slice kernel measured slower (27.6 vs 24.5 us).
-    // ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core kernel; =splitk also routes
-    // Q6_K with K > 3584 to the K-slice kernel.
+    // slices for K > 3584 (matvec_imma_splitk.cu; FFN down 3584 x 18944,
+    // measured on B200: Q4_K 16.4 us against 27.5 us on CUDA cores, Q6_K
+    // 20.7 us against 22.4 us); the CUDA-core streaming kernel otherwise.
+    // ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core kernel.
     if (fmt == ARC_TYPE_EXEC148) {  // route B of the Q4 FFN-down capability
         if (dual || gamma || bias) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec EXEC148: no gamma, bias or dual");
         return exec148_matvec(w0, rows, k, x, residual, y, stream);
     }
     const char* env = std::getenv("ARCLLM_MATVEC_IMPL");
-    const int impl = !env ? 1 : (std::strcmp(env, "cuda") == 0 ? 0 : (std::strcmp(env, "splitk") == 0 ? 2 : 1));
+    const int impl = (env && std::strcmp(env, "cuda") == 0) ? 0 : 1;
     const bool x_aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma)) & 15u) == 0u;
     if (impl >= 1 && x_aligned && matvec_imma_supported(fmt, dual, rows, k))
         return matvec_imma_launch(fmt, dual, w0, w1, rows, k, x, gamma, eps, bias, residual, y, stream);
-    if (impl >= 1 && (fmt == 12 || impl == 2) && x_aligned && matvec_splitk_supported(fmt, dual, rows, k))
+    if (impl >= 1 && x_aligned && matvec_splitk_supported(fmt, dual, rows, k))
         return matvec_splitk_launch(fmt, w0, rows, k, x, gamma, eps, bias, residual, y, stream);
     MatvecPlan pl;
     int st = matvec_plan(fmt, dual, rows, k, &pl);

@@ -157,16 +157,23 @@ def test_matvec_parity(fmt, rows, k):
 
 
 @pytest.mark.parametrize("fmt,rows,k", SPLITK_CASES)
-def test_matvec_splitk_parity(fmt, rows, k, monkeypatch):
-    monkeypatch.setenv("ARCLLM_MATVEC_IMPL", "splitk")
+def test_matvec_splitk_parity(fmt, rows, k):
+    test_matvec_parity(fmt, rows, k)
+
+
+# the CUDA-core streaming kernel (ARCLLM_MATVEC_IMPL=cuda) on the shapes the
+# tensor-core kernels take by default
+@pytest.mark.parametrize("fmt,rows,k", [("q6k", 3584, 18944), ("q4k", 3584, 18944), ("q6k", 700, 3584),
+                                        ("q4k", 13, 4608)])
+def test_matvec_cuda_core_parity(fmt, rows, k, monkeypatch):
+    monkeypatch.setenv("ARCLLM_MATVEC_IMPL", "cuda")
     test_matvec_parity(fmt, rows, k)
 
 
 @pytest.mark.parametrize("fmt", ["q4k", "q6k"])
-def test_matvec_splitk_repeat_bit_identical(fmt, monkeypatch):
+def test_matvec_splitk_repeat_bit_identical(fmt):
     """The cross-CTA reduction re-arms its counters and adds slice partials in
     a fixed order: back-to-back launches give bit-identical rows."""
-    monkeypatch.setenv("ARCLLM_MATVEC_IMPL", "splitk")
     rows, k, seed = 3584, 18944, 5151
     w = gpu_fill(fmt, rows, k, seed)
     x = O.normal_f32(k, seed + 1)
@@ -177,8 +184,7 @@ def test_matvec_splitk_repeat_bit_identical(fmt, monkeypatch):
 
 
 @pytest.mark.parametrize("fmt", ["q4k", "q6k"])
-def test_matvec_splitk_rmsnorm_residual(fmt, monkeypatch):
-    monkeypatch.setenv("ARCLLM_MATVEC_IMPL", "splitk")
+def test_matvec_splitk_rmsnorm_residual(fmt):
     rows, k, seed = 200, 18944, 4343
     w = gpu_fill(fmt, rows, k, seed)
     x = O.normal_f32(k, seed + 1)
