@@ -79,9 +79,19 @@ struct RopeEpilogue {
     const uint32_t* pos;
     uint16_t* cache;  // this layer's cache: row p at p * rows
 };
+// Rank all-gather epilogue of the whole-row kernel: y rows also go to peer_y[r] (other ranks'
+// logits, NVLink peer mappings) and the launch ends with the flag handshake of the ranks
+// (peer_flags[r]: rank r's flag array; done_ctr: this rank's CTA counter, zero between launches).
+struct RankGather {
+    uint32_t n_ranks, self_rank, epoch;
+    unsigned long long wait_ns;
+    float* peer_y[8];
+    uint32_t* peer_flags[8];
+    uint32_t* done_ctr;
+};
 int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                        const float* gamma, float eps, const float* bias, const float* residual, float* y,
-                       cudaStream_t stream, const RopeEpilogue* rope = nullptr);
+                       cudaStream_t stream, const RopeEpilogue* rope = nullptr, const RankGather* gather = nullptr);
 // Integer tensor-core K-slice variant (matvec_imma_splitk.cu) for K > 3584.
 // It adds CTA partials through a per-device scratch: launches of it on one
 // device must not overlap in time (one stream, or ordered streams).

@@ -148,6 +148,81 @@ int arcllm_cuda_matvec_hostio(int ggml_type, const void* w, uint32_t rows, uint3
     ARC_GUARD_END
 }
 
+// ---- rank all-gather over NVLink peer memory ----
+// Exchange buffer of one rank: fp32 logits [rows_total] at 0, then at a 256-byte boundary
+// the flag array (one u32 slot per rank) and, 64 bytes further, this rank's CTA counter.
+static uint64_t gather_flags_offset(uint32_t rows_total) { return ((uint64_t)rows_total * 4u + 255u) & ~uint64_t(255); }
+
+int arcllm_cuda_allgather_buffer_bytes(uint32_t rows_total, uint64_t* out) {
+    ARC_GUARD_BEGIN
+    if (!out || rows_total == 0) return set_error(ARC_E_INVALID_ARGUMENT, "allgather_buffer_bytes: bad argument");
+    *out = gather_flags_offset(rows_total) + 128u;
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_matvec_allgather(int ggml_type, const void* w, uint32_t rows, uint32_t k, const float* x,
+                                 uint32_t row0, uint32_t rows_total, void* const* rank_bufs, uint32_t n_ranks,
+                                 uint32_t rank, uint32_t epoch, uint32_t timeout_us, void* stream) {
+    ARC_GUARD_BEGIN
+    if (ggml_type != ARC_GGML_Q4_K && ggml_type != ARC_GGML_Q6_K)
+        return set_error(ARC_E_INVALID_ARGUMENT, "matvec_allgather: Q4_K or Q6_K weights");
+    if (!rank_bufs || n_ranks == 0 || n_ranks > 8 || rank >= n_ranks || epoch == 0 || rows == 0 ||
+        (uint64_t)row0 + rows > rows_total)
+        return set_error(ARC_E_INVALID_ARGUMENT, "matvec_allgather: bad rank layout or epoch");
+    if (!arc::matvec_imma_supported(ggml_type, false, rows, k) || (reinterpret_cast<uintptr_t>(x) & 15u))
+        return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec_allgather: needs the whole-row tensor-core kernel "
+                                                  "(K/256 <= 14, 16-byte aligned x)");
+    const uint64_t fo = gather_flags_offset(rows_total);
+    arc::RankGather g{};
+    g.n_ranks = n_ranks;
+    g.self_rank = rank;
+    g.epoch = epoch;
+    g.wait_ns = 1000ull * (timeout_us ? timeout_us : 2000000u);
+    for (uint32_t r = 0; r < n_ranks; ++r) {
+        if (!rank_bufs[r] || (reinterpret_cast<uintptr_t>(rank_bufs[r]) & 255u))
+            return set_error(ARC_E_ALIGNMENT, "matvec_allgather: rank buffers must be 256-byte aligned");
+        uint8_t* b = static_cast<uint8_t*>(rank_bufs[r]);
+        g.peer_y[r] = reinterpret_cast<float*>(b) + row0;
+        g.peer_flags[r] = reinterpret_cast<uint32_t*>(b + fo);
+    }
+    g.done_ctr = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(rank_bufs[rank]) + fo + 64u);
+    return arc::matvec_imma_launch(ggml_type, false, w, nullptr, rows, k, x, nullptr, 0.f, nullptr, nullptr,
+                                   g.peer_y[rank], static_cast<cudaStream_t>(stream), nullptr, &g);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_ipc_get_handle(const void* dev_ptr, void* handle_out) {
+    ARC_GUARD_BEGIN
+    if (!dev_ptr || !handle_out) return set_error(ARC_E_INVALID_ARGUMENT, "ipc_get_handle: null pointer");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+    if (e != cudaSuccess) return arc::set_cuda_error(e, "ipc_get_handle");
+    std::memcpy(handle_out, &h, sizeof(h));
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_ipc_open_handle(const void* handle, void** dev_ptr_out) {
+    ARC_GUARD_BEGIN
+    if (!handle || !dev_ptr_out) return set_error(ARC_E_INVALID_ARGUMENT, "ipc_open_handle: null pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    cudaError_t e = cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return arc::set_cuda_error(e, "ipc_open_handle");
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_ipc_close_handle(void* dev_ptr) {
+    ARC_GUARD_BEGIN
+    if (!dev_ptr) return set_error(ARC_E_INVALID_ARGUMENT, "ipc_close_handle: null pointer");
+    cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    if (e != cudaSuccess) return arc::set_cuda_error(e, "ipc_close_handle");
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_matvec_q4k(const void* w, uint32_t rows, uint32_t k, const float* x, const float* bias, float* y,
                            void* stream) {
     return arcllm_cuda_matvec(ARC_GGML_Q4_K, w, rows, k, x, nullptr, 0.f, bias, nullptr, y, stream);

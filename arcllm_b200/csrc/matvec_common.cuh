@@ -13,6 +13,8 @@ namespace {
 constexpr int kMaxStages = 8;
 constexpr uint32_t kStagePad = 16;  // slack after each stage for 32-bit reads that run past a block
 
+constexpr uint32_t kMaxRanks = 8;  // ranks of the all-gather epilogue (one node)
+
 struct MvParams {
     const uint8_t* w0;
     const uint8_t* w1;  // second matrix of the dual (gate/up) form
@@ -38,6 +40,16 @@ struct MvParams {
     const uint32_t* rope_pos;       // device position
     uint16_t* cache;                // cache base + layer offset; row `pos` starts at pos * rows
     uint32_t max_ctx;
+    // rank all-gather epilogue (whole-row integer-MMA kernel, not dual, rope_mode 0; n_ranks 0 =
+    // none): row i of this shard is also stored at peer_y[r][i] for every rank r != self_rank
+    // (NVLink peer stores into the other ranks' logits); then the CTAs count themselves on
+    // done_ctr and the last one writes `epoch` into slot self_rank of every rank's flag array
+    // and waits, at most wait_ns, until every slot of its own array has reached `epoch`
+    uint32_t n_ranks, self_rank, epoch;
+    unsigned long long wait_ns;
+    float* peer_y[kMaxRanks];
+    uint32_t* peer_flags[kMaxRanks];
+    uint32_t* done_ctr;
 };
 
 // Fold N per-row partial sums over the warp: afterwards lane L holds the full

@@ -119,6 +119,9 @@ __device__ __forceinline__ void finish_rows(const MvParams& p, const float* red,
             if (p.bias) a += p.bias[row];
             if (p.residual) a = p.residual[row] + a;
             p.y[row] = a;
+#pragma unroll
+            for (uint32_t q = 0; q < kMaxRanks; ++q)  // all-gather: the same row into every other rank
+                if (q < p.n_ranks && q != p.self_rank) p.peer_y[q][row] = a;
         }
     }
     if (!DUAL && p.rope_mode != 0) {
@@ -156,6 +159,44 @@ __device__ __forceinline__ void finish_rows(const MvParams& p, const float* red,
 // r+1 never touches the buffer of round r being summed here.  All waits are
 // bounded; on a timeout it sets *abort_flag, stops, and waits (bounded) for
 // the copies it already issued.
+// End of the rank all-gather epilogue, run by each CTA's producer warp after
+// its last rows are stored.  Every lane fences its own (local and peer) stores
+// at system scope, lane 0 counts the CTA on done_ctr, and the CTA that
+// completes the count publishes `epoch` into this rank's slot of every rank's
+// flag array (release) and waits until every slot of its own array has
+// reached `epoch` (acquire; wrap-safe, a peer may already be one launch ahead).
+// The wait gives up after p.wait_ns with ARC_DEV_ERR_TIMEOUT.
+__device__ __forceinline__ void rank_gather_sync(const MvParams& p, uint32_t lane) {
+    __threadfence_system();
+    __syncwarp();
+    if (lane != 0) return;
+    if (atomicAdd(p.done_ctr, 1u) != gridDim.x - 1u) return;
+    __threadfence_system();  // the other CTAs' stores are ordered before their counts
+    *p.done_ctr = 0u;        // re-armed for the next launch in stream order
+#pragma unroll
+    for (uint32_t q = 0; q < kMaxRanks; ++q)
+        if (q < p.n_ranks)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[q] + p.self_rank), "r"(p.epoch)
+                         : "memory");
+    const uint32_t* mine = p.peer_flags[0];
+#pragma unroll
+    for (uint32_t q = 1; q < kMaxRanks; ++q)
+        if (q == p.self_rank) mine = p.peer_flags[q];
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t q = 0; q < p.n_ranks; ++q) {
+        for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + q) : "memory");
+            if ((int)(v - p.epoch) >= 0) break;
+            if (globaltimer() - t0 > p.wait_ns) {
+                raise_error(p.err, ARC_DEV_ERR_TIMEOUT);
+                return;
+            }
+            __nanosleep(64);
+        }
+    }
+}
+
 template <int G, bool DUAL>
 __device__ __forceinline__ void produce_and_finish(const MvParams& p, uint8_t* stages, uint64_t* full,
                                                    uint64_t* empty, volatile int* abort_flag, uint32_t mat_off,
@@ -219,6 +260,8 @@ __device__ __forceinline__ void produce_and_finish(const MvParams& p, uint8_t* s
         const uint32_t first = it > S ? it - S : 0;
         for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1u, p.err);
     }
+    // an aborted CTA still counts itself, so the counter re-arms (the error word reports the abort)
+    if (!DUAL && p.n_ranks) rank_gather_sync(p, lane);
 }
 
 template <int FMT, int MT, bool DUAL>
@@ -390,7 +433,7 @@ bool matvec_imma_supported(int fmt, bool dual, uint32_t rows, uint32_t k) {
 
 int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                        const float* gamma, float eps, const float* bias, const float* residual, float* y,
-                       cudaStream_t stream, const RopeEpilogue* rope) {
+                       cudaStream_t stream, const RopeEpilogue* rope, const RankGather* gather) {
     if (!matvec_imma_supported(fmt, dual, rows, k))
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec_imma: shape outside K/256 <= 14 (even for Q6_K)");
     if (!w0 || !x || !y || (dual && !w1)) return set_error(ARC_E_INVALID_ARGUMENT, "matvec: null pointer");
@@ -430,6 +473,22 @@ int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint3
         p.rope_pos = rope->pos;
         p.cache = rope->cache;
         p.max_ctx = rope->max_ctx;
+    }
+    if (gather && gather->n_ranks != 0) {
+        if (dual || (rope && rope->mode != 0) || gather->n_ranks > kMaxRanks || gather->self_rank >= gather->n_ranks ||
+            !gather->done_ctr)
+            return set_error(ARC_E_INVALID_ARGUMENT, "matvec_imma: bad rank all-gather epilogue");
+        p.n_ranks = gather->n_ranks;
+        p.self_rank = gather->self_rank;
+        p.epoch = gather->epoch;
+        p.wait_ns = gather->wait_ns;
+        for (uint32_t r = 0; r < gather->n_ranks; ++r) {
+            if (!gather->peer_y[r] || !gather->peer_flags[r])
+                return set_error(ARC_E_INVALID_ARGUMENT, "matvec_imma: null rank buffer");
+            p.peer_y[r] = gather->peer_y[r];
+            p.peer_flags[r] = gather->peer_flags[r];
+        }
+        p.done_ctr = gather->done_ctr;
     }
     static int sm_count[64] = {};  // per device, queried once
     int dev = 0;

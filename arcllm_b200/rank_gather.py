@@ -1,0 +1,101 @@
+"""Rank exchange buffers for the NVLink all-gather form of the LM-head matvec.
+
+One process per GPU.  Each rank allocates one exchange buffer (fp32 logits of
+all rows, then the per-rank flag array and its CTA counter), shares a CUDA IPC
+handle of it with the other ranks and opens theirs, so that
+``arcllm_cuda_matvec_allgather`` can store each rank's rows into every rank's
+buffer with NVLink peer stores and end with a flag handshake.  The handle
+exchange itself is a host collective supplied by the caller
+(``torch.distributed.all_gather_object`` in bench.py, a multiprocessing pipe in
+the tests): the data path has no host collective and no NCCL call.
+
+The reference runs its LM head on one device
+(src/arcllm_v1_runtime.cpp:285-291); this is the row-sharded multi-GPU form of
+that step.
+"""
+import ctypes as C
+
+from . import GGML_Q6_K, call, lib
+
+HANDLE_BYTES = 64  # cudaIpcMemHandle_t
+
+
+class RankGather:
+    """Exchange buffers of `n_ranks` ranks for a `rows_total`-row result.
+
+    exchange(handle_bytes) -> list of every rank's handle bytes, in rank order
+    (the caller's host all-gather).  After construction, `step()` launches one
+    all-gather matvec and `logits_ptr` holds all rows once it completes.
+
+    Two buffers alternate by epoch parity: a peer that is already running the
+    next launch stores into the other buffer, and it cannot get two launches
+    ahead, because its launch completes only after this rank's next launch --
+    stream-ordered after this rank's reads of the current logits -- has
+    published its flag.
+    """
+
+    def __init__(self, rows_total, n_ranks, rank, exchange, timeout_us=2000000):
+        if not (1 <= n_ranks <= 8 and 0 <= rank < n_ranks):
+            raise ValueError("RankGather: 1 <= n_ranks <= 8 and 0 <= rank < n_ranks")
+        L = lib()
+        self.rows_total, self.n_ranks, self.rank, self.timeout_us = rows_total, n_ranks, rank, timeout_us
+        n = C.c_uint64(0)
+        call("arcllm_cuda_allgather_buffer_bytes", rows_total, C.byref(n))
+        self.nbytes = n.value
+        self._own, self._opened, self._bufs = [], [], []
+        zeros = (C.c_uint8 * self.nbytes)()
+        handles = []
+        for _ in range(2):
+            own = C.c_void_p()
+            call("arcllm_cuda_malloc", self.nbytes, C.byref(own))
+            self._own.append(own)
+            call("arcllm_cuda_memcpy_h2d", own, C.cast(zeros, C.c_void_p), self.nbytes, None)
+            h = (C.c_uint8 * HANDLE_BYTES)()
+            call("arcllm_cuda_ipc_get_handle", own, C.cast(h, C.c_void_p))
+            handles.append(bytes(h))
+        call("arcllm_cuda_stream_synchronize", None)
+        everyone = exchange(handles[0] + handles[1])
+        if len(everyone) != n_ranks:
+            raise RuntimeError("RankGather: exchange returned %d entries for %d ranks" % (len(everyone), n_ranks))
+        for b in range(2):
+            ptrs = []
+            for r, hb in enumerate(everyone):
+                if r == rank:
+                    ptrs.append(self._own[b].value)
+                    continue
+                p = C.c_void_p()
+                raw = hb[b * HANDLE_BYTES:(b + 1) * HANDLE_BYTES]
+                hbuf = (C.c_uint8 * HANDLE_BYTES).from_buffer_copy(raw)
+                call("arcllm_cuda_ipc_open_handle", C.cast(hbuf, C.c_void_p), C.byref(p))
+                self._opened.append(p)
+                ptrs.append(p.value)
+            self._bufs.append((C.c_void_p * n_ranks)(*ptrs))
+        self.epoch = 0
+        self._L = L
+
+    @property
+    def logits_ptr(self):
+        """Device address of this rank's copy of all rows_total results of the
+        last launch."""
+        return self._own[self.epoch & 1].value
+
+    def step(self, w, rows, k, x, row0, stream, ggml_type=GGML_Q6_K):
+        """One all-gather matvec of this rank's rows [row0, row0 + rows)."""
+        self.epoch += 1
+        st = self._L.arcllm_cuda_matvec_allgather(ggml_type, w, rows, k, x, row0, self.rows_total,
+                                                  self._bufs[self.epoch & 1], self.n_ranks, self.rank, self.epoch,
+                                                  self.timeout_us, stream)
+        if st:
+            from . import check
+            check(st, "matvec_allgather")
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's.  Call only after every
+        rank has finished its last step (a host barrier), so no peer still
+        stores into this buffer."""
+        for p in self._opened:
+            call("arcllm_cuda_ipc_close_handle", p)
+        self._opened = []
+        for own in self._own:
+            call("arcllm_cuda_free", own)
+        self._own = []

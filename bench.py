@@ -238,6 +238,9 @@ def main(argv=None):
     ap.add_argument("--only", choices=["decode", "prefill", "extra"],
                     help="profiling: run only the config-3 decode, the config-4 prefill GEMMs or all extra "
                          "configurations and print the result")
+    ap.add_argument("--collective", default="nvlink", choices=["nvlink", "nccl"],
+                    help="N>1: logits all-gather fused into the matvec over NVLink peer stores (default) or the "
+                         "matvec followed by ncclAllGather")
     ap.add_argument("--decode-prompt", type=int, default=256)
     ap.add_argument("--decode-new", type=int, default=128)
     args = ap.parse_args(argv)
@@ -302,7 +305,22 @@ def main(argv=None):
     logits = torch.empty(rows_per * world, dtype=torch.float32, device=dev)
     wp, xp, yp = C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr())
 
+    rg = None
+    if dist is not None and args.collective == "nvlink":
+        from arcllm_b200.rank_gather import RankGather
+
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+
+        rg = RankGather(rows_per * world, world, rank, exchange)
+        barrier()
+
     def step():
+        if rg is not None:  # one kernel: rows + NVLink peer stores + flag handshake
+            rg.step(wp, rows_per, K, xp, r0, sp, TY)
+            return
         st = L.arcllm_cuda_matvec(TY, wp, rows_per, K, xp, None, C.c_float(0.0), None, None, yp, sp)
         if st:
             A.check(st, "matvec")
@@ -321,11 +339,14 @@ def main(argv=None):
     t_start.record()
     for i in range(args.steps):
         ev[i][0].record()
-        st = L.arcllm_cuda_matvec(TY, wp, rows_per, K, xp, None, C.c_float(0.0), None, None, yp, sp)
-        if st:
-            A.check(st, "matvec")
+        if rg is not None:
+            rg.step(wp, rows_per, K, xp, r0, sp, TY)
+        else:
+            st = L.arcllm_cuda_matvec(TY, wp, rows_per, K, xp, None, C.c_float(0.0), None, None, yp, sp)
+            if st:
+                A.check(st, "matvec")
         ev[i][1].record()
-        if dist is not None:
+        if dist is not None and rg is None:
             dist.all_gather_into_tensor(logits, y)
     t_end.record()
     barrier()
@@ -355,6 +376,13 @@ def main(argv=None):
     e2e_steps = 0 if args.no_e2e else max(10, min(args.steps, 500))
 
     def e2e_step():
+        if rg is not None:  # host x in, the fused all-gather matvec, every row's logit out
+            A.check(L.arcllm_cuda_memcpy_h2d(C.c_void_p(xd.data_ptr()), C.c_void_p(xh.data_ptr()), 4 * K, sp))
+            rg.step(wp, rows_per, K, C.c_void_p(xd.data_ptr()), r0, sp, TY)
+            A.check(L.arcllm_cuda_memcpy_d2h(C.c_void_p(lh.data_ptr()), C.c_void_p(rg.logits_ptr),
+                                             4 * rows_per * world, sp))
+            A.check(L.arcllm_cuda_stream_synchronize(sp))
+            return
         A.check(L.arcllm_cuda_matvec_hostio(TY, wp, rows_per, K, C.c_void_p(xh.data_ptr()),
                                             C.c_void_p(xd.data_ptr()), yp, C.c_void_p(yh.data_ptr()), sp),
                 "matvec_hostio")
@@ -404,7 +432,9 @@ def main(argv=None):
             "config": {
                 "workload": ("config1: Q6_K LM-head matvec 152064x3584 (447.07 MB packed weights), fp32 x ~ N(0,1)"
                              if headline else "profiling case: %s matvec %dx%d" % (fmt, ROWS, K))
-                            + ("; rows sharded over %d GPUs + NCCL all-gather of fp32 logits" % world
+                            + (("; rows sharded over %d GPUs, fp32 logits all-gathered by the matvec kernel itself "
+                                "(NVLink peer stores + flag handshake)" % world if rg is not None else
+                                "; rows sharded over %d GPUs + NCCL all-gather of fp32 logits" % world)
                                if world > 1 else ""),
                 "l2": "weights larger than L2 (%.0f MB vs 126 MB): no flush needed between steps"
                       % (q_bytes(fmt, ROWS, K) / 1e6),
@@ -414,13 +444,17 @@ def main(argv=None):
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "kernel": "matvec_imma_kernel (%s)" % fmt,
+                "kernel": "matvec_imma_kernel (%s)" % fmt + (" with the NVLink all-gather epilogue; kernel_ms "
+                                                             "includes the peer stores and the rank handshake"
+                                                             if rg is not None else ""),
                 "kernel_ms": round(kern_ms, 5), "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
             },
             "e2e": {"value": None if e2e_val is None else round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": 4 * K,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
-                    "api": "arcllm_cuda_matvec_hostio (pinned host x in, logits out, stream sync)"},
+                    "api": ("arcllm_cuda_memcpy_h2d + arcllm_cuda_matvec_allgather + arcllm_cuda_memcpy_d2h of all "
+                            "logits + stream sync" if rg is not None else
+                            "arcllm_cuda_matvec_hostio (pinned host x in, logits out, stream sync)")},
             "gpu_launches": args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -429,6 +463,11 @@ def main(argv=None):
             line["extra"] = extra
         print(json.dumps(line), flush=True)
     if dist is not None:
+        dist.barrier()
+        torch.cuda.synchronize()
+        if rg is not None:
+            dist.barrier()  # every rank's last launch is done before the buffers go away
+            rg.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -110,6 +110,39 @@ ARCLLM_CUDA_API int arcllm_cuda_matvec_hostio(int ggml_type, const void *w, uint
                                               const float *x_host, float *x_dev, float *y_dev, float *y_host,
                                               void *stream);
 
+/* ---- row-sharded matvec with the result all-gathered over NVLink --------
+ * Multi-GPU form of the LM head (rows sharded over the ranks: rank r owns rows
+ * [row0, row0 + rows) of a rows_total-row matrix; the reference runs the LM
+ * head on one device, src/arcllm_v1_runtime.cpp:285-291).  One kernel per
+ * rank computes its rows and stores each fp32 result into EVERY rank's
+ * exchange buffer (local store for its own, NVLink peer stores for the
+ * others), then the ranks meet on per-rank flags: when the launch completes
+ * on rank r, rank_bufs[r] holds all rows_total logits.  This replaces
+ * matvec + ncclAllGather.
+ *   rank_bufs[i]: this process's device address of rank i's exchange buffer
+ *                 (its own allocation for i == rank, an IPC mapping otherwise),
+ *                 256-byte aligned, arcllm_cuda_allgather_buffer_bytes bytes,
+ *                 zero-filled before first use;
+ *   epoch: 1, 2, 3 ... -- the same sequence on every rank, one per launch;
+ *   timeout_us: bound of the flag wait (0: 2 s); a wait that runs out sets
+ *               the device error word (ARC_E_DEVICE_TIMEOUT via
+ *               arcllm_cuda_device_error) and the kernel returns.
+ * A rank may not rewrite a buffer that peers still store into: launches of
+ * one epoch sequence must not overlap a reader of the previous logits.
+ * Shapes: the whole-row tensor-core kernel (K/256 <= 14, even for Q6_K),
+ * 16-byte aligned x; n_ranks <= 8. */
+ARCLLM_CUDA_API int arcllm_cuda_allgather_buffer_bytes(uint32_t rows_total, uint64_t *out);
+ARCLLM_CUDA_API int arcllm_cuda_matvec_allgather(int ggml_type, const void *w, uint32_t rows, uint32_t k,
+                                                 const float *x, uint32_t row0, uint32_t rows_total,
+                                                 void *const *rank_bufs, uint32_t n_ranks, uint32_t rank,
+                                                 uint32_t epoch, uint32_t timeout_us, void *stream);
+/* CUDA IPC of exchange buffers between the ranks' processes: a 64-byte
+ * handle of a buffer allocated with arcllm_cuda_malloc, opened in a peer
+ * process (peer access enabled lazily), closed before the owner frees it. */
+ARCLLM_CUDA_API int arcllm_cuda_ipc_get_handle(const void *dev_ptr, void *handle_out);
+ARCLLM_CUDA_API int arcllm_cuda_ipc_open_handle(const void *handle, void **dev_ptr_out);
+ARCLLM_CUDA_API int arcllm_cuda_ipc_close_handle(void *dev_ptr);
+
 /* ---- fused gate/up projection with SiLU-multiply (Q4_K) -------------------
  * s[r] = silu(g[r]) * u[r],  g = W_gate . xn,  u = W_up . xn,  xn as above.
  * Replaces the I002 pair of shaders/sa1_q4k_subgroup_splitk.comp dispatches

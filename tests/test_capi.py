@@ -64,3 +64,29 @@ def test_host_side_argument_validation():
     assert L.arcllm_cuda_status_string(st) == b"ARC_E_UNSUPPORTED_SHAPE"
     st = L.arcllm_cuda_dequant_q4k(None, 4, None, None)
     assert L.arcllm_cuda_status_string(st) == b"ARC_E_INVALID_ARGUMENT"
+
+
+def test_allgather_layout_and_argument_validation():
+    """Exchange-buffer layout and the all-gather matvec's argument checks
+    (all before any device work)."""
+    L = A.lib()
+    name = L.arcllm_cuda_status_string
+    n = C.c_uint64(0)
+    assert L.arcllm_cuda_allgather_buffer_bytes(6016, C.byref(n)) == 0
+    assert n.value == 24064 + 128  # logits, then flags + counter at a 256-byte boundary
+    assert L.arcllm_cuda_allgather_buffer_bytes(6017, C.byref(n)) == 0 and n.value == 24320 + 128
+    ag = L.arcllm_cuda_matvec_allgather
+    w, x = C.c_void_p(256), C.c_void_p(256)
+    ok = (C.c_void_p * 2)(256, 512)
+    cases = [
+        ((A.GGML_Q6_K, w, 3008, 3584, x, 0, 6016, ok, 0, 0, 1, 0, None), b"ARC_E_INVALID_ARGUMENT"),  # no ranks
+        ((A.GGML_Q6_K, w, 3008, 3584, x, 0, 6016, ok, 2, 2, 1, 0, None), b"ARC_E_INVALID_ARGUMENT"),  # rank >= n
+        ((A.GGML_Q6_K, w, 3008, 3584, x, 0, 6016, ok, 2, 0, 0, 0, None), b"ARC_E_INVALID_ARGUMENT"),  # epoch 0
+        ((A.GGML_Q6_K, w, 3008, 3584, x, 3009, 6016, ok, 2, 1, 1, 0, None), b"ARC_E_INVALID_ARGUMENT"),  # past end
+        ((13, w, 3008, 3584, x, 0, 6016, ok, 2, 0, 1, 0, None), b"ARC_E_INVALID_ARGUMENT"),  # type
+        ((A.GGML_Q6_K, w, 3008, 4096, x, 0, 6016, ok, 2, 0, 1, 0, None), b"ARC_E_UNSUPPORTED_SHAPE"),  # K
+        ((A.GGML_Q6_K, w, 3008, 3584, x, 0, 6016, (C.c_void_p * 2)(256, 100), 2, 0, 1, 0, None),
+         b"ARC_E_ALIGNMENT"),
+    ]
+    for args, want in cases:
+        assert name(ag(*args)) == want, args
