@@ -24,6 +24,33 @@ __device__ __forceinline__ float combine(int c0, int c1, int c2, int h, int l) {
     return fmaf((float)(c0 * 256 + c1 - h), 256.0f, (float)(c2 - l));
 }
 
+// Two fp32 lanes per instruction (fma.rn.f32x2 / mul.rn.f32x2): each lane is
+// rounded exactly as the scalar fmaf / __fmul_rn would round it.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 a, b, c;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "mov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 c, a, b, c;\n\t"
+        "mov.b64 {%0, %1}, c;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 a, b, c;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 c, a, b;\n\t"
+        "mov.b64 {%0, %1}, c;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // 32-bit read at a smem offset that is 4-aligned (EVEN) or 2 mod 4 (ODD)
 template <bool ODD>
 __device__ __forceinline__ uint32_t ld32(const uint8_t* base, uint32_t off) {
@@ -196,6 +223,20 @@ __device__ __forceinline__ void gather_xfrag(const uint8_t* pA, const float* kA,
     }
 }
 
+// The four 4-code words of one (ql word a, ql word b = a + 32 bytes, qh word)
+// triple: code = low or high nibble | two qh bits << 4.  qh is split once into
+// the bit pairs of quarters 0/2 (0x33) and 1/3 (0xCC), so each code word is one
+// shift and one bit-select (the other bit positions of the shifted pair are
+// zero or fall in the nibble half of the select).
+__device__ __forceinline__ void q6_codes(uint32_t a, uint32_t b, uint32_t qh, uint32_t (&v)[4]) {
+    constexpr uint32_t K = 0x0F0F0F0Fu;
+    const uint32_t qm = qh & 0x33333333u, qn = qh & 0xCCCCCCCCu;
+    v[0] = (a & K) | ((qm << 4) & ~K);
+    v[1] = (b & K) | ((qn << 2) & ~K);
+    v[2] = ((a >> 4) & K) | (qm & ~K);
+    v[3] = ((b >> 4) & K) | ((qn >> 2) & ~K);
+}
+
 // Stage-local rows of M-tile m: (row of lanes g, row of lanes g+8).  For Q6_K
 // with two tiles the rows are interleaved (4g+m, 4g+2+m) so that the eight
 // row groups of a 32-bit shared-memory read fall into different banks
@@ -250,6 +291,9 @@ __device__ __forceinline__ void q4_tile(const uint8_t* st, uint32_t r0, uint32_t
 // (ql[0..63], qh[0..31], scales 0..7) of block bA and half 1 of block bB.
 // bA and bB have opposite parity, so every warp does one 4-byte-aligned half
 // and one half at 2 mod 4 in shared memory (ODD0: half 0 is the odd one).
+// The two MMAs into one accumulator are issued apart (window order 0, 2, 1, 3)
+// and the scale epilogue runs on both rows at once in packed fp32 pairs (the
+// same roundings per row as the scalar form).
 template <bool ODD0>
 __device__ __forceinline__ void q6_tile(const uint8_t* st, uint32_t row0, uint32_t row1, uint32_t offA, uint32_t offB,
                                         uint32_t t, const XFrag& f, float& y0, float& y1) {
@@ -279,43 +323,43 @@ __device__ __forceinline__ void q6_tile(const uint8_t* st, uint32_t row0, uint32
                     qb = ld32<false>(st, ro + 64u * h + 32u);
                     qh = ld32<false>(st, ro + 128u + 32u * h);
                 }
-                v[lh][r][0] = (qa & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
-                v[lh][r][1] = (qb & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
-                v[lh][r][2] = ((qa >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
-                v[lh][r][3] = ((qb >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
+                q6_codes(qa, qb, qh, v[lh][r]);
             }
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int qq = 0; qq < 4; ++qq) {
+            const int q = ((qq & 1) << 1) | (qq >> 1);
             const int m = 4 * h + q, i = 2 * h + (q >> 1);
             imma(D1[i], v[0][0][q], v[0][1][q], v[1][0][q], v[1][1][q], f.b1[m][0], f.b1[m][1]);
             imma(D2[i], v[0][0][q], v[0][1][q], v[1][0][q], v[1][1][q], f.b2[m][0], f.b2[m][1]);
         }
     }
-    float out[2];
+    float2 part[2];  // [half] (row0, row1)
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const uint32_t ro = r ? row1 : row0;
-        float part[2];
+    for (int h = 0; h < 2; ++h) {
+        const int8_t* sc0 = reinterpret_cast<const int8_t*>(st + row0 + (h ? offB : offA) + 192u + t);
+        const int8_t* sc1 = reinterpret_cast<const int8_t*>(st + row1 + (h ? offB : offA) + 192u + t);
+        float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            // group 4i + t of half h lives in block h ? bB : bA (scales 8h..8h+7)
-            const int8_t* sc = reinterpret_cast<const int8_t*>(st + ro + (h ? offB : offA) + 192u + t);
-            float acc = 0.f;
-#pragma unroll
-            for (int ii = 0; ii < 2; ++ii) {
-                const int i = 2 * h + ii;
-                const float F = combine(D1[i][2 * r], D1[i][2 * r + 1], D2[i][2 * r], f.xh[i], f.xl[i]);
-                acc = fmaf((float)sc[4 * i] * f.sx[i], F, acc);
-            }
-            part[h] = acc;
+        for (int ii = 0; ii < 2; ++ii) {
+            const int i = 2 * h + ii;
+            const float2 hi = make_float2((float)(D1[i][0] * 256 + D1[i][1] - f.xh[i]),
+                                          (float)(D1[i][2] * 256 + D1[i][3] - f.xh[i]));
+            const float2 lo = make_float2((float)(D2[i][0] - f.xl[i]), (float)(D2[i][2] - f.xl[i]));
+            const float2 F = fma2(hi, make_float2(256.0f, 256.0f), lo);
+            const float2 s = mul2(make_float2((float)sc0[4 * i], (float)sc1[4 * i]), make_float2(f.sx[i], f.sx[i]));
+            acc = fma2(s, F, acc);
         }
-        const float dA = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(st + ro + offA + 208u)));
-        const float dB = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(st + ro + offB + 208u)));
-        out[r] = fmaf(dA, part[0], dB * part[1]);
+        part[h] = acc;
     }
-    y0 += out[0];
-    y1 += out[1];
+    auto d_of = [&](uint32_t ro, uint32_t off) {
+        return __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(st + ro + off + 208u)));
+    };
+    const float2 dA = make_float2(d_of(row0, offA), d_of(row1, offA));
+    const float2 dB = make_float2(d_of(row0, offB), d_of(row1, offB));
+    const float2 o = fma2(dA, part[0], mul2(dB, part[1]));
+    y0 += o.x;
+    y1 += o.y;
 }
 
 // q6_tile with each half's scale epilogue run right after its MMAs, so only
@@ -350,10 +394,7 @@ __device__ __forceinline__ void q6_tile_lowreg(const uint8_t* st, uint32_t row0,
                     qb = ld32<false>(st, ro + 64u * h + 32u);
                     qh = ld32<false>(st, ro + 128u + 32u * h);
                 }
-                v[lh][r][0] = (qa & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
-                v[lh][r][1] = (qb & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
-                v[lh][r][2] = ((qa >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
-                v[lh][r][3] = ((qb >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
+                q6_codes(qa, qb, qh, v[lh][r]);
             }
         }
 #pragma unroll
