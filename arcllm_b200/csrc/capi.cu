@@ -138,10 +138,20 @@ int arcllm_cuda_matvec_hostio(int ggml_type, const void* w, uint32_t rows, uint3
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaMemcpyAsync(x_dev, x_host, sizeof(float) * k, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_hostio h2d");
-    int st = arc::matvec_any(ggml_type, false, w, nullptr, rows, k, x_dev, nullptr, 0.f, nullptr, nullptr, y_dev, s);
+    // Pinned (page-locked, device-mapped) y_host: the kernel stores the rows straight into it over
+    // the host link while it streams the weights, as the reference's shaders write their output to
+    // host-visible mapped memory.  Pageable y_host: y_dev, then one device-to-host copy.
+    cudaPointerAttributes at{};
+    const bool mapped = cudaPointerGetAttributes(&at, y_host) == cudaSuccess && at.type == cudaMemoryTypeHost &&
+                        at.devicePointer != nullptr;
+    if (!mapped) cudaGetLastError();  // clear a lookup failure of an unregistered pointer
+    float* y_out = mapped ? static_cast<float*>(at.devicePointer) : y_dev;
+    int st = arc::matvec_any(ggml_type, false, w, nullptr, rows, k, x_dev, nullptr, 0.f, nullptr, nullptr, y_out, s);
     if (st != ARC_OK) return st;
-    e = cudaMemcpyAsync(y_host, y_dev, sizeof(float) * rows, cudaMemcpyDeviceToHost, s);
-    if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_hostio d2h");
+    if (!mapped) {
+        e = cudaMemcpyAsync(y_host, y_dev, sizeof(float) * rows, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_hostio d2h");
+    }
     e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_hostio sync");
     return ARC_OK;

@@ -478,7 +478,8 @@ def main(argv=None):
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
                     "api": ("arcllm_cuda_memcpy_h2d + arcllm_cuda_matvec_allgather + arcllm_cuda_memcpy_d2h of all "
                             "logits + stream sync" if rg is not None else
-                            "arcllm_cuda_matvec_hostio (pinned host x in, logits out, stream sync)")},
+                            "arcllm_cuda_matvec_hostio (pinned host x copied in, logits stored by the kernel into "
+                            "pinned mapped host memory, stream sync)")},
             "gpu_launches": args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,

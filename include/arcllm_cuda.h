@@ -103,9 +103,12 @@ ARCLLM_CUDA_API int arcllm_cuda_matvec_q6k(const void *w, uint32_t rows, uint32_
 /* End-to-end form for callers that hold HOST activations (the reference's
  * flow: input written to mapped memory, one submit, fence wait, logits read
  * back -- src/arcllm_v1_runtime.cpp:440-446):  copies k floats x_host ->
- * x_dev, runs arcllm_cuda_matvec (no norm/bias/residual), copies rows floats
- * y_dev -> y_host and waits for `stream`.  x_dev / y_dev are caller-owned
- * device buffers; host buffers should be pinned for asynchronous copies. */
+ * x_dev, runs arcllm_cuda_matvec (no norm/bias/residual), delivers the rows
+ * floats to y_host and waits for `stream`.  x_dev / y_dev are caller-owned
+ * device buffers.  A pinned (page-locked, hence device-mapped) y_host is
+ * written by the kernel itself while it runs, as the reference reads logits
+ * from host-visible mapped memory; a pageable y_host gets y_dev copied to it
+ * after the kernel.  x_host should be pinned for an asynchronous copy. */
 ARCLLM_CUDA_API int arcllm_cuda_matvec_hostio(int ggml_type, const void *w, uint32_t rows, uint32_t k,
                                               const float *x_host, float *x_dev, float *y_dev, float *y_host,
                                               void *stream);

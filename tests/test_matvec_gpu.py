@@ -306,3 +306,23 @@ def test_matvec_nonfinite_x_propagates(fmt, bad):
     assert not np.isfinite(y_ref).any()
     assert not np.isfinite(y).any()
     G.check_device_error()
+
+
+@pytest.mark.parametrize("pinned", [True, False])
+def test_matvec_hostio_pinned_and_pageable(pinned):
+    """arcllm_cuda_matvec_hostio: a pinned y_host is written by the kernel
+    itself (mapped host memory), a pageable one by a copy afterwards; both
+    hold the device matvec's rows bit for bit."""
+    rows, k, seed = 152064 // 8, 3584, 3131
+    w = gpu_fill("q6k", rows, k, seed)
+    x = O.normal_f32(k, seed + 1)
+    y_ref = run_matvec("q6k", w, rows, k, x)
+    xh = torch.from_numpy(x.copy())
+    yh = torch.full((rows,), float("nan"), dtype=torch.float32)
+    if pinned:
+        xh, yh = xh.pin_memory(), yh.pin_memory()
+    xd, yd = G.empty_f32(k), G.empty_f32(rows)
+    A.call("arcllm_cuda_matvec_hostio", A.GGML_Q6_K, G.ptr(w), rows, k, C.c_void_p(xh.data_ptr()), G.ptr(xd),
+           G.ptr(yd), C.c_void_p(yh.data_ptr()), G.stream())
+    assert np.array_equal(yh.numpy().view(np.uint32), y_ref.view(np.uint32))
+    G.check_device_error()
