@@ -15,12 +15,20 @@
 //                     src/p8c_segmented_access_correctness.cpp:1136-1158) as
 //                     split-KV: each CTA takes one KV head and a slice of the
 //                     positions for all q heads of that group, keeps an online
-//                     softmax, and a merge pass combines the slices.
+//                     softmax, and a merge pass combines the slices.  With
+//                     at most 16 slices the slices of one KV head form a
+//                     thread-block cluster and merge through distributed
+//                     shared memory inside the same kernel (same arithmetic
+//                     and order as the separate merge kernel, one launch less
+//                     per layer).
 //   argmax_key /      greedy select (src/arcllm_v1_runtime.cpp:132-148):
 //   greedy_finalize   first index of the maximum over finite logits, as a
 //                     packed 64-bit key reduced with atomicMax; a one-thread
 //                     kernel turns it into the next token on the device.
 #include <cfloat>
+#include <cstdlib>
+
+#include <cooperative_groups.h>
 
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
@@ -119,15 +127,61 @@ __global__ void rope_kv_store_kernel(float* __restrict__ q, float* __restrict__ 
     }
 }
 
+// Slices actually holding positions when n positions are split n_splits ways.
+__device__ __forceinline__ uint32_t attn_used_slices(uint32_t n, uint32_t n_splits) {
+    const uint32_t chunk = (n + n_splits - 1u) / n_splits;
+    return (n + chunk - 1u) / chunk;
+}
+
+// Merge the `used` slices of one output (q head, dim): an online merge over
+// chunks of 8 slices whose (max, sum, acc) loads are all issued before any is
+// used.  slice(sp, m, l, a) loads slice sp's values.
+template <typename Slice>
+__device__ __forceinline__ float attn_merge_slices(uint32_t used, Slice slice) {
+    constexpr int CH = 8;
+    float M = -FLT_MAX, L = 0.f, A = 0.f;
+    for (uint32_t sp0 = 0; sp0 < used; sp0 += CH) {
+        float mm[CH], ll[CH], aa[CH];
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+            const uint32_t sp = sp0 + j;
+            if (sp < used) {
+                slice(sp, mm[j], ll[j], aa[j]);
+            } else {
+                mm[j] = -FLT_MAX, ll[j] = 0.f, aa[j] = 0.f;
+            }
+        }
+        float cm = M;
+#pragma unroll
+        for (int j = 0; j < CH; ++j) cm = fmaxf(cm, mm[j]);
+        const float r = __expf(M - cm);
+        L *= r;
+        A *= r;
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+            const float f = __expf(mm[j] - cm);
+            L = fmaf(ll[j], f, L);
+            A = fmaf(aa[j], f, A);
+        }
+        M = cm;
+    }
+    return A / L;
+}
+
 // Split-KV attention, one CTA per (slice, kv head).  Warps stride over the
 // slice's positions; each lane owns 4 of the 128 head dims, holds all G q
 // heads of the group in registers, and keeps an online softmax per head.
-template <int GQ>
+// CLUSTER: the kv head's slices are one thread-block cluster (grid.x =
+// n_splits <= 16); each CTA leaves its slice result in shared memory, the
+// cluster synchronises, and CTA c of C merges outputs 256c + 256C*j + t of the
+// kv head from all slices' shared memory, writing `out` directly.  Otherwise the
+// slice results go to `part` for attn_merge_kernel.
+template <int GQ, bool CLUSTER>
 __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restrict__ q,
                                                            const uint16_t* __restrict__ kc,
                                                            const uint16_t* __restrict__ vc,
                                                            const uint32_t* __restrict__ pos_src, AttnShape s,
-                                                           float* __restrict__ part) {
+                                                           float* __restrict__ part, float* __restrict__ out) {
     pdl_trigger();
     pdl_wait();  // inputs come from the preceding kernels
     constexpr int D = 128, NW = 8;
@@ -187,6 +241,7 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
         *reinterpret_cast<float4*>(&sm_acc[warp][g][lane * 4u]) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
     }
     __syncthreads();
+    __shared__ float res[CLUSTER ? GQ : 1][D + 2];  // this slice's (max, sum, acc[128]) per q head
     // combine the 8 warps: thread (g, d) for g < GQ, d < 128 (GQ*128 <= 1024, two passes of 256 threads... )
     for (uint32_t idx = threadIdx.x; idx < GQ * D; idx += 256u) {
         const uint32_t g = idx / D, d = idx - g * D;
@@ -200,52 +255,40 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
             L = fmaf(sm_l[w][g], f, L);
             A = fmaf(sm_acc[w][g][d], f, A);
         }
-        float* o = part + (((uint64_t)kvh * s.n_splits + split) * GQ + g) * (D + 2u);
+        float* o = CLUSTER ? &res[g][0] : part + (((uint64_t)kvh * s.n_splits + split) * GQ + g) * (D + 2u);
         o[2 + d] = A;
         if (d == 0) o[0] = M, o[1] = L;
     }
+    if constexpr (CLUSTER) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();  // every slice's result is in its CTA's shared memory
+        const uint32_t used = attn_used_slices(n, s.n_splits);
+        for (uint32_t o = cl.block_rank() * 256u + threadIdx.x; o < GQ * D; o += cl.num_blocks() * 256u) {
+            const uint32_t g = o / D, d = o - g * D;
+            out[(kvh * GQ + g) * D + d] = attn_merge_slices(used, [&](uint32_t sp, float& mm, float& ll, float& aa) {
+                const float* r = cl.map_shared_rank(&res[g][0], sp);
+                mm = r[0], ll = r[1], aa = r[2 + d];
+            });
+        }
+        cl.sync();  // no CTA leaves while the others still read its shared memory
+    }
 }
 
-// Merge the slices of one q head: an online merge over chunks of 8 slices
-// whose (max, sum, acc) loads are all issued before any is used.
+// Merge the slices of one q head (the form without a cluster).
 __global__ void attn_merge_kernel(const float* __restrict__ part, const uint32_t* __restrict__ pos_src, AttnShape s,
                                   uint32_t gq, float* __restrict__ out) {
     pdl_trigger();
     pdl_wait();  // inputs come from the preceding kernels
-    constexpr int D = 128, CH = 8;
+    constexpr int D = 128;
     const uint32_t qh = blockIdx.x, d = threadIdx.x;
     const uint32_t kvh = qh / gq, g = qh - kvh * gq;
     const uint32_t n = min(*pos_src, s.max_ctx - 1u) + 1u;
-    const uint32_t chunk = (n + s.n_splits - 1u) / s.n_splits;
-    const uint32_t used = (n + chunk - 1u) / chunk;
-    float M = -FLT_MAX, L = 0.f, A = 0.f;
-    for (uint32_t sp0 = 0; sp0 < used; sp0 += CH) {
-        float mm[CH], ll[CH], aa[CH];
-#pragma unroll
-        for (int j = 0; j < CH; ++j) {
-            const uint32_t sp = sp0 + j;
-            if (sp < used) {
-                const float* pp = part + (((uint64_t)kvh * s.n_splits + sp) * gq + g) * (D + 2u);
-                mm[j] = pp[0], ll[j] = pp[1], aa[j] = pp[2 + d];
-            } else {
-                mm[j] = -FLT_MAX, ll[j] = 0.f, aa[j] = 0.f;
-            }
-        }
-        float cm = M;
-#pragma unroll
-        for (int j = 0; j < CH; ++j) cm = fmaxf(cm, mm[j]);
-        const float r = __expf(M - cm);
-        L *= r;
-        A *= r;
-#pragma unroll
-        for (int j = 0; j < CH; ++j) {
-            const float f = __expf(mm[j] - cm);
-            L = fmaf(ll[j], f, L);
-            A = fmaf(aa[j], f, A);
-        }
-        M = cm;
-    }
-    out[qh * D + d] = A / L;
+    out[qh * D + d] = attn_merge_slices(attn_used_slices(n, s.n_splits), [&](uint32_t sp, float& mm, float& ll,
+                                                                            float& aa) {
+        const float* pp = part + (((uint64_t)kvh * s.n_splits + sp) * gq + g) * (D + 2u);
+        mm = pp[0], ll = pp[1], aa = pp[2 + d];
+    });
 }
 
 // orderable encoding of a float: larger float -> larger unsigned; -0.0 and
@@ -315,12 +358,23 @@ int decode_ops_prepare() {
     cudaError_t e = cudaFuncGetAttributes(&a, embed_f16_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, embed_q4k_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, rope_kv_store_kernel);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<1>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<2>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<4>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<7>);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<8>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<1, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<2, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<4, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<7, false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_partial_kernel<8, false>);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, attn_merge_kernel);
+    // clusters of up to 16 slices (16 is beyond the portable 8: opt in per kernel)
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_partial_kernel<1, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_partial_kernel<2, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_partial_kernel<4, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_partial_kernel<7, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_partial_kernel<8, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, argmax_key_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, greedy_finalize_kernel);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "decode ops prepare");
@@ -357,6 +411,73 @@ int launch_rope_kv_store(float* q, float* k, const float* v, const float2* table
                           "rope_kv_store launch");
 }
 
+namespace {
+
+// The cluster form: one launch, grid (n_splits, kv_heads), clusters of n_splits CTAs.
+template <int GQ>
+cudaError_t launch_attn_cluster(dim3 grid, cudaStream_t stream, const float* q, const uint16_t* kc,
+                                const uint16_t* vc, const uint32_t* pos_src, const AttnShape& s, float* out) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = grid.x;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (pdl_enabled()) {
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 2;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_partial_kernel<GQ, true>, q, kc, vc, pos_src, s,
+                                             static_cast<float*>(nullptr), out);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+// Whether clusters of `size` CTAs of the GQ cluster kernel fit on this device (asked once per
+// device and size; ARCLLM_ATTN_CLUSTER=0 turns the cluster form off).
+template <int GQ>
+bool attn_cluster_ok(uint32_t size, uint32_t kv_heads) {
+    static int known[64][17] = {};  // 0 unknown, 1 yes, 2 no
+    if (size < 2u || size > 16u || kv_heads == 0u) return false;
+    if (const char* v = std::getenv("ARCLLM_ATTN_CLUSTER"))
+        if (v[0] == '0') return false;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int& k = known[dev & 63][size];
+    if (k == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(size, kv_heads);
+        cfg.blockDim = dim3(256);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = size;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, attn_partial_kernel<GQ, true>, &cfg);
+        if (e != cudaSuccess) cudaGetLastError();
+        k = (e == cudaSuccess && n > 0) ? 1 : 2;
+    }
+    return k == 1;
+}
+
+template <int GQ>
+cudaError_t launch_attn_gq(dim3 grid, cudaStream_t stream, const float* q, const uint16_t* kc, const uint16_t* vc,
+                           const uint32_t* pos_src, const AttnShape& s, float* part, float* out, bool* clustered) {
+    *clustered = attn_cluster_ok<GQ>(s.n_splits, s.kv_heads);
+    if (*clustered) return launch_attn_cluster<GQ>(grid, stream, q, kc, vc, pos_src, s, out);
+    return launch_kernel(attn_partial_kernel<GQ, false>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part, out);
+}
+
+}  // namespace
+
 int launch_attention(const float* q, const uint16_t* kc, const uint16_t* vc, const uint32_t* pos_src,
                      const AttnShape& s, float* part, float* out, cudaStream_t stream) {
     if (s.head_dim != 128u) return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: head_dim must be 128");
@@ -365,16 +486,32 @@ int launch_attention(const float* q, const uint16_t* kc, const uint16_t* vc, con
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: q_heads must be 1..8 x kv_heads");
     dim3 grid(s.n_splits, s.kv_heads);
     cudaError_t e;
+    bool clustered = false;
     switch (gq) {
-        case 1: e = launch_kernel(attn_partial_kernel<1>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
-        case 2: e = launch_kernel(attn_partial_kernel<2>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
-        case 4: e = launch_kernel(attn_partial_kernel<4>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
-        case 7: e = launch_kernel(attn_partial_kernel<7>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
-        case 8: e = launch_kernel(attn_partial_kernel<8>, grid, dim3(256), 0, stream, q, kc, vc, pos_src, s, part); break;
+        case 1: e = launch_attn_gq<1>(grid, stream, q, kc, vc, pos_src, s, part, out, &clustered); break;
+        case 2: e = launch_attn_gq<2>(grid, stream, q, kc, vc, pos_src, s, part, out, &clustered); break;
+        case 4: e = launch_attn_gq<4>(grid, stream, q, kc, vc, pos_src, s, part, out, &clustered); break;
+        case 7: e = launch_attn_gq<7>(grid, stream, q, kc, vc, pos_src, s, part, out, &clustered); break;
+        case 8: e = launch_attn_gq<8>(grid, stream, q, kc, vc, pos_src, s, part, out, &clustered); break;
         default: return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: q heads per kv head must be 1, 2, 4, 7 or 8");
     }
-    if (e == cudaSuccess) e = launch_kernel(attn_merge_kernel, dim3(s.q_heads), dim3(128), 0, stream, part, pos_src, s, gq, out);
+    if (e == cudaSuccess && !clustered)
+        e = launch_kernel(attn_merge_kernel, dim3(s.q_heads), dim3(128), 0, stream, part, pos_src, s, gq, out);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "attention launch");
+}
+
+int attention_launches(uint32_t n_splits, uint32_t q_heads, uint32_t kv_heads) {
+    const uint32_t gq = kv_heads ? q_heads / kv_heads : 0u;
+    bool c = false;
+    switch (gq) {
+        case 1: c = attn_cluster_ok<1>(n_splits, kv_heads); break;
+        case 2: c = attn_cluster_ok<2>(n_splits, kv_heads); break;
+        case 4: c = attn_cluster_ok<4>(n_splits, kv_heads); break;
+        case 7: c = attn_cluster_ok<7>(n_splits, kv_heads); break;
+        case 8: c = attn_cluster_ok<8>(n_splits, kv_heads); break;
+        default: break;
+    }
+    return c ? 1 : 2;
 }
 
 int launch_argmax(const float* logits, uint32_t n, unsigned long long* key, uint32_t* nonfinite,

@@ -39,6 +39,8 @@ int launch_embed_rows(int type, const void* table, const uint32_t* token_src, ui
 int launch_rope_kv_store(float* q, float* k, const float* v, const float2* table, const uint32_t* pos_src,
                          uint16_t* kc, uint16_t* vc, const RopeKvShape& s, cudaStream_t stream);
 // part: scratch of kv_heads * n_splits * (q_heads/kv_heads) * (head_dim + 2) floats
+// kernel launches one launch_attention call makes (1: slices merged in their cluster, 2: slices + merge)
+int attention_launches(uint32_t n_splits, uint32_t q_heads, uint32_t kv_heads);
 int launch_attention(const float* q, const uint16_t* kc, const uint16_t* vc, const uint32_t* pos_src,
                      const AttnShape& s, float* part, float* out, cudaStream_t stream);
 // key: max over i of (ordered(logits[i]) << 32 | ~i) via atomicMax (caller zeroes it);

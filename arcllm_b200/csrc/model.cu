@@ -170,7 +170,7 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
         ARC_TRY(matvec_any(ARC_GGML_Q4_K, true, L.w_gate, L.w_up, c.ffn, H, hm, L.ffn_norm, c.rms_eps, nullptr,
                            nullptr, m->s, st));
         ARC_TRY(mv(L.type_down, L.w_down, H, c.ffn, m->s, nullptr, 0.f, nullptr, hm, hc, st));
-        n += 8;
+        n += 6 + (uint32_t)attention_launches(m->attn_splits, c.n_heads, c.n_kv_heads);  // Q K V (attn) O gate/up down
     }
     if (with_head) {
         ARC_TRY(mv(m->out_type, m->out_w, m->lm_rows, H, hc, m->out_norm, c.rms_eps, nullptr, nullptr,

@@ -72,6 +72,29 @@ def test_attention_decode(pos, splits):
     assert np.abs(y - ref).max() <= 1e-4 * 4.0
 
 
+@pytest.mark.parametrize("pos,splits", [(5, 16), (300, 16), (4095, 16), (37, 3), (1000, 8)])
+def test_attention_cluster_merge_bit_identical(pos, splits, monkeypatch):
+    """Slices merged through distributed shared memory inside their cluster
+    equal the separate merge kernel's output bit for bit."""
+    QH, KVH, D, MC, layers, layer = 28, 4, 128, 4096, 2, 1
+    KV = KVH * D
+    kc = O.normal_f32(layers * MC * KV, 40 + pos, 0.0, 1.0).astype(np.float16)
+    vc = O.normal_f32(layers * MC * KV, 41 + pos, 0.0, 1.0).astype(np.float16)
+    q = O.normal_f32(QH * D, 42 + pos, 0.0, 1.0)
+    kcd, vcd, qd = G.to_dev(kc.view(np.uint16)), G.to_dev(vc.view(np.uint16)), G.to_dev(q)
+    posd = G.to_dev(np.array([pos], np.uint32))
+    scratch = G.empty_f32(KVH * splits * (QH // KVH) * (D + 2))
+    outs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("ARCLLM_ATTN_CLUSTER", flag)
+        out = G.empty_f32(QH * D)
+        A.call("arcllm_cuda_attention_decode", G.ptr(qd), G.ptr(kcd), G.ptr(vcd), G.ptr(posd), QH, KVH, D, MC,
+               layer, splits, G.ptr(scratch), G.ptr(out), G.stream())
+        outs[flag] = G.host(out)
+    assert np.array_equal(outs["1"].view(np.uint32), outs["0"].view(np.uint32))
+    G.check_device_error()
+
+
 @pytest.mark.parametrize("etype", [A.GGML_F16, A.GGML_Q4_K])
 def test_embed(etype):
     V, H, tok = 1000, 512, 777
@@ -169,7 +192,8 @@ def test_generate_matches_stepwise_and_reports_stats():
             ref.append(O.argmax(m.logits())[0])
     assert toks == ref
     assert st.finite == 1 and st.decode_steps == 7 and st.prefill_graph_launches == 8
-    assert st.decode_launches_per_step == 1 + 8 * SMALL["n_layers"] + 3  # RoPE + KV store fused into Q/K/V
+    # RoPE + KV store fused into Q/K/V, attention slices merged inside their cluster
+    assert st.decode_launches_per_step == 1 + 7 * SMALL["n_layers"] + 3
     assert st.decode_graph_launches_per_step == 1
     m.close()
 
@@ -202,7 +226,7 @@ def test_fused_rope_kv_epilogue_bit_identical(monkeypatch):
         m.close()
     a, b = out["1"], out["0"]
     assert a[0] == b[0]
-    assert a[1] == 1 + 8 * SMALL["n_layers"] + 3 and b[1] == 1 + 9 * SMALL["n_layers"] + 3
+    assert a[1] == 1 + 7 * SMALL["n_layers"] + 3 and b[1] == 1 + 8 * SMALL["n_layers"] + 3
     assert np.array_equal(a[2].view(np.uint32), b[2].view(np.uint32))
     for l in range(2):
         for j in range(2):

@@ -62,7 +62,7 @@ def test_generate_cli_matches_oracle(tmp_path, emb):
     assert len(toks) == 6 and s["finite"] is True
     assert s["decode_steps"] == 5 and s["route_a_steps"] == 5 and s["route_b_steps"] == 0
     assert s["prefill_submits"] == len(prompt) and s["decode_submits_per_step"] == 1
-    assert s["decode_dispatches_per_step"] == 1 + 8 * SMALL["n_layers"] + 3  # RoPE + KV store fused
+    assert s["decode_dispatches_per_step"] == 1 + 7 * SMALL["n_layers"] + 3  # RoPE + KV fused, clustered attention
     # the same weights filled on the device through the C ABI decode to the same tokens
     from arcllm_b200.synthetic import SyntheticModel
     m = SyntheticModel(SMALL, types=types, seed=seed)
