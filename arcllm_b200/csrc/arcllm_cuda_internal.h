@@ -102,9 +102,8 @@ bool matvec_splitk_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
 int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, const float* x, const float* gamma,
                          float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
 // Pick the kernel for a matvec: the integer tensor-core forms where they
-// apply (whole rows for K <= 3584, K slices for Q4_K with K > 3584), else the
-// CUDA-core streaming form (ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core
-// form, =splitk also sends Q6_K with K > 3584 to the K-slice form).
+// apply (whole rows for K <= 3584, K slices for K > 3584), else the CUDA-core
+// streaming form (ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core form).
 int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                const float* gamma, float eps, const float* bias, const float* residual, float* y,
                cudaStream_t stream);
