@@ -12,9 +12,10 @@
 //                       token-by-token path would store the same inputs);
 //   attention_prefill   causal GQA attention, query row t over positions
 //                       0 .. pos0+t of the cache (shaders/p7_attention_prefill_online.comp,
-//                       CPU form p8c...:1136-1158), one CTA per (row, KV head)
-//                       with the group's q heads in registers and an online
-//                       softmax; the result is written as bf16 for the O GEMM;
+//                       CPU form p8c...:1136-1158) on the tensor cores: per
+//                       warp a 16-row tile of (query row, q head) pairs of one
+//                       KV head, flash-attention style over 16-position tiles
+//                       of the cache; the result is written as bf16 for the O GEMM;
 //   silu_mul_rows_bf16  s = silu(g) * u (p8c...:1064-1073), bf16 for the down GEMM.
 #include <algorithm>
 #include <cfloat>
@@ -93,82 +94,191 @@ __global__ void rope_kv_rows_kernel(float* __restrict__ q, float* __restrict__ k
     }
 }
 
-// Causal attention for query row t (blockIdx.x) and KV head blockIdx.y over
-// positions 0 .. pos0+t.  Warps stride over positions; lane L owns head dims
-// 4L..4L+3 of all GQ q heads of the group; the 8 warps' online-softmax states
-// are combined in shared memory at the end (in warp order).
+// D += A * B, m16n8k16, fp16 operands, fp32 accumulators
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(p)));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_addr(p)));
+}
+
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// 16-byte global -> shared copy that bypasses L1 (cp.async, completion by group)
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Causal attention of query rows r over cache positions 0 .. pos0+r on the
+// tensor cores (flash-attention tiling).  A warp owns a 16-row A tile: RQ
+// consecutive query rows x the GQ q heads of KV head blockIdx.y (GQ = 7 is
+// padded to 8 rows per query row).  It walks the positions in tiles of 16:
+// K and V tiles are copied into shared memory with cp.async (two buffers,
+// the next tile in flight while this one is used), S = Q K^T comes from
+// ldmatrix B fragments and m16n8k16 MMAs, the online softmax runs on the S
+// fragments, and O += P V takes P straight from those registers with V
+// fragments from ldmatrix.trans.  Q enters as a pair of fp16 halves (q*scale
+// = hi + lo), so S is exact to about 2^-22 of |q| |k| (the cache is fp16
+// already): scores of the near-one-hot synthetic models stay as sharp as in
+// fp32.  P enters the P V product as fp16 (11 bits, the output is bf16).
+// |q| * scale must stay inside the fp16 range (< 65504).
 template <int GQ>
-__global__ void __launch_bounds__(256) attention_prefill_kernel(const float* __restrict__ q,
-                                                                const uint16_t* __restrict__ kc,
-                                                                const uint16_t* __restrict__ vc, uint32_t pos0,
-                                                                AttnShape s, uint16_t* __restrict__ out) {
-    constexpr int D = 128, NW = 8;
-    __shared__ float sm_m[NW][GQ], sm_l[NW][GQ];
-    __shared__ float sm_acc[NW][GQ][D];
-    const uint32_t t = blockIdx.x, kvh = blockIdx.y;
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t n = pos0 + t + 1u;
-    const uint32_t hdim = s.q_heads * D, kv_dim = s.kv_heads * D;
-    float qv[GQ][4];
+__global__ void __launch_bounds__(64) attention_prefill_kernel(const float* __restrict__ q,
+                                                               const uint16_t* __restrict__ kc,
+                                                               const uint16_t* __restrict__ vc, uint32_t pos0,
+                                                               uint32_t T, AttnShape s, uint16_t* __restrict__ out) {
+    constexpr int D = 128, GP = GQ == 7 ? 8 : GQ, RQ = 16 / GP, NWARP = 2, PT = 16;
+    constexpr uint32_t ROWB = D * 2 + 16;  // bytes per cached row in smem (padding: conflict-free ldmatrix)
+    __shared__ __align__(128) uint8_t sm[NWARP][2][2][PT * ROWB];  // [warp][buffer][K, V][position row]
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, g = lane >> 2, t = lane & 3u;
+    const uint32_t r0 = (blockIdx.x * NWARP + warp) * RQ;
+    if (r0 >= T) return;  // warp-level work only: no CTA barrier below
+    const uint32_t kvh = blockIdx.y, hdim = s.q_heads * D, kv_dim = s.kv_heads * D;
+    const uint32_t p_hi = pos0 + min(r0 + (uint32_t)RQ, T) - 1u;  // last position this warp's rows see
+    // rows g and g + 8 of the A tile
+    uint32_t qrow[2], head[2], lim[2];
+    bool valid[2];
 #pragma unroll
-    for (int g = 0; g < GQ; ++g) {
-        const float4 a = *reinterpret_cast<const float4*>(q + (uint64_t)t * hdim + (kvh * GQ + g) * D + lane * 4u);
-        qv[g][0] = a.x * s.scale, qv[g][1] = a.y * s.scale, qv[g][2] = a.z * s.scale, qv[g][3] = a.w * s.scale;
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t ri = g + 8u * h, qr = r0 + ri / GP;
+        head[h] = ri % GP;
+        valid[h] = head[h] < (uint32_t)GQ && qr < T;
+        qrow[h] = min(qr, T - 1u);
+        lim[h] = pos0 + qrow[h];
     }
-    float m[GQ], l[GQ], acc[GQ][4];
+    // Q fragments, hi and lo fp16 halves of q * scale; register h + 2j of k-step kk holds
+    // row g + 8h, dims 16kk + 2t + 8j, +1
+    uint32_t qa[8][4], qb[8][4];
 #pragma unroll
-    for (int g = 0; g < GQ; ++g) {
-        m[g] = -FLT_MAX, l[g] = 0.f;
-        acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
-    }
-    const uint64_t lbase = (uint64_t)s.layer * s.max_ctx * kv_dim + kvh * D + lane * 4u;
-    for (uint32_t p = warp; p < n; p += NW) {
-        const uint2 kraw = *reinterpret_cast<const uint2*>(kc + lbase + (uint64_t)p * kv_dim);
-        const uint2 vraw = *reinterpret_cast<const uint2*>(vc + lbase + (uint64_t)p * kv_dim);
-        const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kraw.x));
-        const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kraw.y));
-        const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vraw.x));
-        const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vraw.y));
-        float sc[GQ];
+    for (int kk = 0; kk < 8; ++kk)
 #pragma unroll
-        for (int g = 0; g < GQ; ++g)
-            sc[g] = fmaf(qv[g][0], k01.x, fmaf(qv[g][1], k01.y, fmaf(qv[g][2], k23.x, qv[g][3] * k23.y)));
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
+            for (int j = 0; j < 2; ++j) {
+                float2 v = make_float2(0.f, 0.f);
+                if (valid[h])
+                    v = *reinterpret_cast<const float2*>(q + (uint64_t)qrow[h] * hdim + (kvh * GQ + head[h]) * D +
+                                                         16u * kk + 2u * t + 8u * j);
+                v.x *= s.scale, v.y *= s.scale;
+                const __half2 hi = __floats2half2_rn(v.x, v.y);
+                const float2 hf = __half22float2(hi);
+                qa[kk][h + 2 * j] = *reinterpret_cast<const uint32_t*>(&hi);
+                qb[kk][h + 2 * j] = pack_f16(v.x - hf.x, v.y - hf.y);
+            }
+    float o[16][4];
 #pragma unroll
-            for (int g = 0; g < GQ; ++g) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], o);
+    for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    const uint64_t lbase = (uint64_t)s.layer * s.max_ctx * kv_dim + kvh * D;
+    auto issue = [&](uint32_t tile, int buf) {  // K and V rows of positions tile*16 .. +15 (clamped)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t c = lane + 32u * j, row = c >> 4, ch = c & 15u;
+            const uint32_t pos = min(tile * PT + row, p_hi);
+            const uint64_t src = lbase + (uint64_t)pos * kv_dim + ch * 8u;
+            cp_async_16(&sm[warp][buf][0][row * ROWB + ch * 16u], kc + src);
+            cp_async_16(&sm[warp][buf][1][row * ROWB + ch * 16u], vc + src);
         }
-#pragma unroll
-        for (int g = 0; g < GQ; ++g) {
-            const float mn = fmaxf(m[g], sc[g]);
-            const float a = __expf(m[g] - mn), pr = __expf(sc[g] - mn);
-            l[g] = fmaf(l[g], a, pr);
-            acc[g][0] = fmaf(acc[g][0], a, pr * v01.x);
-            acc[g][1] = fmaf(acc[g][1], a, pr * v01.y);
-            acc[g][2] = fmaf(acc[g][2], a, pr * v23.x);
-            acc[g][3] = fmaf(acc[g][3], a, pr * v23.y);
-            m[g] = mn;
+        cp_async_commit();
+    };
+    const uint32_t ntiles = p_hi / PT + 1u;
+    issue(0, 0);
+    for (uint32_t tile = 0; tile < ntiles; ++tile) {
+        const int buf = tile & 1u;
+        if (tile + 1u < ntiles) {
+            issue(tile + 1u, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
+        __syncwarp();
+        const uint8_t* Ks = sm[warp][buf][0];
+        const uint8_t* Vs = sm[warp][buf][1];
+        const uint32_t mi = lane >> 3, mr = lane & 7u;  // ldmatrix: matrix and row this lane addresses
+        float sc[2][4];
+#pragma unroll
+        for (int pb = 0; pb < 2; ++pb) {
+            sc[pb][0] = sc[pb][1] = sc[pb][2] = sc[pb][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < 8; kk += 2) {
+                uint32_t b[4];
+                ldsm_x4(b, Ks + (8u * pb + mr) * ROWB + 2u * (16u * (kk + (mi >> 1)) + 8u * (mi & 1u)));
+                mma_f16_16816(sc[pb], qa[kk], b[0], b[1]);
+                mma_f16_16816(sc[pb], qb[kk], b[0], b[1]);
+                mma_f16_16816(sc[pb], qa[kk + 1], b[2], b[3]);
+                mma_f16_16816(sc[pb], qb[kk + 1], b[2], b[3]);
+            }
+        }
+        // causal mask and online softmax; element c of block pb: row g + 8(c >> 1), position 8pb + 2t + (c & 1)
+        const uint32_t p0 = tile * PT;
+#pragma unroll
+        for (int pb = 0; pb < 2; ++pb)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                if (p0 + 8u * pb + 2u * t + (c & 1) > lim[c >> 1]) sc[pb][c] = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float mx = fmaxf(fmaxf(sc[0][2 * h], sc[0][2 * h + 1]), fmaxf(sc[1][2 * h], sc[1][2 * h + 1]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mn = fmaxf(m[h], mx);
+            const float alpha = __expf(m[h] - mn);
+            m[h] = mn;
+            float ps = 0.f;
+#pragma unroll
+            for (int pb = 0; pb < 2; ++pb)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    sc[pb][2 * h + c] = __expf(sc[pb][2 * h + c] - mn);
+                    ps += sc[pb][2 * h + c];
+                }
+            ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+            l[h] = fmaf(l[h], alpha, ps);
+#pragma unroll
+            for (int nt = 0; nt < 16; ++nt) o[nt][2 * h] *= alpha, o[nt][2 * h + 1] *= alpha;
+        }
+        // O += P V with P (16 rows x 16 positions) from the S fragments
+        const uint32_t pa[4] = {pack_f16(sc[0][0], sc[0][1]), pack_f16(sc[0][2], sc[0][3]),
+                                pack_f16(sc[1][0], sc[1][1]), pack_f16(sc[1][2], sc[1][3])};
+#pragma unroll
+        for (int nt = 0; nt < 16; nt += 2) {
+            uint32_t v[4];
+            ldsm_x4_trans(v, Vs + (8u * (mi & 1u) + mr) * ROWB + 2u * (8u * (nt + (mi >> 1))));
+            mma_f16_16816(o[nt], pa, v[0], v[1]);
+            mma_f16_16816(o[nt + 1], pa, v[2], v[3]);
+        }
+        __syncwarp();  // this buffer is refilled two tiles later
     }
 #pragma unroll
-    for (int g = 0; g < GQ; ++g) {
-        if (lane == 0) sm_m[warp][g] = m[g], sm_l[warp][g] = l[g];
-        *reinterpret_cast<float4*>(&sm_acc[warp][g][lane * 4u]) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-    }
-    __syncthreads();
-    for (uint32_t idx = threadIdx.x; idx < GQ * D; idx += 256u) {
-        const uint32_t g = idx / D, d = idx - g * D;
-        float M = -FLT_MAX;
+    for (int h = 0; h < 2; ++h) {
+        if (!valid[h]) continue;
+        uint16_t* dst = out + (uint64_t)qrow[h] * hdim + (kvh * GQ + head[h]) * D + 2u * t;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][g]);
-        float L = 0.f, Acc = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            const float f = __expf(sm_m[w][g] - M);
-            L = fmaf(sm_l[w][g], f, L);
-            Acc = fmaf(sm_acc[w][g][d], f, Acc);
+        for (int nt = 0; nt < 16; ++nt) {
+            const uint32_t lo = f2bf(o[nt][2 * h] / l[h]), hi = f2bf(o[nt][2 * h + 1] / l[h]);
+            *reinterpret_cast<uint32_t*>(dst + 8u * nt) = lo | (hi << 16);
         }
-        out[(uint64_t)t * hdim + (kvh * GQ + g) * D + d] = f2bf(Acc / L);
     }
 }
 
@@ -221,16 +331,21 @@ int launch_attention_prefill(const float* q, const uint16_t* kc, const uint16_t*
     if (rows == 0) return ARC_OK;
     if (s.head_dim != 128u) return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: head_dim must be 128");
     if (pos0 + rows > s.max_ctx) return set_error(ARC_E_INVALID_ARGUMENT, "attention: positions past the context");
+    if (((reinterpret_cast<uintptr_t>(kc) | reinterpret_cast<uintptr_t>(vc)) & 15u) ||
+        (reinterpret_cast<uintptr_t>(q) & 7u) || (reinterpret_cast<uintptr_t>(out) & 3u))
+        return set_error(ARC_E_ALIGNMENT, "attention prefill: caches 16-byte, q 8-byte, out 4-byte aligned");
     const uint32_t gq = s.q_heads / s.kv_heads;
     if (gq * s.kv_heads != s.q_heads) return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: q_heads % kv_heads");
-    const dim3 grid(rows, s.kv_heads);
+    // two warps per CTA, each 16 / (q heads per KV head, 7 -> 8) query rows
+    const uint32_t rq = 16u / (gq == 7u ? 8u : gq);
+    const dim3 grid((rows + 2u * rq - 1u) / (2u * rq), s.kv_heads);
     cudaError_t e;
     switch (gq) {
-        case 1: e = launch_kernel(attention_prefill_kernel<1>, grid, dim3(256), 0, stream, q, kc, vc, pos0, s, out); break;
-        case 2: e = launch_kernel(attention_prefill_kernel<2>, grid, dim3(256), 0, stream, q, kc, vc, pos0, s, out); break;
-        case 4: e = launch_kernel(attention_prefill_kernel<4>, grid, dim3(256), 0, stream, q, kc, vc, pos0, s, out); break;
-        case 7: e = launch_kernel(attention_prefill_kernel<7>, grid, dim3(256), 0, stream, q, kc, vc, pos0, s, out); break;
-        case 8: e = launch_kernel(attention_prefill_kernel<8>, grid, dim3(256), 0, stream, q, kc, vc, pos0, s, out); break;
+        case 1: e = launch_kernel(attention_prefill_kernel<1>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
+        case 2: e = launch_kernel(attention_prefill_kernel<2>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
+        case 4: e = launch_kernel(attention_prefill_kernel<4>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
+        case 7: e = launch_kernel(attention_prefill_kernel<7>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
+        case 8: e = launch_kernel(attention_prefill_kernel<8>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
         default: return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: q heads per kv head must be 1, 2, 4, 7 or 8");
     }
     return launch_checked(e, "attention prefill launch");
