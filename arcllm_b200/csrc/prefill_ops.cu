@@ -215,20 +215,26 @@ __global__ void __launch_bounds__(64) attention_prefill_kernel(const float* __re
         const uint8_t* Ks = sm[warp][buf][0];
         const uint8_t* Vs = sm[warp][buf][1];
         const uint32_t mi = lane >> 3, mr = lane & 7u;  // ldmatrix: matrix and row this lane addresses
-        float sc[2][4];
+        // S in four independent accumulator chains (position block x hi/lo half of q), summed after
+        float sc[2][4], sl[2][4];
 #pragma unroll
         for (int pb = 0; pb < 2; ++pb) {
             sc[pb][0] = sc[pb][1] = sc[pb][2] = sc[pb][3] = 0.f;
+            sl[pb][0] = sl[pb][1] = sl[pb][2] = sl[pb][3] = 0.f;
 #pragma unroll
             for (int kk = 0; kk < 8; kk += 2) {
                 uint32_t b[4];
                 ldsm_x4(b, Ks + (8u * pb + mr) * ROWB + 2u * (16u * (kk + (mi >> 1)) + 8u * (mi & 1u)));
                 mma_f16_16816(sc[pb], qa[kk], b[0], b[1]);
-                mma_f16_16816(sc[pb], qb[kk], b[0], b[1]);
+                mma_f16_16816(sl[pb], qb[kk], b[0], b[1]);
                 mma_f16_16816(sc[pb], qa[kk + 1], b[2], b[3]);
-                mma_f16_16816(sc[pb], qb[kk + 1], b[2], b[3]);
+                mma_f16_16816(sl[pb], qb[kk + 1], b[2], b[3]);
             }
         }
+#pragma unroll
+        for (int pb = 0; pb < 2; ++pb)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) sc[pb][c] += sl[pb][c];
         // causal mask and online softmax; element c of block pb: row g + 8(c >> 1), position 8pb + 2t + (c & 1)
         const uint32_t p0 = tile * PT;
 #pragma unroll
@@ -282,12 +288,27 @@ __global__ void __launch_bounds__(64) attention_prefill_kernel(const float* __re
     }
 }
 
+__device__ __forceinline__ uint16_t silu_mul_bf16(float a, float u) { return f2bf((a / (1.0f + expf(-a))) * u); }
+
+// Four elements per thread and step (float4 loads, one 8-byte store) when n % 4 == 0
+// and the pointers allow it; otherwise one element at a time.  Same expression per element.
 __global__ void silu_mul_rows_bf16_kernel(const float* __restrict__ g, const float* __restrict__ u, uint64_t n,
                                           uint16_t* __restrict__ out) {
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
-        const float a = g[i];
-        out[i] = f2bf((a / (1.0f + expf(-a))) * u[i]);
+    const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (uint64_t)gridDim.x * blockDim.x;
+    const bool vec = (n % 4u) == 0u && ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u)) & 15u) == 0u &&
+                     (reinterpret_cast<uintptr_t>(out) & 7u) == 0u;
+    if (vec) {
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        const float4* u4 = reinterpret_cast<const float4*>(u);
+        uint2* o4 = reinterpret_cast<uint2*>(out);
+        for (uint64_t i = tid; i < n / 4u; i += stride) {
+            const float4 a = g4[i], b = u4[i];
+            o4[i] = make_uint2((uint32_t)silu_mul_bf16(a.x, b.x) | ((uint32_t)silu_mul_bf16(a.y, b.y) << 16),
+                               (uint32_t)silu_mul_bf16(a.z, b.z) | ((uint32_t)silu_mul_bf16(a.w, b.w) << 16));
+        }
+        return;
     }
+    for (uint64_t i = tid; i < n; i += stride) out[i] = silu_mul_bf16(g[i], u[i]);
 }
 
 // After a batched prefill of positions 0 .. n_prompt-2: the decode graph
@@ -353,7 +374,7 @@ int launch_attention_prefill(const float* q, const uint16_t* kc, const uint16_t*
 
 int launch_silu_mul_rows_bf16(const float* g, const float* u, uint64_t n, uint16_t* out, cudaStream_t stream) {
     if (n == 0) return ARC_OK;
-    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n + 255) / 256, 148u * 16u);
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n / 4u + 255) / 256 + 1u, 148u * 16u);
     return launch_checked(launch_kernel(silu_mul_rows_bf16_kernel, dim3(blocks), dim3(256), 0, stream, g, u, n, out),
                           "silu mul launch");
 }
