@@ -348,6 +348,11 @@ int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
     m->prefill_down_type.assign(c.n_layers, 0);
     m->lm_row0 = 0;
     m->lm_rows = c.vocab;
+    // tuning override for experiments: ARCLLM_ATTN_SPLITS=<KV slices per head> (1 .. 64)
+    if (const char* e = std::getenv("ARCLLM_ATTN_SPLITS")) {
+        const unsigned long v = std::strtoul(e, nullptr, 10);
+        if (v >= 1 && v <= 64) m->attn_splits = (uint32_t)v;
+    }
     const uint32_t gq = c.n_heads / c.n_kv_heads;
     const size_t kv_dim = (size_t)c.n_kv_heads * c.head_dim;
     size_t off = 0;
