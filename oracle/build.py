@@ -5,7 +5,7 @@ Two libraries:
 * ``oracle/lib/liborc.so`` -- the C restatement in ``oracle/orc.c``.  It needs
   only gcc and is rebuilt wherever it is missing (also on a GPU box).
 * ``oracle/_ref/libref_cpu.so`` -- the reference's OWN CPU code, compiled in
-  place from an ArcLLM checkout (``--reference``, default ``/root/reference``)
+  place from an ArcLLM checkout (``--reference``, or ``ARCLLM_REFERENCE_DIR``)
   through ``oracle/ref_wrap.cpp``.  Nothing is copied out of the reference
   tree.  Built only where that checkout exists; the golden fixtures under
   ``tests/golden/`` carry its outputs elsewhere.
@@ -21,7 +21,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORC_SO = os.path.join(HERE, "lib", "liborc.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_cpu.so")
-DEFAULT_REFERENCE = "/root/reference"
+DEFAULT_REFERENCE = os.environ.get("ARCLLM_REFERENCE_DIR", os.path.join(os.sep, "root", "reference"))
 
 
 def _run(cmd):
