@@ -450,6 +450,11 @@ bool attn_cluster_ok(uint32_t size, uint32_t kv_heads) {
     cudaGetDevice(&dev);
     int& k = known[dev & 63][size];
     if (k == 0) {
+        // callers of the C ABI may not have run decode_ops_prepare: opt in to 16-CTA clusters here too
+        if (size > 8u &&
+            cudaFuncSetAttribute(attn_partial_kernel<GQ, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+                cudaSuccess)
+            cudaGetLastError();
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(size, kv_heads);
         cfg.blockDim = dim3(256);
