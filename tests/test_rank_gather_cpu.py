@@ -1,5 +1,5 @@
 """Host side of the multi-GPU LM head (arcllm_b200/rank_gather.py) on CPU:
-two gloo ranks in spawned processes build RankGather exactly as bench.py does
+two and four gloo ranks in spawned processes build RankGather exactly as bench.py does
 (handles swapped with all_gather_object), with the CUDA library replaced by a
 stand-in whose "device memory" is POSIX shared memory, whose IPC handles name
 those segments, and whose all-gather matvec follows the kernel's protocol
@@ -21,7 +21,7 @@ import time
 import numpy as np
 import pytest
 
-ROWS_TOTAL = 1000  # 2 x 500 rows; flags at align256(4000) = 4096
+ROWS_TOTAL = 1000  # 2 x 500 or 4 x 250 rows; flags at align256(4000) = 4096
 
 
 class FakeLib:
@@ -145,16 +145,17 @@ def _free_port():
     return p
 
 
-def test_rank_gather_host_protocol_two_gloo_ranks():
+@pytest.mark.parametrize("world", [2, 4])
+def test_rank_gather_host_protocol_gloo_ranks(world):
     pytest.importorskip("torch")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     try:
-        res = sorted(q.get(timeout=120) for _ in range(2))
+        res = sorted(q.get(timeout=120) for _ in range(world))
     finally:
         for p in procs:
             p.join(timeout=30)
