@@ -18,6 +18,11 @@
 //   * a call needs kv_heads * n_splits * (q_heads / kv_heads) * (head_dim + 2)
 //     floats (58,240 for Qwen2.5-7B with 16 splits); larger requests are
 //     rejected with ARC_E_UNSUPPORTED_SHAPE and nothing is launched;
+//   * the array carries the partials only when the slices are merged by the
+//     separate merge kernel (n_splits == 1 or > 16, no schedulable 16-CTA
+//     cluster, or ARCLLM_ATTN_CLUSTER=0); the clustered form merges through
+//     distributed shared memory and leaves the array untouched.  The size
+//     limit is checked either way, as part of the contract;
 //   * all calls on a device share the one array: calls whose kernels overlap on
 //     the GPU (different streams without ordering) race and corrupt each
 //     other's results.  Calls ordered on one stream are safe;

@@ -25,8 +25,10 @@
 //   greedy_finalize   first index of the maximum over finite logits, as a
 //                     packed 64-bit key reduced with atomicMax; a one-thread
 //                     kernel turns it into the next token on the device.
+#include <atomic>
 #include <cfloat>
 #include <cstdlib>
+#include <mutex>
 
 #include <cooperative_groups.h>
 
@@ -439,17 +441,25 @@ cudaError_t launch_attn_cluster(dim3 grid, cudaStream_t stream, const float* q, 
 }
 
 // Whether clusters of `size` CTAs of the GQ cluster kernel fit on this device (asked once per
-// device and size; ARCLLM_ATTN_CLUSTER=0 turns the cluster form off).
+// device and size under a lock, so host threads making their first call together agree;
+// devices 64 and up take the two-kernel form; ARCLLM_ATTN_CLUSTER=0 turns the cluster form off).
 template <int GQ>
 bool attn_cluster_ok(uint32_t size, uint32_t kv_heads) {
-    static int known[64][17] = {};  // 0 unknown, 1 yes, 2 no
+    static std::atomic<int> known[64][17] = {};  // 0 unknown, 1 yes, 2 no
+    static std::mutex probe_mutex;
     if (size < 2u || size > 16u || kv_heads == 0u) return false;
     if (const char* v = std::getenv("ARCLLM_ATTN_CLUSTER"))
         if (v[0] == '0') return false;
     int dev = 0;
-    cudaGetDevice(&dev);
-    int& k = known[dev & 63][size];
-    if (k == 0) {
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (dev < 0 || dev >= 64) return false;
+    std::atomic<int>& k = known[dev][size];
+    if (k.load(std::memory_order_acquire) == 0) {
+        std::lock_guard<std::mutex> lock(probe_mutex);
+        if (k.load(std::memory_order_relaxed) != 0) return k.load(std::memory_order_relaxed) == 1;
         // callers of the C ABI may not have run decode_ops_prepare: opt in to 16-CTA clusters here too
         if (size > 8u &&
             cudaFuncSetAttribute(attn_partial_kernel<GQ, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
@@ -468,9 +478,9 @@ bool attn_cluster_ok(uint32_t size, uint32_t kv_heads) {
         int n = 0;
         const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, attn_partial_kernel<GQ, true>, &cfg);
         if (e != cudaSuccess) cudaGetLastError();
-        k = (e == cudaSuccess && n > 0) ? 1 : 2;
+        k.store((e == cudaSuccess && n > 0) ? 1 : 2, std::memory_order_release);
     }
-    return k == 1;
+    return k.load(std::memory_order_acquire) == 1;
 }
 
 template <int GQ>

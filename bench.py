@@ -235,9 +235,10 @@ def main(argv=None):
     ap.add_argument("--fmt", default="q6k", choices=["q6k", "q4k"], help="profiling override of the workload")
     ap.add_argument("--rows", type=int, default=LM_ROWS, help="profiling override of the workload")
     ap.add_argument("--k", type=int, default=HIDDEN, help="profiling override of the workload")
-    ap.add_argument("--only", choices=["decode", "prefill", "extra"],
-                    help="profiling: run only the config-3 decode, the config-4 prefill GEMMs or all extra "
-                         "configurations and print the result")
+    ap.add_argument("--only", choices=["decode", "prefill", "extra", "matvec", "gateup"],
+                    help="profiling: run only the config-3 decode, the config-4 prefill GEMMs, all extra "
+                         "configurations, one matvec shape (--fmt/--rows/--k) or the fused gate/up "
+                         "(--rows/--k) over rotating weight copies, and print the result")
     ap.add_argument("--launch", default="graph", choices=["graph", "stream"],
                     help="N=1 headline: the K timed launches captured in one CUDA graph and replayed once "
                          "(default), or launched one by one with per-launch CUDA events")
@@ -257,6 +258,9 @@ def main(argv=None):
         torch.cuda.set_device(0)
         if args.only == "decode":
             res = run_decode(A, torch, measured_peaks()[0], args.decode_prompt, args.decode_new)
+        elif args.only in ("matvec", "gateup"):
+            res = run_one_matvec(A, torch, measured_peaks()[0], args.fmt, args.rows, args.k, args.steps,
+                                 args.warmup, dual=args.only == "gateup")
         else:
             res = run_extra(A, A.lib(), torch, torch.device("cuda", 0),
                             C.c_void_p(torch.cuda.current_stream().cuda_stream), measured_peaks()[0],
@@ -622,6 +626,57 @@ def run_extra(A, L, torch, dev, sp, hbm_peak, which="all"):
     out.update(run_prefill_gemm(A, L, torch, dev, sp, timed, copies, make_w))
     out["config3_decode"] = run_decode(A, torch, hbm_peak)
     return out
+
+
+def run_one_matvec(A, torch, hbm_peak, fmt, rows, k, steps, warmup, dual=False):
+    """One matvec shape (or the fused Q4_K gate/up pair with RMSNorm and
+    SiLU*mul when `dual`) launched `steps` times on one stream over rotating
+    weight copies totalling >= 3x L2, timed with CUDA events around the whole
+    run (for launch lists and single-kernel ncu captures)."""
+    dev = torch.device("cuda", 0)
+    sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    L = A.lib()
+    if dual:
+        fmt = "q4k"
+    nmat = 2 if dual else 1
+    per = nmat * q_bytes(fmt, rows, k)
+    ncop = max(2, -(-3 * L2_BYTES // per))
+    ws = []
+    for c in range(ncop * nmat):
+        t = torch.empty(q_bytes(fmt, rows, k) + 16, dtype=torch.uint8, device=dev)
+        A.call("arcllm_cuda_fill_" + fmt, C.c_void_p(t.data_ptr()), 0, rows * (k // 256), 0x600 + c, sp)
+        ws.append(t)
+    x = torch.empty(k, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(x.data_ptr()), 0, k, 0x7B, C.c_float(0), C.c_float(1), sp)
+    gamma = torch.empty(k, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(gamma.data_ptr()), 0, k, 0x7C, C.c_float(1), C.c_float(0.1), sp)
+    y = torch.empty(rows, dtype=torch.float32, device=dev)
+    ty = A.GGML_Q4_K if fmt == "q4k" else A.GGML_Q6_K
+
+    def launch(i):
+        c = i % ncop
+        if dual:
+            A.check(L.arcllm_cuda_gateup_silu_q4k(C.c_void_p(ws[2 * c].data_ptr()), C.c_void_p(ws[2 * c + 1].data_ptr()),
+                                                  rows, k, C.c_void_p(x.data_ptr()), C.c_void_p(gamma.data_ptr()),
+                                                  C.c_float(1e-6), C.c_void_p(y.data_ptr()), sp), "gateup")
+        else:
+            A.check(L.arcllm_cuda_matvec(ty, C.c_void_p(ws[c].data_ptr()), rows, k, C.c_void_p(x.data_ptr()), None,
+                                         C.c_float(0), None, None, C.c_void_p(y.data_ptr()), sp), "matvec")
+
+    for i in range(warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        launch(i)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / max(1, steps)
+    alg = nmat * q_bytes(fmt, rows, k) + 4 * (k + rows)
+    return {"workload": ("gateup_q4k_2x%dx%d" % (rows, k)) if dual else ("%s_%dx%d" % (fmt, rows, k)),
+            "us_per_launch_stream": round(ms * 1e3, 2), "GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
+            "frac_of_hbm": round(alg / (ms * 1e-3) / 1e9 / hbm_peak, 4), "weight_copies": ncop, "launches": steps}
 
 
 def run_prefill_gemm(A, L, torch, dev, sp, timed, copies, make_w, m=256):

@@ -243,6 +243,9 @@ ARCLLM_CUDA_API int arcllm_cuda_attention_prefill(const float *q, const uint16_t
  * exit; needs kv_heads*n_splits*(q_heads/kv_heads)*(head_dim+2) <= 65536, else
  * ARC_E_UNSUPPORTED_SHAPE.  Allocates nothing.  All calls share the array:
  * calls that overlap on the GPU race; calls ordered on one stream are fine.
+ * The array is in play only when the slices are merged by the separate merge
+ * kernel (n_splits 1 or > 16, no schedulable cluster, ARCLLM_ATTN_CLUSTER=0);
+ * the clustered form merges in distributed shared memory instead.
  * The first call on a device looks up the array's address (cudaGetSymbolAddress),
  * so make it outside stream capture. */
 ARCLLM_CUDA_API int arcllm_cuda_attention_decode_noalloc(const float *q, const uint16_t *k_cache,

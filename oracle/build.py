@@ -5,7 +5,8 @@ Two libraries:
 * ``oracle/lib/liborc.so`` -- the C restatement in ``oracle/orc.c``.  It needs
   only gcc and is rebuilt wherever it is missing (also on a GPU box).
 * ``oracle/_ref/libref_cpu.so`` -- the reference's OWN CPU code, compiled in
-  place from an ArcLLM checkout (``--reference``, or ``ARCLLM_REFERENCE_DIR``)
+  place from an ArcLLM checkout (``--reference``, ``ARCLLM_REFERENCE_DIR``, or
+  a ``reference`` directory beside this repository)
   through ``oracle/ref_wrap.cpp``.  Nothing is copied out of the reference
   tree.  Built only where that checkout exists; the golden fixtures under
   ``tests/golden/`` carry its outputs elsewhere.
@@ -21,7 +22,17 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORC_SO = os.path.join(HERE, "lib", "liborc.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_cpu.so")
-DEFAULT_REFERENCE = os.environ.get("ARCLLM_REFERENCE_DIR", os.path.join(os.sep, "root", "reference"))
+
+
+def default_reference():
+    """The ArcLLM checkout: ARCLLM_REFERENCE_DIR when set, else a directory
+    named ``reference`` beside this repository's root (None when neither
+    exists)."""
+    d = os.environ.get("ARCLLM_REFERENCE_DIR")
+    if d:
+        return d
+    sibling = os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return sibling if os.path.isdir(sibling) else None
 
 
 def _run(cmd):
@@ -42,9 +53,12 @@ def build_orc(force=False):
     return ORC_SO
 
 
-def build_ref(reference=DEFAULT_REFERENCE, force=False):
+def build_ref(reference=None, force=False):
     """Compile the reference's CPU functions in place; returns the .so path or
     None when no reference checkout is present."""
+    reference = reference or default_reference()
+    if not reference:
+        return None
     src_dir = os.path.join(reference, "src")
     if not os.path.isfile(os.path.join(src_dir, "p8c_segmented_access_correctness.cpp")):
         return None
@@ -61,7 +75,7 @@ def build_ref(reference=DEFAULT_REFERENCE, force=False):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", default=None)
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args(argv)
     print("orc:", build_orc(a.force))
