@@ -42,6 +42,8 @@ SIGNATURES = {
     "arcllm_cuda_gateup_silu_q4k": [_vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp],
     "arcllm_cuda_gemm_q4k_bf16": [_vp, _u32, _u32, _vp, _u32, _vp, _vp],
     "arcllm_cuda_gemm_bf16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],
+    "arcllm_cuda_gemm_f16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],
+    "arcllm_cuda_rmsnorm_rows": [_vp, _vp, _f32, _u32, _u32, _i32, _vp, _vp],
     "arcllm_cuda_rope_kv_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
                                  _vp],
     "arcllm_cuda_attention_prefill": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _vp],
@@ -73,6 +75,7 @@ SIGNATURES = {
     "arcllm_cuda_model_generate": [_vp, _vp, _u32, _u32, _vp, _vp, _vp],
     "arcllm_cuda_model_begin": [_vp, _vp, _u32, _u32, _vp],
     "arcllm_cuda_model_step": [_vp, _i32, _i32, _vp],
+    "arcllm_cuda_model_prefill": [_vp, _vp],
     "arcllm_cuda_model_set_prefill_mode": [_vp, _i32],
     "arcllm_cuda_model_set_prefill_down": [_vp, _u32, _vp, _i32],
     "arcllm_cuda_model_logits": [_vp, C.POINTER(_vp)],

@@ -128,8 +128,9 @@ int gemm_q4k_bf16_prepare();
 int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,
                   cudaStream_t stream);
 // Q4_K (12) or Q6_K (14) weights; y = residual + x W^T when residual is non-null.
+// x and the dequantised W in bf16, or in fp16 when `fp16` (x then holds fp16).
 int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
-                 const float* residual, float* y, cudaStream_t stream);
+                 const float* residual, float* y, cudaStream_t stream, bool fp16 = false);
 
 std::vector<float> rope_table(uint32_t max_ctx, uint32_t head_dim, float theta);
 int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out);
@@ -141,6 +142,7 @@ int model_shard_lm_head(arcllm_cuda_model* m, uint32_t row0, uint32_t rows);
 int model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
                 cudaStream_t st);
 int model_step(arcllm_cuda_model* m, int with_head, int use_graph, cudaStream_t st);
+int model_prefill(arcllm_cuda_model* m, cudaStream_t st, bool* batched_out);
 int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
                    uint32_t* out_host, arcllm_cuda_gen_stats* stats, cudaStream_t st);
 int model_set_prefill_mode(arcllm_cuda_model* m, int mode);

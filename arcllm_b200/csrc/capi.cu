@@ -278,6 +278,21 @@ int arcllm_cuda_gemm_bf16(int type, const void* w, uint32_t n, uint32_t k, const
     ARC_GUARD_END
 }
 
+int arcllm_cuda_gemm_f16(int type, const void* w, uint32_t n, uint32_t k, const uint16_t* x_f16, uint32_t m,
+                         const float* residual, float* y, void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::gemm_kq_bf16(type, w, n, k, x_f16, m, residual, y, static_cast<cudaStream_t>(stream), true);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_rmsnorm_rows(const float* x, const float* gamma, float eps, uint32_t rows, uint32_t h, int out_fp16,
+                             uint16_t* out, void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::launch_rmsnorm_rows_bf16(x, gamma, eps, rows, h, out, static_cast<cudaStream_t>(stream),
+                                         out_fp16 != 0);
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_fill_q4k(void* w, uint64_t block_begin, uint64_t n_blocks, uint64_t seed, void* stream) {
     ARC_GUARD_BEGIN
     return arc::fill_blocks(12, w, block_begin, n_blocks, seed, static_cast<cudaStream_t>(stream));
@@ -494,6 +509,12 @@ int arcllm_cuda_model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, u
                             void* stream) {
     ARC_GUARD_BEGIN
     return arc::model_begin(m, prompt_host, n_prompt, max_new, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_prefill(arcllm_cuda_model* m, void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::model_prefill(m, static_cast<cudaStream_t>(stream), nullptr);
     ARC_GUARD_END
 }
 

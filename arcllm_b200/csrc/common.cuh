@@ -22,6 +22,7 @@ namespace arc {
 enum : uint32_t {
     ARC_DEV_ERR_TIMEOUT = 1u,      // a bounded mbarrier / flag wait gave up
     ARC_DEV_ERR_BOUNDS = 2u,       // a kernel rejected an out-of-range index
+    ARC_DEV_ERR_RANGE = 4u,        // a value rounded to fp16 left the fp16 range
 };
 
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s

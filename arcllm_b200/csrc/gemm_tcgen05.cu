@@ -18,7 +18,9 @@
 //               ahead), then read the accumulators back with tcgen05.ld
 //               (warp w serves TMEM lanes 32*(w%4)..) and store Y.
 // Both MMAs of a K step share the dequantised B tile, so each weight is
-// dequantised once per CTA.  When N/128 tiles leave SMs idle (the FFN-down
+// dequantised once per CTA.  The operands are bf16, or fp16 (same rate, 11
+// instead of 8 significant bits) for the projections whose outputs feed the
+// attention scores.  When N/128 tiles leave SMs idle (the FFN-down
 // shape, N = 3584), K is split across CTAs, the CTAs store partial tiles and
 // a grid-wide reduce kernel adds them in split order (deterministic; the
 // last CTA of each column tile adding them alone was the slowest part of the
@@ -28,6 +30,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 
@@ -39,13 +42,13 @@ namespace {
 
 constexpr uint32_t kBN = 128;          // output columns per CTA
 constexpr uint32_t kBK = 64;           // K per stage (128 bytes of bf16: one swizzle row)
-constexpr uint32_t kStages = 4;
 constexpr uint32_t kAHalf = 128 * kBK * 2;   // 16 KB: one 128-row box of X
 constexpr uint32_t kBTile = kBN * kBK * 2;   // 16 KB: dequantised W tile
-constexpr uint32_t kStageBytes = 2 * kAHalf + kBTile;  // 48 KB
 constexpr uint32_t kDqWarps = 8;                         // dequantising warps: 2 threads per W row
 constexpr uint32_t kThreads = (2 + kDqWarps) * 32;
 constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kStages = 4;
+constexpr uint32_t kStageBytes = 2 * kAHalf + kBTile;  // 48 KB
 
 struct GemmSmemTail {
     uint64_t full_a[kStages];
@@ -82,12 +85,15 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return d;
 }
 
-// kind::f16 instruction descriptor: bf16 A and B (K-major), f32 accumulator, M=128, N=128
-constexpr uint32_t kIdesc = (1u << 4)          // D format f32
-                            | (1u << 7)        // A format bf16
-                            | (1u << 10)       // B format bf16
-                            | ((kBN >> 3) << 17)
-                            | ((128u >> 4) << 24);
+// kind::f16 instruction descriptor: A and B both bf16 (F16 = false) or both fp16
+// (F16 = true), K-major, f32 accumulator, M=128, N=128
+template <bool F16>
+constexpr uint32_t idesc() {
+    return (1u << 4)                  // D format f32
+           | ((F16 ? 0u : 1u) << 7)   // A format: 0 f16, 1 bf16
+           | ((F16 ? 0u : 1u) << 10)  // B format: 0 f16, 1 bf16
+           | ((kBN >> 3) << 17) | ((128u >> 4) << 24);
+}
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -97,13 +103,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+template <bool F16>
+__device__ __forceinline__ void umma_16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         :
-        : "r"(tmem_d), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+        : "r"(tmem_d), "l"(da), "l"(db), "r"(idesc<F16>()), "r"(accumulate)
         : "memory");
 }
 
@@ -130,22 +137,49 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
     return r;
 }
 
-// bf16x2 arithmetic on raw bits (both halves)
-__device__ __forceinline__ uint32_t bsub2(uint32_t a, uint32_t b) {
+__device__ __forceinline__ uint32_t f16x2(float lo, float hi) {
     uint32_t r;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
-}
-__device__ __forceinline__ uint32_t bfma2(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t r;
-    asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
 }
 
+// Packed 16-bit pairs of the GEMM's operand type: bf16 (F16 = false) or fp16.
+template <bool F16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    return F16 ? f16x2(lo, hi) : bf16x2(lo, hi);
+}
+// x2 arithmetic on raw bits (both halves), one rounding each
+template <bool F16>
+__device__ __forceinline__ uint32_t sub2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if (F16)
+        asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    else
+        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+template <bool F16>
+__device__ __forceinline__ uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    if (F16)
+        asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    else
+        asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+// x2 of the value B with small integers c exact as (B + c) - B: the bit
+// pattern of B ORed with c (B = 128 in bf16, 1024 in fp16: ulp 1 there)
+template <bool F16>
+constexpr uint32_t kIntBase2 = F16 ? 0x64006400u : 0x43004300u;
+// x2 of B + 32 (the Q6_K code offset folded into the subtraction)
+template <bool F16>
+constexpr uint32_t kIntBase32x2 = F16 ? 0x64206420u : 0x43204320u;
+
 // Per super-block constants of one thread's sub-blocks 2c + hi (c = 0..3):
-// scale f = d*sc and offset -(dmin*mn), each rounded to bf16 and broadcast to
-// both halves of a bf16x2.  src/p8c_segmented_access_correctness.cpp:531-540
+// scale f = d*sc and offset -(dmin*mn), each rounded to the operand type and
+// broadcast to both halves of a pair.  src/p8c_segmented_access_correctness.cpp:531-540
 // (scale/min unpacking), :1166-1181 (w = d*sc*q - dmin*mn).
+template <bool F16>
 __device__ __forceinline__ void subblock_consts(uint4 hd, uint32_t hi, uint32_t (&fb)[4], uint32_t (&ob)[4]) {
     const uint32_t S[3] = {hd.y, hd.z, hd.w};
     auto sbyte = [&](uint32_t i) { return (S[i >> 2] >> (8u * (i & 3u))) & 0xFFu; };
@@ -162,21 +196,23 @@ __device__ __forceinline__ void subblock_consts(uint4 hd, uint32_t hi, uint32_t 
             sc = (sbyte(j + 4) & 15u) | ((sbyte(j - 4) >> 6) << 4);
             mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
         }
-        fb[c] = bf16x2(d * (float)sc, d * (float)sc);
-        ob[c] = bf16x2(-(dmin * (float)mn), -(dmin * (float)mn));
+        fb[c] = pack2<F16>(d * (float)sc, d * (float)sc);
+        ob[c] = pack2<F16>(-(dmin * (float)mn), -(dmin * (float)mn));
     }
 }
 
 // Dequantise the 32 weights of sub-block 2c+hi of one Q4_K row -- elements
 // 32*hi .. +31 of the 64-element stage row, the low (hi=0) or high (hi=1)
-// nibbles of its 32 code bytes -- to bf16 pairs: q as bf16 via 128+q (exact)
-// minus 128, then one bf16x2 FMA q*f - o (one rounding).  Stored as 16-byte
-// chunks 4*hi .. 4*hi+3 of row n of the swizzled B tile.
+// nibbles of its 32 code bytes -- to bf16 (fp16) pairs: q via (B + q) - B
+// (exact; B = 128 in bf16, 1024 in fp16), then one x2 FMA q*f - o (one
+// rounding).  Stored as 16-byte chunks 4*hi .. 4*hi+3 of row n of the
+// swizzled B tile.
+template <bool F16>
 __device__ __forceinline__ void dequant_subblock(uint4 q0, uint4 q1, uint32_t fb, uint32_t ob, uint32_t n, uint32_t hi,
                                                  uint8_t* btile) {
     const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     uint8_t* rowbase = btile + (n >> 3) * 1024u + (n & 7u) * 128u;
-    constexpr uint32_t k128 = 0x43004300u;  // bf16x2(128, 128)
+    constexpr uint32_t k128 = kIntBase2<F16>;
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) {  // output chunk: elements 8*ch .. +7 = code bytes 8*ch .. +7
         uint32_t out[4];
@@ -186,7 +222,7 @@ __device__ __forceinline__ void dequant_subblock(uint4 q0, uint4 q1, uint32_t fb
             // bytes (2*(pr&1), 2*(pr&1)+1) of the word into the low byte of each 16-bit half
             const uint32_t spread = __byte_perm(word, 0u, (pr & 1) ? 0x4342u : 0x4140u);
             const uint32_t q = hi ? ((spread >> 4) & 0x000F000Fu) : (spread & 0x000F000Fu);
-            out[pr] = bfma2(bsub2(q | k128, k128), fb, ob);
+            out[pr] = fma2<F16>(sub2<F16>(q | k128, k128), fb, ob);
         }
         const uint32_t chunk = 4u * hi + ch;
         *reinterpret_cast<uint4*>(rowbase + ((chunk ^ (n & 7u)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
@@ -209,15 +245,17 @@ __device__ __forceinline__ uint32_t raw9_word(const Raw9& o, int i, uint32_t sh)
 }
 
 // Dequantise quarter q of half h of one Q6_K super-block row -- 32 weights,
-// elements 32*hi .. +31 of the 64-element stage row -- to bf16: the 6-bit code
-// c = low nibble of ql | 2 bits of qh << 4 (src/p8c_segmented_access_correctness.cpp:905-956),
-// c - 32 as bf16 via (128 + c) - 160 (exact), times f = bf16(d * sc) with one
-// rounding; scales sc[8h + 2q] (elements 0..15) and sc[8h + 2q + 1] (16..31).
+// elements 32*hi .. +31 of the 64-element stage row -- to bf16 (fp16): the
+// 6-bit code c = low nibble of ql | 2 bits of qh << 4
+// (src/p8c_segmented_access_correctness.cpp:905-956), c - 32 via (B + c) - (B + 32)
+// (exact), times f = d * sc rounded to the operand type, with one rounding;
+// scales sc[8h + 2q] (elements 0..15) and sc[8h + 2q + 1] (16..31).
+template <bool F16>
 __device__ __forceinline__ void dequant_q6_quarter(const Raw9& ql, uint32_t shl, const Raw9& qh, uint32_t shh,
                                                    uint32_t lo_shift, uint32_t qh_shift, uint32_t f0, uint32_t f1,
                                                    uint32_t n, uint32_t hi, uint8_t* btile) {
     uint8_t* rowbase = btile + (n >> 3) * 1024u + (n & 7u) * 128u;
-    constexpr uint32_t k128 = 0x43004300u, k160 = 0x43204320u, kNegZero = 0x80008000u;
+    constexpr uint32_t k128 = kIntBase2<F16>, k160 = kIntBase32x2<F16>, kNegZero = 0x80008000u;
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) {  // output chunk: elements 8*ch .. +7
         uint32_t out[4];
@@ -229,7 +267,7 @@ __device__ __forceinline__ void dequant_q6_quarter(const Raw9& ql, uint32_t shl,
 #pragma unroll
             for (int pr = 0; pr < 2; ++pr) {
                 const uint32_t spread = __byte_perm(c, 0u, pr ? 0x4342u : 0x4140u);
-                out[2 * wi + pr] = bfma2(bsub2(spread | k128, k160), ch < 2 ? f0 : f1, kNegZero);
+                out[2 * wi + pr] = fma2<F16>(sub2<F16>(spread | k128, k160), ch < 2 ? f0 : f1, kNegZero);
             }
         }
         const uint32_t chunk = 4u * hi + ch;
@@ -237,11 +275,15 @@ __device__ __forceinline__ void dequant_q6_quarter(const Raw9& ql, uint32_t shl,
     }
 }
 
-template <int FMT>
+// F16: X and the dequantised W tile in fp16 (11 significant bits) instead of
+// bf16 (8): the scale and offset of each sub-block, q*f - o and X all round
+// 8x more finely, at the same tensor-core rate.
+template <int FMT, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kq_bf16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w, uint32_t n_total,
                         uint32_t k, uint32_t m, const float* __restrict__ residual, float* __restrict__ y,
                         unsigned int* err, const SplitKWs sk) {
+    constexpr uint32_t kBOff = 2 * kAHalf;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_align_up<1024>(smem_raw, 0);
     GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + kStages * kStageBytes);
@@ -307,10 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t st = smem_u32(smem + s * kStageBytes);
 #pragma unroll
                 for (uint32_t kk = 0; kk < kBK / 16u; ++kk) {
-                    const uint64_t db = sw128_desc(st + 2 * kAHalf + 32u * kk);
+                    const uint64_t db = sw128_desc(st + kBOff + 32u * kk);
                     const uint32_t acc = (kb | kk) != 0u;
-                    umma_bf16(tmem, sw128_desc(st + 32u * kk), db, acc);
-                    umma_bf16(tmem + 128u, sw128_desc(st + kAHalf + 32u * kk), db, acc);
+                    umma_16<F16>(tmem, sw128_desc(st + 32u * kk), db, acc);
+                    umma_16<F16>(tmem + 128u, sw128_desc(st + kAHalf + 32u * kk), db, acc);
                 }
                 umma_commit(&tail->empty[s]);  // stage free once these MMAs have read it
             }
@@ -354,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kb + kPf < nkb) load6(kb + kPf, pql[slot], pqh[slot], psc[slot]);
                 const float d = __half2float(__ushort_as_half((unsigned short)(scd >> 16)));
                 const float s0 = d * (float)(int8_t)(scd & 0xFFu), s1 = d * (float)(int8_t)((scd >> 8) & 0xFFu);
-                const uint32_t f0 = bf16x2(s0, s0), f1 = bf16x2(s1, s1);
+                const uint32_t f0 = pack2<F16>(s0, s0), f1 = pack2<F16>(s1, s1);
                 const uint32_t s = kb % kStages;
                 bool ok = true;
                 if (kb >= kStages) {
@@ -366,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     stop6 = true;
                     break;
                 }
-                dequant_q6_quarter(ql, shl, qh, shh, 4u * (sub & 1u), 2u * q, f0, f1, nrow, hi,
-                                   smem + s * kStageBytes + 2 * kAHalf);
+                dequant_q6_quarter<F16>(ql, shl, qh, shh, 4u * (sub & 1u), 2u * q, f0, f1, nrow, hi,
+                                        smem + s * kStageBytes + kBOff);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tail->full_b[s]);
@@ -391,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t fb[4], ob[4];
             bool stop = false;
             for (uint32_t kb0 = 0; kb0 < nkb && !stop; kb0 += kPrefetch) {  // kPrefetch == 4: one super-block
-                subblock_consts(hd_next, hi, fb, ob);
+                subblock_consts<F16>(hd_next, hi, fb, ob);
                 if (kb0 + 4u < nkb) hd_next = ld_nc_v4(row + ((kb0 >> 2) + 1u) * 144u);
     #pragma unroll
                 for (uint32_t i = 0; i < kPrefetch; ++i) {
@@ -410,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         stop = true;
                         break;
                     }
-                    dequant_subblock(c0, c1, fb[i], ob[i], nrow, hi, smem + s * kStageBytes + 2 * kAHalf);
+                    dequant_subblock<F16>(c0, c1, fb[i], ob[i], nrow, hi, smem + s * kStageBytes + kBOff);
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tail->full_b[s]);
@@ -509,21 +551,32 @@ int gemm_splitk_reserve(size_t ws_floats, float** ws) {
 }  // namespace
 
 int gemm_q4k_bf16_prepare() {
-    static bool done[64] = {};
+    static std::atomic<bool> done[64] = {};
+    static std::mutex prep_mutex;
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (done[dev & 63]) return ARC_OK;
-    cudaError_t e =
-        cudaFuncSetAttribute(gemm_kq_bf16_kernel<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return set_error(ARC_E_CUDA, "gemm prepare: no current device below index 64");
+    if (done[dev].load(std::memory_order_acquire)) return ARC_OK;
+    std::lock_guard<std::mutex> lock(prep_mutex);
+    if (done[dev].load(std::memory_order_relaxed)) return ARC_OK;
+    cudaError_t e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<12, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kSmemBytes);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<14>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+        e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<14, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<12, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<14, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmemBytes);
     if (e != cudaSuccess) return set_cuda_error(e, "gemm prepare");
-    done[dev & 63] = true;
+    done[dev].store(true, std::memory_order_release);
     return ARC_OK;
 }
 
 int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
-                 const float* residual, float* y, cudaStream_t stream) {
+                 const float* residual, float* y, cudaStream_t stream, bool fp16) {
     if (fmt != 12 && fmt != 14) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: weights must be Q4_K or Q6_K");
     if (!w || !x || !y) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: null pointer");
     if (m == 0 || m > 256 || n == 0 || n % kBN || k == 0 || k % 256u)
@@ -540,9 +593,10 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
     const cuuint64_t strides[1] = {(cuuint64_t)k * 2u};
     const cuuint32_t box[2] = {kBK, 128};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box,
-                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = enc(&map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                           const_cast<uint16_t*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: tensor map for X rejected");
     // split K so that about one CTA per SM is busy (whole super-blocks per split)
     int dev = 0;
@@ -561,11 +615,20 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
         st = gemm_splitk_reserve((size_t)ks * m * n, &sk.ws);
         if (st != ARC_OK) return st;
     }
-    cudaError_t e =
-        fmt == 12 ? launch_kernel(gemm_kq_bf16_kernel<12>, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
-                                  static_cast<const uint8_t*>(w), n, k, m, residual, y, dev_error_word(), sk)
-                  : launch_kernel(gemm_kq_bf16_kernel<14>, dim3(tiles, ks), dim3(kThreads), kSmemBytes, stream, map,
-                                  static_cast<const uint8_t*>(w), n, k, m, residual, y, dev_error_word(), sk);
+    const uint8_t* wb = static_cast<const uint8_t*>(w);
+    const dim3 grid(tiles, ks), block(kThreads);
+    unsigned int* err = dev_error_word();
+    cudaError_t e;
+    if (fp16)
+        e = fmt == 12 ? launch_kernel(gemm_kq_bf16_kernel<12, true>, grid, block, kSmemBytes, stream, map, wb, n, k, m,
+                                      residual, y, err, sk)
+                      : launch_kernel(gemm_kq_bf16_kernel<14, true>, grid, block, kSmemBytes, stream, map, wb, n, k, m,
+                                      residual, y, err, sk);
+    else
+        e = fmt == 12 ? launch_kernel(gemm_kq_bf16_kernel<12, false>, grid, block, kSmemBytes, stream, map, wb, n, k,
+                                      m, residual, y, err, sk)
+                      : launch_kernel(gemm_kq_bf16_kernel<14, false>, grid, block, kSmemBytes, stream, map, wb, n, k,
+                                      m, residual, y, err, sk);
     if (e == cudaSuccess && ks > 1) {
         const uint64_t n4 = (uint64_t)m * n / 4u;
         const uint32_t blocks = (uint32_t)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)sms * 8u);

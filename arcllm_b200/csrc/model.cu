@@ -12,8 +12,8 @@
 // RMSNorm fused into the dual gate/up matvec with silu(g)*u, down projection
 // + residual.  Then output RMSNorm fused into the LM head, argmax, finalize.
 // The prompt (all but its last token) is consumed in batches of up to 256
-// rows on the tensor cores (enqueue_prefill_chunk: bf16 tcgen05 GEMMs for
-// every projection, batched RMSNorm / RoPE + KV store / causal attention /
+// rows on the tensor cores (enqueue_prefill_chunk: tcgen05 GEMMs for every
+// projection, fp16 operands for Q/K/V and bf16 for the rest, batched RMSNorm / RoPE + KV store / causal attention /
 // SiLU kernels -- the reference's prefill chain, src/arcllm_v1_runtime.cpp:
 // 340-369), or, in prefill mode 0, token by token through the decode layer
 // chain without the LM head (the prefill graph, fp32 throughout).
@@ -68,6 +68,7 @@ struct arcllm_cuda_model {
           *pf_u = nullptr;
     uint16_t *pf_xb = nullptr, *pf_attn = nullptr, *pf_s = nullptr;
     uint32_t launches_prefill_batched = 0;
+    uint32_t begun_prompt = 0;  // prompt length of the last begin() (0: none)
 };
 
 namespace arc {
@@ -281,10 +282,14 @@ int enqueue_prefill_chunk(arcllm_cuda_model* m, uint32_t pos0, uint32_t T, cudaS
         const arcllm_cuda_layer& L = m->layers[l];
         int type_down = 0;
         const void* w_down = prefill_down_w(m, l, &type_down);
-        ARC_TRY(launch_rmsnorm_rows_bf16(m->pf_h, L.attn_norm, c.rms_eps, T, H, m->pf_xb, st));
-        ARC_TRY(gemm_kq_bf16(L.type_q, L.wq, H, H, m->pf_xb, T, nullptr, m->pf_q, st));
-        ARC_TRY(gemm_kq_bf16(L.type_k, L.wk, KV, H, m->pf_xb, T, nullptr, m->pf_k, st));
-        ARC_TRY(gemm_kq_bf16(L.type_v, L.wv, KV, H, m->pf_xb, T, nullptr, m->pf_v, st));
+        // Q, K and V feed the attention scores, which the synthetic models make nearly one-hot
+        // (q.k/sqrt(d) of 1e3-1e4): their GEMMs run on fp16 operands (11 significant bits;
+        // bf16's rounding of the sub-block scales moved near-tied positions), the other
+        // GEMMs on bf16
+        ARC_TRY(launch_rmsnorm_rows_bf16(m->pf_h, L.attn_norm, c.rms_eps, T, H, m->pf_xb, st, true));
+        ARC_TRY(gemm_kq_bf16(L.type_q, L.wq, H, H, m->pf_xb, T, nullptr, m->pf_q, st, true));
+        ARC_TRY(gemm_kq_bf16(L.type_k, L.wk, KV, H, m->pf_xb, T, nullptr, m->pf_k, st, true));
+        ARC_TRY(gemm_kq_bf16(L.type_v, L.wv, KV, H, m->pf_xb, T, nullptr, m->pf_v, st, true));
         RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
         ARC_TRY(launch_rope_kv_rows(m->pf_q, m->pf_k, m->pf_v, L.bq, L.bk, L.bv, m->rope, pos0, T, m->kc, m->vc, rs,
                                     st));
@@ -476,6 +481,32 @@ int model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_pr
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->state, &s, sizeof s, cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // `s` lives on this stack frame
     if (e != cudaSuccess) return set_cuda_error(e, "begin: upload");
+    m->begun_prompt = n_prompt;
+    return ARC_OK;
+}
+
+// Prompt tokens 0 .. n-2 of the request begun last: batched on the tensor
+// cores when the model allows it (else one fp32 prefill step per token).
+// Afterwards the next step(with_head) yields the first generated token.
+int model_prefill(arcllm_cuda_model* m, cudaStream_t st, bool* batched_out) {
+    if (!m) return set_error(ARC_E_INVALID_ARGUMENT, "prefill: null model");
+    ARC_TRY(ready(m));
+    const uint32_t n_prompt = m->begun_prompt;
+    if (n_prompt == 0) return set_error(ARC_E_INVALID_ARGUMENT, "prefill: begin() first");
+    m->begun_prompt = 0;  // the prompt is consumed once
+    const bool batched = n_prompt > 1 && prefill_batched_ok(m);
+    m->launches_prefill_batched = 0;
+    if (batched) {
+        ARC_TRY(prefill_alloc(m));
+        for (uint32_t p0 = 0; p0 + 1 < n_prompt; p0 += kPrefillRows)
+            ARC_TRY(enqueue_prefill_chunk(m, p0, std::min(kPrefillRows, n_prompt - 1u - p0), st,
+                                          &m->launches_prefill_batched));
+        ARC_TRY(launch_prefill_done(m->state, m->prompt, n_prompt, st));
+        ++m->launches_prefill_batched;
+    } else {
+        for (uint32_t i = 0; i + 1 < n_prompt; ++i) ARC_TRY(model_step(m, 0, 1, st));
+    }
+    if (batched_out) *batched_out = batched;
     return ARC_OK;
 }
 
@@ -502,19 +533,10 @@ int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventCreate(&e2);
-    const bool batched = n_prompt > 1 && prefill_batched_ok(m);
-    if (batched) ARC_TRY(prefill_alloc(m));
-    m->launches_prefill_batched = 0;
+    if (n_prompt > 1 && prefill_batched_ok(m)) ARC_TRY(prefill_alloc(m));  // outside the timed region
+    bool batched = false;
     cudaEventRecord(e0, st);
-    if (batched) {
-        for (uint32_t p0 = 0; p0 + 1 < n_prompt; p0 += kPrefillRows)
-            ARC_TRY(enqueue_prefill_chunk(m, p0, std::min(kPrefillRows, n_prompt - 1u - p0), st,
-                                          &m->launches_prefill_batched));
-        ARC_TRY(launch_prefill_done(m->state, m->prompt, n_prompt, st));
-        ++m->launches_prefill_batched;
-    } else {
-        for (uint32_t i = 0; i + 1 < n_prompt; ++i) ARC_TRY(model_step(m, 0, 1, st));
-    }
+    ARC_TRY(model_prefill(m, st, &batched));
     ARC_TRY(model_step(m, 1, 1, st));  // last prompt token: first generated token
     cudaEventRecord(e1, st);
     for (uint32_t i = 1; i < max_new; ++i) ARC_TRY(model_step(m, 1, 1, st));

@@ -34,10 +34,12 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
     return r;
 }
 
-// One CTA (256 threads) per row.
+// One CTA (256 threads) per row; bf16 output, or fp16 when FP16 (values that
+// round to +-inf in fp16 raise the device error word's range bit).
+template <bool FP16>
 __global__ void __launch_bounds__(256) rmsnorm_rows_bf16_kernel(const float* __restrict__ x,
                                                                 const float* __restrict__ gamma, float eps, uint32_t h,
-                                                                uint16_t* __restrict__ out) {
+                                                                uint16_t* __restrict__ out, unsigned int* err) {
     __shared__ double red[8];
     const float* xr = x + (uint64_t)blockIdx.x * h;
     double ss = 0.0;
@@ -53,7 +55,18 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_bf16_kernel(const float* __r
     for (int w = 0; w < 8; ++w) tot += red[w];
     const float inv = 1.0f / sqrtf((float)(tot / (double)h) + eps);
     uint16_t* o = out + (uint64_t)blockIdx.x * h;
-    for (uint32_t i = threadIdx.x; i < h; i += 256u) o[i] = f2bf((xr[i] * inv) * gamma[i]);
+    bool range = false;
+    for (uint32_t i = threadIdx.x; i < h; i += 256u) {
+        const float v = (xr[i] * inv) * gamma[i];
+        if (FP16) {
+            const __half hv = __float2half_rn(v);
+            range |= __hisinf(hv) != 0 && isfinite(v);
+            o[i] = __half_as_ushort(hv);
+        } else {
+            o[i] = f2bf(v);
+        }
+    }
+    if (FP16 && range) raise_error(err, ARC_DEV_ERR_RANGE);
 }
 
 // One thread per rotation pair of one row: q pairs, then k pairs (with v).
@@ -141,12 +154,15 @@ __device__ __forceinline__ void cp_async_wait() {
 // = hi + lo), so S is exact to about 2^-22 of |q| |k| (the cache is fp16
 // already): scores of the near-one-hot synthetic models stay as sharp as in
 // fp32.  P enters the P V product as fp16 (11 bits, the output is bf16).
-// |q| * scale must stay inside the fp16 range (< 65504).
+// |q| * scale must stay inside the fp16 range (< 65504); an element beyond it
+// raises the device error word's range bit (its row's output is then not
+// meaningful).
 template <int GQ>
 __global__ void __launch_bounds__(64) attention_prefill_kernel(const float* __restrict__ q,
                                                                const uint16_t* __restrict__ kc,
                                                                const uint16_t* __restrict__ vc, uint32_t pos0,
-                                                               uint32_t T, AttnShape s, uint16_t* __restrict__ out) {
+                                                               uint32_t T, AttnShape s, uint16_t* __restrict__ out,
+                                                               unsigned int* err) {
     constexpr int D = 128, GP = GQ == 7 ? 8 : GQ, RQ = 16 / GP, NWARP = 2, PT = 16;
     constexpr uint32_t ROWB = D * 2 + 16;  // bytes per cached row in smem (padding: conflict-free ldmatrix)
     __shared__ __align__(128) uint8_t sm[NWARP][2][2][PT * ROWB];  // [warp][buffer][K, V][position row]
@@ -169,6 +185,7 @@ __global__ void __launch_bounds__(64) attention_prefill_kernel(const float* __re
     // Q fragments, hi and lo fp16 halves of q * scale; register h + 2j of k-step kk holds
     // row g + 8h, dims 16kk + 2t + 8j, +1
     uint32_t qa[8][4], qb[8][4];
+    bool range = false;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
 #pragma unroll
@@ -182,9 +199,11 @@ __global__ void __launch_bounds__(64) attention_prefill_kernel(const float* __re
                 v.x *= s.scale, v.y *= s.scale;
                 const __half2 hi = __floats2half2_rn(v.x, v.y);
                 const float2 hf = __half22float2(hi);
+                range |= (isinf(hf.x) && isfinite(v.x)) || (isinf(hf.y) && isfinite(v.y));
                 qa[kk][h + 2 * j] = *reinterpret_cast<const uint32_t*>(&hi);
                 qb[kk][h + 2 * j] = pack_f16(v.x - hf.x, v.y - hf.y);
             }
+    if (range) raise_error(err, ARC_DEV_ERR_RANGE);
     float o[16][4];
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
@@ -329,11 +348,15 @@ int launch_prefill_done(GreedyState* st, const uint32_t* prompt, uint32_t n_prom
 }
 
 int launch_rmsnorm_rows_bf16(const float* x, const float* gamma, float eps, uint32_t rows, uint32_t h, uint16_t* out,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, bool fp16) {
     if (rows == 0) return ARC_OK;
-    return launch_checked(
-        launch_kernel(rmsnorm_rows_bf16_kernel, dim3(rows), dim3(256), 0, stream, x, gamma, eps, h, out),
-        "rmsnorm rows launch");
+    if (!x || !gamma || !out || h == 0) return set_error(ARC_E_INVALID_ARGUMENT, "rmsnorm rows: null pointer or h 0");
+    const cudaError_t e =
+        fp16 ? launch_kernel(rmsnorm_rows_bf16_kernel<true>, dim3(rows), dim3(256), 0, stream, x, gamma, eps, h, out,
+                             dev_error_word())
+             : launch_kernel(rmsnorm_rows_bf16_kernel<false>, dim3(rows), dim3(256), 0, stream, x, gamma, eps, h, out,
+                             dev_error_word());
+    return launch_checked(e, "rmsnorm rows launch");
 }
 
 int launch_rope_kv_rows(float* q, float* k, const float* v, const float* bq, const float* bk, const float* bv,
@@ -360,13 +383,14 @@ int launch_attention_prefill(const float* q, const uint16_t* kc, const uint16_t*
     // two warps per CTA, each 16 / (q heads per KV head, 7 -> 8) query rows
     const uint32_t rq = 16u / (gq == 7u ? 8u : gq);
     const dim3 grid((rows + 2u * rq - 1u) / (2u * rq), s.kv_heads);
+    unsigned int* err = dev_error_word();
     cudaError_t e;
     switch (gq) {
-        case 1: e = launch_kernel(attention_prefill_kernel<1>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
-        case 2: e = launch_kernel(attention_prefill_kernel<2>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
-        case 4: e = launch_kernel(attention_prefill_kernel<4>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
-        case 7: e = launch_kernel(attention_prefill_kernel<7>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
-        case 8: e = launch_kernel(attention_prefill_kernel<8>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out); break;
+        case 1: e = launch_kernel(attention_prefill_kernel<1>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out, err); break;
+        case 2: e = launch_kernel(attention_prefill_kernel<2>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out, err); break;
+        case 4: e = launch_kernel(attention_prefill_kernel<4>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out, err); break;
+        case 7: e = launch_kernel(attention_prefill_kernel<7>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out, err); break;
+        case 8: e = launch_kernel(attention_prefill_kernel<8>, grid, dim3(64), 0, stream, q, kc, vc, pos0, rows, s, out, err); break;
         default: return set_error(ARC_E_UNSUPPORTED_SHAPE, "attention: q heads per kv head must be 1, 2, 4, 7 or 8");
     }
     return launch_checked(e, "attention prefill launch");

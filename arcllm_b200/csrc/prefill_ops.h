@@ -8,9 +8,10 @@
 
 namespace arc {
 
-// out[r][i] = bf16((x[r][i] * rsqrt(mean_i(x[r]^2) + eps)) * gamma[i])
+// out[r][i] = v rounded to bf16 (or fp16 when `fp16`; an overflow sets the
+// device error word's range bit), v = (x[r][i] * rsqrt(mean_i(x[r]^2) + eps)) * gamma[i]
 int launch_rmsnorm_rows_bf16(const float* x, const float* gamma, float eps, uint32_t rows, uint32_t h, uint16_t* out,
-                             cudaStream_t stream);
+                             cudaStream_t stream, bool fp16 = false);
 // rows t of q[rows][q_heads*hd], k, v[rows][kv_dim] (+ biases, nullable): RoPE
 // at position pos0+t, q and k rotated in place, k and v stored to the fp16 cache
 int launch_rope_kv_rows(float* q, float* k, const float* v, const float* bq, const float* bk, const float* bv,

@@ -166,6 +166,10 @@ class SyntheticModel:
         pa = (C.c_uint32 * len(prompt))(*prompt)
         call("arcllm_cuda_model_begin", self.h, pa, len(prompt), max_new, self.stream)
 
+    def prefill(self):
+        """after begin(): consume the prompt but its last token as generate() does"""
+        call("arcllm_cuda_model_prefill", self.h, self.stream)
+
     def step(self, with_head=True, use_graph=True):
         call("arcllm_cuda_model_step", self.h, 1 if with_head else 0, 1 if use_graph else 0, self.stream)
 

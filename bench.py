@@ -730,6 +730,27 @@ def run_decode(A, torch, hbm_peak, n_prompt=256, max_new=128):
            "e2e_tok_s_incl_prefill": round(max_new / wall, 1),
            "launches_per_token": st.decode_launches_per_step, "graph_launches_per_token": 1,
            "first_tokens": toks[:4], "finite": bool(st.finite)}
+    # Precision of the default path (batched bf16 tensor-core prefill) against the fp32
+    # token-by-token prefill on the same prompt, both on this GPU (the CPU-oracle check of
+    # the 28-layer model is tests/test_decode_e2e_gpu.py): the generated tokens position by
+    # position, and the logits of the first decode steps.
+    m.set_prefill_mode(0)
+    toks32, _ = m.generate(prompt, max_new)
+    window = min(4, max_new)
+    lg = {}
+    for mode in (1, 0):
+        m.set_prefill_mode(mode)
+        m.begin(prompt, window)
+        m.prefill()
+        lg[mode] = []
+        for _ in range(window):
+            m.step(with_head=True, use_graph=True)
+            lg[mode].append(m.logits().astype("float64"))
+    import numpy as np
+    rels = [float(np.linalg.norm(a - b) / np.linalg.norm(b)) for a, b in zip(lg[1], lg[0])]
+    res["vs_fp32_token_prefill"] = {
+        "token_match_rate": round(sum(int(a == b) for a, b in zip(toks, toks32)) / max_new, 4),
+        "logits_rel_l2_max_first_%d_steps" % window: float("%.3g" % max(rels))}
     m.close()
     torch.cuda.empty_cache()
     return res

@@ -65,7 +65,8 @@ ARCLLM_CUDA_API const char *arcllm_cuda_status_string(int status);
 ARCLLM_CUDA_API const char *arcllm_cuda_last_error_message(void);
 
 /* Reads (and clears) the device error word the kernels set when a bounded
- * wait gives up (bit 0) or an index check fails (bit 1).  Synchronises
+ * wait gives up (bit 0), an index check fails (bit 1) or an fp16 operand
+ * leaves the fp16 range (bit 2).  Synchronises
  * `stream` first.  Returns ARC_E_DEVICE_TIMEOUT if bit 0 was set. */
 ARCLLM_CUDA_API int arcllm_cuda_device_error(void *stream, uint32_t *out_bits);
 
@@ -181,6 +182,23 @@ ARCLLM_CUDA_API int arcllm_cuda_gemm_q4k_bf16(const void *w, uint32_t n, uint32_
  * fused into the epilogue).  Q6_K rows need only be 2-byte aligned. */
 ARCLLM_CUDA_API int arcllm_cuda_gemm_bf16(int type, const void *w, uint32_t n, uint32_t k, const uint16_t *x_bf16,
                                           uint32_t m, const float *residual, float *y, void *stream);
+/* The same GEMM with fp16 operands: x_f16 is fp16 and the weights are
+ * dequantised to fp16 (scale and offset of each sub-block and q*f - o rounded
+ * to 11 significant bits instead of bf16's 8), at the same tensor-core rate.
+ * generate() uses it for the prefill Q/K/V projections
+ * (src/arcllm_v1_runtime.cpp:349-353), whose outputs feed the attention
+ * scores: with bf16 operands the per-sub-block rounding of the scales moved
+ * near-tied positions of the synthetic 7B-shape models.  Activations must stay
+ * inside the fp16 range (|x| < 65504). */
+ARCLLM_CUDA_API int arcllm_cuda_gemm_f16(int type, const void *w, uint32_t n, uint32_t k, const uint16_t *x_f16,
+                                         uint32_t m, const float *residual, float *y, void *stream);
+/* Batched RMSNorm of the prefill chain (shaders/p7_rmsnorm_seq.comp per row,
+ * src/arcllm_v1_runtime.cpp:347,355; sum of squares in double as
+ * src/p8c_segmented_access_correctness.cpp:958-969): out[r][i] = v rounded to
+ * bf16 (out_fp16 == 0) or fp16, v = x[r][i] * rsqrt(mean(x[r]^2) + eps) * gamma[i].
+ * An fp16 value that overflows sets bit 2 of the device error word. */
+ARCLLM_CUDA_API int arcllm_cuda_rmsnorm_rows(const float *x, const float *gamma, float eps, uint32_t rows, uint32_t h,
+                                             int out_fp16, uint16_t *out, void *stream);
 
 /* ---- synthetic fixture streams -------------------------------------------
  * Deterministic, counter-based generators (element n of a splitmix64
@@ -335,6 +353,11 @@ ARCLLM_CUDA_API int arcllm_cuda_model_generate(arcllm_cuda_model *m, const uint3
 ARCLLM_CUDA_API int arcllm_cuda_model_begin(arcllm_cuda_model *m, const uint32_t *prompt_host, uint32_t n_prompt,
                                             uint32_t max_new, void *stream);
 ARCLLM_CUDA_API int arcllm_cuda_model_step(arcllm_cuda_model *m, int with_head, int use_graph, void *stream);
+/* After begin(): consume prompt tokens 0 .. n-2 the way generate() does (the
+ * batched tensor-core prefill in mode 1, fp32 steps in mode 0; the reference's
+ * prefill submit, src/arcllm_v1_runtime.cpp:340-369,440-446), so that the next
+ * step(with_head = 1) yields the first generated token.  Once per begin(). */
+ARCLLM_CUDA_API int arcllm_cuda_model_prefill(arcllm_cuda_model *m, void *stream);
 /* Prefill mode: 1 = batched on the tensor cores (default), 0 = token by token. */
 ARCLLM_CUDA_API int arcllm_cuda_model_set_prefill_mode(arcllm_cuda_model *m, int mode);
 /* Q4_K/Q6_K down weights of `layer` for the batched prefill, needed when the

@@ -15,16 +15,21 @@ from arcllm_b200 import GGML_F16, GGML_Q4_K
 
 class OracleModel:
     def __init__(self, cfg, specs, threads=8):
+        from concurrent.futures import ThreadPoolExecutor
         self.cfg, self.specs, self.threads = cfg, specs, threads
         self.w = {}
-        for name, s in specs.items():
+
+        def make(item):  # the C fill routines release the GIL: tensors fill in parallel
+            name, s = item
             if s["kind"] == "quant":
                 fmt = "q4k" if s["type"] == GGML_Q4_K else "q6k"
-                self.w[name] = (fmt, O.fill_weights(fmt, s["rows"], s["cols"], s["seed"]))
-            elif s["kind"] == "normal16":
-                self.w[name] = ("f16", None)  # rows generated on demand
-            else:
-                self.w[name] = ("f32", O.normal_f32(s["rows"] * s["cols"], s["seed"], s["mu"], s["sigma"]))
+                return name, (fmt, O.fill_weights(fmt, s["rows"], s["cols"], s["seed"]))
+            if s["kind"] == "normal16":
+                return name, ("f16", None)  # rows generated on demand
+            return name, ("f32", O.normal_f32(s["rows"] * s["cols"], s["seed"], s["mu"], s["sigma"]))
+
+        with ThreadPoolExecutor(max(1, threads)) as ex:
+            self.w = dict(ex.map(make, specs.items()))
         L, C_, KV = cfg["n_layers"], cfg["max_ctx"], cfg["n_kv_heads"] * cfg["head_dim"]
         self.kc = np.zeros(L * C_ * KV, np.float32)
         self.vc = np.zeros(L * C_ * KV, np.float32)
@@ -45,7 +50,9 @@ class OracleModel:
         rb = (H // 256) * 144
         return O.dequant(fmt, w[tok * rb:(tok + 1) * rb], 1, H).ravel()
 
-    def step(self, tok, pos, fp16_cache=False):
+    def step(self, tok, pos, fp16_cache=False, head=True):
+        """Hidden state of token `tok` at position `pos` through every layer
+        (its K/V rows land in the cache); the logits when `head`, else None."""
         c = self.cfg
         H, eps, th = c["hidden"], c["rms_eps"], c["rope_theta"]
         QH, KVH, D, MC = c["n_heads"], c["n_kv_heads"], c["head_dim"], c["max_ctx"]
@@ -70,5 +77,7 @@ class OracleModel:
             xn2 = O.rmsnorm(h1, self.w[p + "ffn_norm"][1], eps)
             s = O.swiglu(self.mv(p + "w_gate", xn2), self.mv(p + "w_up", xn2))
             h = O.add(h1, self.mv(p + "w_down", s))
+        if not head:
+            return None
         xn = O.rmsnorm(h, self.w["output_norm"][1], eps)
         return self.mv("output", xn)

@@ -1,9 +1,10 @@
-"""Prefill GEMM on tcgen05 (arcllm_cuda_gemm_q4k_bf16 / arcllm_cuda_gemm_bf16):
-y = (residual +) x * W^T with x bf16 [m x k], W Q4_K or Q6_K [n x k], fp32
-accumulation.  Checked tightly against the same
-product with W dequantised the way the kernel does it (bf16 scale and offset
-per sub-block, one bf16 rounding of q*f - o), and at the stated 1e-2 rel-L2
-against the CPU oracle's bit-exact fp32 dequantisation."""
+"""Prefill GEMM on tcgen05 (arcllm_cuda_gemm_q4k_bf16 / arcllm_cuda_gemm_bf16 /
+arcllm_cuda_gemm_f16): y = (residual +) x * W^T with x bf16 (fp16) [m x k],
+W Q4_K or Q6_K [n x k], fp32 accumulation.  Checked tightly against the same
+product with W dequantised the way the kernel does it (bf16 or fp16 scale and
+offset per sub-block, one rounding of q*f - o), and at the stated 1e-2 rel-L2
+(6e-4 for the fp16 form) against the CPU oracle's bit-exact fp32
+dequantisation; plus the batched RMSNorm that produces x."""
 import ctypes as C
 
 import numpy as np
@@ -17,13 +18,13 @@ import gpu_util as G
 pytestmark = pytest.mark.gpu
 
 
-def bf16_round(a):
-    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.bfloat16).to(torch.float32).numpy()
+def bf16_round(a, dt=torch.bfloat16):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dt).to(torch.float32).numpy()
 
 
-def q4k_bf16_weights(w_host, n, k):
-    """The kernel's bf16 weights: f = bf16(d*sc), o = bf16(dmin*mn) per
-    sub-block, w = bf16(q*f - o) with one rounding."""
+def q4k_bf16_weights(w_host, n, k, dt=torch.bfloat16):
+    """The kernel's bf16 (or fp16, dt) weights: f = rnd(d*sc), o = rnd(dmin*mn)
+    per sub-block, w = rnd(q*f - o) with one rounding."""
     nb = k // 256
     blk = w_host.reshape(n * nb, 144)
     d = blk[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
@@ -38,30 +39,30 @@ def q4k_bf16_weights(w_host, n, k):
         else:
             sc[:, j] = (s[:, j + 4] & 15) | ((s[:, j - 4] >> 6) << 4)
             mn[:, j] = (s[:, j + 4] >> 4) | ((s[:, j] >> 6) << 4)
-    f = bf16_round((d[:, None] * sc.astype(np.float32)).astype(np.float32)).astype(np.float64)
-    o = bf16_round((dmin[:, None] * mn.astype(np.float32)).astype(np.float32)).astype(np.float64)
+    f = bf16_round((d[:, None] * sc.astype(np.float32)).astype(np.float32), dt).astype(np.float64)
+    o = bf16_round((dmin[:, None] * mn.astype(np.float32)).astype(np.float32), dt).astype(np.float64)
     kk = np.arange(256)
     byte = blk[:, 16 + (kk >> 6) * 32 + (kk & 31)].astype(np.int32)
     q = np.where((kk & 63) < 32, byte & 15, byte >> 4).astype(np.float64)
     w = q * f[:, kk >> 5] - o[:, kk >> 5]
-    return bf16_round(w.astype(np.float32)).reshape(n, k)
+    return bf16_round(w.astype(np.float32), dt).reshape(n, k)
 
 
-def q6k_bf16_weights(w_host, n, k):
-    """The kernel's bf16 Q6_K weights: f = bf16(d*sc) per 16-element group,
-    w = bf16((c - 32) * f) with one rounding."""
+def q6k_bf16_weights(w_host, n, k, dt=torch.bfloat16):
+    """The kernel's bf16 (or fp16, dt) Q6_K weights: f = rnd(d*sc) per
+    16-element group, w = rnd((c - 32) * f) with one rounding."""
     nb = k // 256
     blk = w_host.reshape(n * nb, 210)
     d = blk[:, 208:210].copy().view(np.float16).astype(np.float32)[:, 0]
     sc = blk[:, 192:208].astype(np.int8).astype(np.float32)
-    f = bf16_round((d[:, None] * sc).astype(np.float32)).astype(np.float64)
+    f = bf16_round((d[:, None] * sc).astype(np.float32), dt).astype(np.float64)
     kk = np.arange(256)
     h, q, l = kk >> 7, (kk & 127) >> 5, kk & 31
     low = (blk[:, 64 * h + 32 * (q & 1) + l].astype(np.int32) >> (4 * (q >> 1))) & 15
     high = (blk[:, 128 + 32 * h + l].astype(np.int32) >> (2 * q)) & 3
     c = (low | (high << 4)).astype(np.float64) - 32.0
     w = c * f[:, 8 * h + 2 * q + (l >> 4)]
-    return bf16_round(w.astype(np.float32)).reshape(n, k)
+    return bf16_round(w.astype(np.float32), dt).reshape(n, k)
 
 
 def run_gemm_t(fmt, m, n, k, seed, residual=False):
@@ -138,3 +139,60 @@ def test_gemm_rejects_bad_shapes():
     for m, n, k in ((257, 128, 512), (0, 128, 512), (256, 100, 512), (256, 128, 300)):
         st = L.arcllm_cuda_gemm_q4k_bf16(*args(m, n, k))
         assert L.arcllm_cuda_status_string(st) == b"ARC_E_UNSUPPORTED_SHAPE"
+
+
+
+@pytest.mark.parametrize("fmt,m,n,k,res", [("q4k", 255, 3584, 3584, False), ("q4k", 255, 512, 3584, False),
+                                           ("q6k", 255, 512, 3584, True), ("q4k", 100, 384, 1024, True),
+                                           ("q6k", 256, 3584, 18944, False), ("q4k", 1, 128, 512, False)])
+def test_gemm_f16_operands(fmt, m, n, k, res):
+    """arcllm_cuda_gemm_f16: fp16 x times the weights dequantised to fp16 (the
+    kernel's rounding: f, o and q*f - o each to fp16).  Within 1e-5 of that
+    product, and about 8x closer to the fp32-dequantised product than the
+    bf16 GEMM (the Q/K/V projections of the prefill use it)."""
+    seed = 2300 + m + n + k
+    w_host = O.fill_weights(fmt, n, k, seed)
+    w = G.to_dev(w_host)
+    x32 = O.normal_f32(m * k, seed + 1).reshape(m, k)
+    xh = torch.from_numpy(x32).to(torch.float16).to(G.dev())
+    r = torch.from_numpy(O.normal_f32(m * n, seed + 2).reshape(m, n)).to(G.dev()) if res else None
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device=G.dev())
+    A.call("arcllm_cuda_gemm_f16", 12 if fmt == "q4k" else 14, G.ptr(w), n, k, C.c_void_p(xh.data_ptr()), m,
+           C.c_void_p(r.data_ptr()) if res else None, C.c_void_p(y.data_ptr()), G.stream())
+    torch.cuda.synchronize()
+    G.check_device_error()
+    yv = y.cpu().numpy().astype(np.float64)
+    wf = (q4k_bf16_weights if fmt == "q4k" else q6k_bf16_weights)(w_host, n, k, torch.float16).astype(np.float64)
+    wd = O.dequant(fmt, w_host, n, k).reshape(n, k).astype(np.float64)
+    rr = r.cpu().numpy().astype(np.float64) if res else 0.0
+    xf = xh.float().cpu().numpy().astype(np.float64)
+    y_k = rr + xf @ wf.T
+    y_f = x32.astype(np.float64) @ wd.T
+    rel_k = np.linalg.norm(yv - y_k) / np.linalg.norm(y_k)
+    rel_f = np.linalg.norm(yv - rr - y_f) / np.linalg.norm(y_f)
+    print("f16 gemm %s %dx%dx%d res=%d: rel-L2 %.2e (kernel's fp16 W), %.2e (fp32 x and W)"
+          % (fmt, m, n, k, res, rel_k, rel_f))
+    assert np.isfinite(yv).all()
+    assert rel_k <= 1e-5
+    assert rel_f <= 6e-4
+
+
+@pytest.mark.parametrize("fp16", [0, 1])
+def test_rmsnorm_rows(fp16):
+    """arcllm_cuda_rmsnorm_rows: v = x * rsqrt(mean(x^2) + eps) * gamma per row
+    (sum of squares in double), rounded to bf16 or fp16."""
+    rows, h, eps = 37, 3584, 1e-6
+    x = O.normal_f32(rows * h, 77, 0.0, 3.0).reshape(rows, h)
+    g = O.normal_f32(h, 78, 1.0, 0.1)
+    xd, gd = G.to_dev(x), G.to_dev(g)
+    out = torch.empty(rows * h, dtype=torch.int16, device=G.dev())
+    A.call("arcllm_cuda_rmsnorm_rows", G.ptr(xd), G.ptr(gd), C.c_float(eps), rows, h, fp16, G.ptr(out), G.stream())
+    raw = G.host(out).view(np.uint16)
+    got = raw.view(np.float16).astype(np.float32) if fp16 else (raw.astype(np.uint32) << 16).view(np.float32)
+    ss = (x.astype(np.float64) ** 2).sum(axis=1)
+    inv = (np.float32(1.0) / np.sqrt((ss / h).astype(np.float32) + np.float32(eps))).astype(np.float32)
+    v = ((x * inv[:, None]).astype(np.float32) * g[None, :]).astype(np.float32)
+    want = bf16_round(v, torch.float16 if fp16 else torch.bfloat16)
+    assert np.mean(got.reshape(rows, h) == want) > 0.999
+    assert np.abs(got.reshape(rows, h) - v).max() <= 2.0 ** (-10 if fp16 else -7) * np.abs(v).max()
+    G.check_device_error()

@@ -1,16 +1,21 @@
 """Batched prefill on the tensor cores (the model's default prefill mode): the
-prompt's rows go through every layer as bf16 tcgen05 GEMMs plus batched
-RMSNorm / RoPE + KV store / causal attention / SiLU kernels.  The batched RoPE
-+ KV store is bit-exact against the oracle and the causal attention within
-bf16 rounding of it; the whole chain is checked against the CPU oracle's fp32
+prompt's rows go through every layer as tcgen05 GEMMs plus batched RMSNorm /
+RoPE + KV store / causal attention / SiLU kernels.  The batched RoPE + KV
+store is bit-exact against the oracle and the causal attention within bf16
+rounding of it; the whole chain is checked against the CPU oracle's fp32
 token-by-token forward pass (logits of the first generated token, rel-L2 <=
-1e-2, the end-to-end tolerance) and against the model's own fp32 token path
-(first-layer K/V cache rows, rel-L2 <= 1e-2), including prompts longer than
-one 256-row batch.  Deeper layers' cache rows are printed, not bounded: the
-synthetic models' K rows reach norms of 1e3-4e3 after the first layer, so
-attention is close to one-hot and a bf16-sized change can move a prompt row's
-choice between near-tied positions (seen as a few rows differing by 10-40 %
-while the checked logits agree to ~1e-4)."""
+1e-2, the end-to-end tolerance, and the same first token) and against the
+model's own fp32 token path (first-layer K/V cache rows, rel-L2 <= 1e-2),
+including prompts longer than one 256-row batch.
+
+The synthetic models' K rows reach norms of 1e3-4e3 after the first layer,
+so attention is close to one-hot and positions can be nearly tied: a
+bf16-sized change of q or k flips the choice between them.  With bf16
+operands the per-sub-block rounding of the weight scales alone moved the
+logits of a 10-token 7B-shape prompt 7.5e-2 from the oracle, so the Q/K/V
+GEMMs run on fp16 operands (11 significant bits, same tensor-core rate; the
+other GEMMs stay bf16), which holds the 7B-shape prompts below within the
+1e-2 bar."""
 import ctypes as C
 
 import numpy as np
@@ -53,10 +58,9 @@ def prefill_both(cfg, prompt, types=None, seed=0x5EED + 11):
 
 def oracle_last_logits(cfg, specs, prompt, threads=8):
     ref = OracleModel(cfg, specs, threads=threads)
-    y = None
-    for pos, t in enumerate(prompt):
-        y = ref.step(t, pos)
-    return y
+    for pos, t in enumerate(prompt[:-1]):
+        ref.step(t, pos, head=False)
+    return ref.step(prompt[-1], len(prompt) - 1)
 
 
 def rope_table_dev(max_ctx, dim=128, theta=1.0e6):
@@ -149,20 +153,19 @@ def test_batched_prefill_spans_batches():
     assert b["st"].prefill_launches == 2 * (1 + 12 * SMALL["n_layers"]) + 1 + b["st"].decode_launches_per_step
 
 
-def test_batched_prefill_qwen7b_shape():
+@pytest.mark.parametrize("n_prompt,pseed", [(10, 0x7D), (24, 0x7D), (255, 0x7F)])
+def test_batched_prefill_qwen7b_shape(n_prompt, pseed):
     """Full Qwen2.5-7B layer shapes (28/4 heads: 7 q heads per KV head), two
-    layers.  The first layer's cache rows must agree with the fp32 token path
-    to bf16 precision and the first generated token with the oracle.  On this
-    prompt rows 8 and 9 of the second layer come out 20-30 % different (their
-    first-layer attention has two near-tied positions; the same rows differ
-    with 11- and 24-token prompts, so it is the data, not the batch edge), and
-    the last token's attention leans on row 8: the logits then differ from the
-    oracle by 7.5e-2.  The check is that any logits deviation above the 1e-2
-    tolerance comes with such a flipped row."""
+    layers.  The 10-token prompt is the one whose attention has near-tied
+    positions (with bf16 operands in the Q/K/V GEMMs its logits missed the
+    oracle by 7.5e-2); the 24-token prompt extends it;
+    255 rows fill one whole batch.  Logits within 1e-2 of the oracle, the
+    first token equal to the oracle's, the first layer's cache rows within
+    1e-2 of the fp32 token path."""
     import os
     cfg = dict(n_layers=2, hidden=3584, n_heads=28, n_kv_heads=4, head_dim=128, ffn=18944, vocab=152064,
                max_ctx=4096, rms_eps=1e-6, rope_theta=1.0e6)
-    prompt = [int(t) for t in O.tokens(10, 0x7D, cfg["vocab"])]
+    prompt = [int(t) for t in O.tokens(n_prompt, pseed, cfg["vocab"])]
     out, specs = prefill_both(cfg, prompt, seed=0x5EED + 12)
     b, t = out[1], out[0]
     y_ref = oracle_last_logits(cfg, specs, prompt, threads=max(8, os.cpu_count() or 8))
@@ -170,9 +173,9 @@ def test_batched_prefill_qwen7b_shape():
     kv0 = max(rel(b["kv"][0][0], t["kv"][0][0]), rel(b["kv"][0][1], t["kv"][0][1]))
     kb, kt = b["kv"][1][0].astype(np.float64), t["kv"][1][0].astype(np.float64)
     row_err = np.linalg.norm(kb - kt, axis=1) / np.linalg.norm(kt, axis=1)
-    print("7B shape batched prefill: logits rel-L2 %.2e (token path %.2e), layer-0 KV %.2e, layer-1 K rows %s"
-          % (r, rt, kv0, ["%.1e" % v for v in row_err]))
+    print("7B shape batched prefill, %d tokens: logits rel-L2 %.2e (token path %.2e), layer-0 KV %.2e, "
+          "layer-1 K rows max %.1e" % (n_prompt, r, rt, kv0, row_err.max()))
     assert kv0 <= 1e-2
+    assert r <= 1e-2
     assert b["tok"] == O.argmax(y_ref)[0] == t["tok"]
-    assert r <= 1e-2 or row_err.max() > 0.1
     assert b["st"].prefill_graph_launches == 1
