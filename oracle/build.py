@@ -1,9 +1,11 @@
 """Build recipe for the oracle (TEST INFRASTRUCTURE ONLY).
 
-Two libraries:
+Three libraries:
 
 * ``oracle/lib/liborc.so`` -- the C restatement in ``oracle/orc.c``.  It needs
   only gcc and is rebuilt wherever it is missing (also on a GPU box).
+* ``oracle/_ref/libref_policy.so`` -- the reference's OWN policy engine and
+  Q4 FFN-down registration (``oracle/ref_policy.cpp``), same conditions.
 * ``oracle/_ref/libref_cpu.so`` -- the reference's OWN CPU code, compiled in
   place from an ArcLLM checkout (``--reference``, ``ARCLLM_REFERENCE_DIR``, or
   a ``reference`` directory beside this repository)
@@ -22,6 +24,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORC_SO = os.path.join(HERE, "lib", "liborc.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_cpu.so")
+REF_POLICY_SO = os.path.join(HERE, "_ref", "libref_policy.so")
 
 
 def default_reference():
@@ -73,6 +76,26 @@ def build_ref(reference=None, force=False):
     return REF_SO
 
 
+def build_ref_policy(reference=None, force=False):
+    """Compile the reference's generic policy engine (v4), primitive registry
+    (v2) and the Q4 FFN-down registration in place through
+    oracle/ref_policy.cpp; returns the .so path or None without a checkout."""
+    reference = reference or default_reference()
+    if not reference:
+        return None
+    src_dir = os.path.join(reference, "src")
+    if not os.path.isfile(os.path.join(src_dir, "arcllm_v1_generic_policy_engine_v4.cpp")):
+        return None
+    wrap = os.path.join(HERE, "ref_policy.cpp")
+    if not force and os.path.exists(REF_POLICY_SO) and os.path.getmtime(REF_POLICY_SO) >= os.path.getmtime(wrap):
+        return REF_POLICY_SO
+    os.makedirs(os.path.dirname(REF_POLICY_SO), exist_ok=True)
+    tmp = REF_POLICY_SO + ".tmp%d" % os.getpid()
+    _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-w", "-I", src_dir, wrap, "-o", tmp])
+    os.replace(tmp, REF_POLICY_SO)
+    return REF_POLICY_SO
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=None)
@@ -80,6 +103,7 @@ def main(argv=None):
     a = ap.parse_args(argv)
     print("orc:", build_orc(a.force))
     print("ref:", build_ref(a.reference, a.force))
+    print("ref policy:", build_ref_policy(a.reference, a.force))
 
 
 if __name__ == "__main__":
