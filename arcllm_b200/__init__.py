@@ -81,6 +81,11 @@ SIGNATURES = {
     "arcllm_cuda_model_logits": [_vp, C.POINTER(_vp)],
     "arcllm_cuda_model_kv_cache": [_vp, C.POINTER(_vp), C.POINTER(_vp)],
     "arcllm_cuda_model_shard_lm_head": [_vp, _u32, _u32],
+    "arcllm_cuda_model_tp_exchange_words": [_vp, _u32, C.POINTER(_u32)],
+    "arcllm_cuda_model_set_tensor_parallel": [_vp, _vp, _u32, _u32, _u32],
+    "arcllm_cuda_exchange_buffer_bytes": [_u32, C.POINTER(C.c_uint64)],
+    "arcllm_cuda_exchange_gather": [_vp, _u32, _u32, _u32, _vp, _u32, _u32, _vp, _u32, _u32, _vp],
+    "arcllm_cuda_shard_rows": [_u32, _u32, _u32, _u32, C.POINTER(_u32), C.POINTER(_u32)],
 }
 _RESTYPE = {
     "arcllm_cuda_status_string": C.c_char_p,

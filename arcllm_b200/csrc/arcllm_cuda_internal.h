@@ -110,6 +110,20 @@ int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows
 int matvec_launch(const MatvecPlan& pl, const void* w0, const void* w1, const float* x, const float* gamma,
                   float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
 
+// Rank exchange over NVLink peer stores (exchange.cu).  bufs[q]: rank q's
+// exchange buffer as this process maps it (its own allocation for q == rank),
+// exchange_buffer_bytes(max_words) bytes, 256-byte aligned, zero-filled once.
+struct ExchangeRanks {
+    void* bufs[8];
+    uint32_t n_ranks, rank, max_words, timeout_us;
+};
+uint64_t exchange_buffer_bytes(uint32_t max_words);
+// dst[0, n_total) on every rank = the slices src[0, n_local) that each rank
+// contributes at its offset `off` (32-bit words).
+int exchange_gather(const ExchangeRanks& ex, const void* src, uint32_t n_local, uint32_t off, void* dst,
+                    uint32_t n_total, cudaStream_t stream);
+int shard_rows(uint32_t n, uint32_t align, uint32_t n_ranks, uint32_t rank, uint32_t* row0, uint32_t* rows);
+
 // cuTensorMapEncodeTiled (driver entry point), or null (gemm_tcgen05.cu).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -143,6 +157,9 @@ int model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_pr
                 cudaStream_t st);
 int model_step(arcllm_cuda_model* m, int with_head, int use_graph, cudaStream_t st);
 int model_prefill(arcllm_cuda_model* m, cudaStream_t st, bool* batched_out);
+int model_tp_exchange_words(const arcllm_cuda_model_config* cfg, uint32_t n_ranks, uint32_t* out);
+int model_set_tensor_parallel(arcllm_cuda_model* m, void* const* rank_bufs, uint32_t n_ranks, uint32_t rank,
+                              uint32_t timeout_us);
 int model_generate(arcllm_cuda_model* m, const uint32_t* prompt_host, uint32_t n_prompt, uint32_t max_new,
                    uint32_t* out_host, arcllm_cuda_gen_stats* stats, cudaStream_t st);
 int model_set_prefill_mode(arcllm_cuda_model* m, int mode);

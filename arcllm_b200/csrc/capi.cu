@@ -233,6 +233,37 @@ int arcllm_cuda_ipc_close_handle(void* dev_ptr) {
     ARC_GUARD_END
 }
 
+int arcllm_cuda_exchange_buffer_bytes(uint32_t max_words, uint64_t* out) {
+    ARC_GUARD_BEGIN
+    if (!out || max_words == 0) return set_error(ARC_E_INVALID_ARGUMENT, "exchange_buffer_bytes: bad argument");
+    *out = arc::exchange_buffer_bytes(max_words);
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_exchange_gather(void* const* rank_bufs, uint32_t n_ranks, uint32_t rank, uint32_t max_words,
+                                const void* src, uint32_t n_local, uint32_t offset, void* dst, uint32_t n_total,
+                                uint32_t timeout_us, void* stream) {
+    ARC_GUARD_BEGIN
+    if (!rank_bufs || n_ranks == 0 || n_ranks > 8 || rank >= n_ranks)
+        return set_error(ARC_E_INVALID_ARGUMENT, "exchange_gather: 1..8 ranks, rank < n_ranks");
+    arc::ExchangeRanks ex{};
+    for (uint32_t q = 0; q < n_ranks; ++q) ex.bufs[q] = rank_bufs[q];
+    ex.n_ranks = n_ranks;
+    ex.rank = rank;
+    ex.max_words = max_words;
+    ex.timeout_us = timeout_us;
+    return arc::exchange_gather(ex, src, n_local, offset, dst, n_total, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_shard_rows(uint32_t n, uint32_t align, uint32_t n_ranks, uint32_t rank, uint32_t* row0,
+                           uint32_t* rows) {
+    ARC_GUARD_BEGIN
+    return arc::shard_rows(n, align, n_ranks, rank, row0, rows);
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_matvec_q4k(const void* w, uint32_t rows, uint32_t k, const float* x, const float* bias, float* y,
                            void* stream) {
     return arcllm_cuda_matvec(ARC_GGML_Q4_K, w, rows, k, x, nullptr, 0.f, bias, nullptr, y, stream);
@@ -509,6 +540,19 @@ int arcllm_cuda_model_begin(arcllm_cuda_model* m, const uint32_t* prompt_host, u
                             void* stream) {
     ARC_GUARD_BEGIN
     return arc::model_begin(m, prompt_host, n_prompt, max_new, static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_tp_exchange_words(const arcllm_cuda_model_config* cfg, uint32_t n_ranks, uint32_t* out) {
+    ARC_GUARD_BEGIN
+    return arc::model_tp_exchange_words(cfg, n_ranks, out);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_model_set_tensor_parallel(arcllm_cuda_model* m, void* const* rank_bufs, uint32_t n_ranks,
+                                          uint32_t rank, uint32_t timeout_us) {
+    ARC_GUARD_BEGIN
+    return arc::model_set_tensor_parallel(m, rank_bufs, n_ranks, rank, timeout_us);
     ARC_GUARD_END
 }
 

@@ -303,8 +303,8 @@ __device__ __forceinline__ uint32_t f2ord(float f) {
 
 // key = ord(value) << 32 | ~index : atomicMax keeps the largest value and,
 // among equal values, the smallest index (the reference's strict '>' scan).
-__global__ void argmax_key_kernel(const float* __restrict__ logits, uint32_t n, unsigned long long* key_out,
-                                  uint32_t* nonfinite_out) {
+__global__ void argmax_key_kernel(const float* __restrict__ logits, uint32_t n, uint32_t base,
+                                  unsigned long long* key_out, uint32_t* nonfinite_out) {
     pdl_trigger();
     pdl_wait();  // inputs come from the preceding kernels
     unsigned long long best = 0ull;
@@ -315,7 +315,7 @@ __global__ void argmax_key_kernel(const float* __restrict__ logits, uint32_t n, 
             nonfinite = 1u;
             continue;
         }
-        const unsigned long long key = ((unsigned long long)f2ord(v) << 32) | (unsigned long long)(~i);
+        const unsigned long long key = ((unsigned long long)f2ord(v) << 32) | (unsigned long long)(~(base + i));
         best = key > best ? key : best;
     }
 #pragma unroll
@@ -328,6 +328,26 @@ __global__ void argmax_key_kernel(const float* __restrict__ logits, uint32_t n, 
         if (best) atomicMax(key_out, best);
         if (nonfinite) atomicOr(nonfinite_out, 1u);
     }
+}
+
+// Tensor-parallel greedy select: the ranks' (nonfinite, pad, key lo, key hi)
+// records, gathered in rank order, combined into this rank's state -- the
+// largest key (the first index of the maximum over all shards, since each
+// key carries the complemented global index) and any non-finite flag.
+__global__ void greedy_combine_kernel(GreedyState* st, const uint32_t* __restrict__ recs, uint32_t n_ranks) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    unsigned long long best = 0ull;
+    uint32_t nonfinite = 0;
+    for (uint32_t q = 0; q < n_ranks; ++q) {
+        nonfinite |= recs[4u * q];
+        const unsigned long long key = (unsigned long long)recs[4u * q + 2u] |
+                                       ((unsigned long long)recs[4u * q + 3u] << 32);
+        best = key > best ? key : best;
+    }
+    st->argmax_key = best;
+    st->nonfinite |= nonfinite;
 }
 
 // Advance the decode state by one token: next token = prompt[pos+1] while the
@@ -379,6 +399,7 @@ int decode_ops_prepare() {
         e = cudaFuncSetAttribute(attn_partial_kernel<8, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, argmax_key_kernel);
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, greedy_finalize_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, greedy_combine_kernel);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "decode ops prepare");
 }
 
@@ -530,9 +551,15 @@ int attention_launches(uint32_t n_splits, uint32_t q_heads, uint32_t kv_heads) {
 }
 
 int launch_argmax(const float* logits, uint32_t n, unsigned long long* key, uint32_t* nonfinite,
-                  cudaStream_t stream) {
-    return launch_checked(launch_kernel(argmax_key_kernel, dim3(148), dim3(256), 0, stream, logits, n, key, nonfinite),
-                          "argmax launch");
+                  cudaStream_t stream, uint32_t base) {
+    return launch_checked(
+        launch_kernel(argmax_key_kernel, dim3(148), dim3(256), 0, stream, logits, n, base, key, nonfinite),
+        "argmax launch");
+}
+
+int launch_greedy_combine(GreedyState* st, const uint32_t* recs, uint32_t n_ranks, cudaStream_t stream) {
+    return launch_checked(launch_kernel(greedy_combine_kernel, dim3(1), dim3(32), 0, stream, st, recs, n_ranks),
+                          "greedy combine launch");
 }
 
 int launch_greedy_finalize(GreedyState* st, const uint32_t* prompt, uint32_t* out_tokens, uint32_t max_out,

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <cstddef>
 #include <cstdint>
 
 namespace arc {
@@ -17,6 +18,10 @@ struct alignas(16) GreedyState {
     uint32_t pad;
     unsigned long long argmax_key;  // packed (ordered value, ~index), reset by the finalize step
 };
+
+// The tensor-parallel greedy select exchanges words 4..7 (nonfinite, pad, argmax_key).
+static_assert(offsetof(GreedyState, nonfinite) == 16 && offsetof(GreedyState, argmax_key) == 24,
+              "GreedyState layout");
 
 struct RopeKvShape {
     uint32_t q_heads, kv_heads, head_dim, max_ctx, layer;
@@ -46,7 +51,10 @@ int launch_attention(const float* q, const uint16_t* kc, const uint16_t* vc, con
 // key: max over i of (ordered(logits[i]) << 32 | ~i) via atomicMax (caller zeroes it);
 // nonfinite: bit 0 set when a non-finite logit is seen.
 int launch_argmax(const float* logits, uint32_t n, unsigned long long* key, uint32_t* nonfinite,
-                  cudaStream_t stream);
+                  cudaStream_t stream, uint32_t base = 0);
+// Tensor-parallel greedy select: combine the ranks' gathered (nonfinite, pad, key lo, key hi)
+// records (GreedyState words 4..7 of every rank) into st
+int launch_greedy_combine(GreedyState* st, const uint32_t* recs, uint32_t n_ranks, cudaStream_t stream);
 int launch_greedy_finalize(GreedyState* st, const uint32_t* prompt, uint32_t* out_tokens, uint32_t max_out,
                            cudaStream_t stream);
 

@@ -551,13 +551,17 @@ int matvec_any(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows
     // measured on B200: Q4_K 16.4 us against 27.5 us on CUDA cores, Q6_K
     // 20.7 us against 22.4 us); the CUDA-core streaming kernel otherwise.
     // ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core kernel.
-    if (fmt == ARC_TYPE_EXEC148) {  // route B of the Q4 FFN-down capability
-        if (dual || gamma || bias) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec EXEC148: no gamma, bias or dual");
-        return exec148_matvec(w0, rows, k, x, residual, y, stream);
-    }
     const char* env = std::getenv("ARCLLM_MATVEC_IMPL");
     const int impl = (env && std::strcmp(env, "cuda") == 0) ? 0 : 1;
     const bool x_aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma)) & 15u) == 0u;
+    if (fmt == ARC_TYPE_EXEC148) {  // route B of the Q4 FFN-down capability
+        if (dual || gamma || bias) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec EXEC148: no gamma, bias or dual");
+        // the K-slice integer-MMA kernel where its shape rules hold, else the CUDA-core kernel
+        if (impl >= 1 && x_aligned && (reinterpret_cast<uintptr_t>(w0) & 15u) == 0u &&
+            matvec_splitk_supported(fmt, false, rows, k))
+            return matvec_splitk_launch(fmt, w0, rows, k, x, nullptr, 0.f, nullptr, residual, y, stream);
+        return exec148_matvec(w0, rows, k, x, residual, y, stream);
+    }
     if (impl >= 1 && x_aligned && matvec_imma_supported(fmt, dual, rows, k))
         return matvec_imma_launch(fmt, dual, w0, w1, rows, k, x, gamma, eps, bias, residual, y, stream);
     if (impl >= 1 && x_aligned && matvec_splitk_supported(fmt, dual, rows, k))

@@ -129,7 +129,7 @@ __device__ __forceinline__ void quantize8(const float (&v)[8], uint32_t lane, ui
         make_uint2(pack4(l1[0], l1[1], l1[2], l1[3]), pack4(l1[4], l1[5], l1[6], l1[7]));
     *reinterpret_cast<uint2*>(planes + 512 + o) =
         make_uint2(pack4(l2[0], l2[1], l2[2], l2[3]), pack4(l2[4], l2[5], l2[6], l2[7]));
-    if (FMT == 12) {
+    if (FMT != 14) {  // Q4_K and EXEC148: one scale per 32-element window
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     } else {  // 16-element scale groups: lanes (q, q^1) of a window share one
@@ -221,6 +221,89 @@ __device__ __forceinline__ void gather_xfrag(const uint8_t* pA, const float* kA,
         }
         f.xs[0] = f.xs[1] = 0.f;
     }
+}
+
+// Routed B fragments for the EXEC148 layout (148-byte blocks: d, dmin, eight
+// (sc, mn) bytes, then window j's 32 codes as 16 bytes of element pairs,
+// byte b = q[2b] | q[2b+1] << 4).  MMA m = 2p + hh of a block takes the 32
+// code bytes of windows 2p, 2p+1: k slot 4u+i <- byte 8u+i, slot 16+4u+i <-
+// byte 8u+4+i, low nibbles (hh = 0: even elements) or high nibbles shifted
+// down (hh = 1: odd elements).  Byte b of that span is byte b & 15 of window
+// 2p + (b >> 4), so lane (g, t) (column pair c = g >> 1, limb g & 1) carries
+// window w = 2p + (t >> 1) -- elements 16(t&1) + hh + 2i (b0) and
+// 16(t&1) + 8 + hh + 2i (b1), i = 0..3 -- when w & 3 == c, zeros otherwise.
+// Windows 4i .. 4i+3 accumulate in D[i], so lane t applies the scales of
+// windows t and 4 + t, as for Q4_K.
+__device__ __forceinline__ void gather_xfrag_e148(const uint8_t* pl, const float* kc, uint32_t lane, XFrag& f) {
+    const uint32_t g = lane >> 2, t = lane & 3u, c = g >> 1, L = g & 1u;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const uint32_t w = 2u * p + (t >> 1);
+        const bool on = (w & 3u) == c;
+        const uint4 q1 = *reinterpret_cast<const uint4*>(pl + 256u * L + 32u * w + 16u * (t & 1u));
+        const uint4 q2 = L == 0 ? *reinterpret_cast<const uint4*>(pl + 512u + 32u * w + 16u * (t & 1u))
+                                : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const uint32_t sel = hh ? 0x7531u : 0x6420u;  // odd or even bytes of a word pair
+            const int m = 2 * p + hh;
+            f.b1[m][0] = on ? __byte_perm(q1.x, q1.y, sel) : 0u;
+            f.b1[m][1] = on ? __byte_perm(q1.z, q1.w, sel) : 0u;
+            f.b2[m][0] = on ? __byte_perm(q2.x, q2.y, sel) : 0u;
+            f.b2[m][1] = on ? __byte_perm(q2.z, q2.w, sel) : 0u;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t w = 4u * i + t;
+        f.sx[i] = kc[6 * w];
+        f.xs[i] = kc[6 * w + 1];
+    }
+    f.sx[2] = f.sx[3] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f.xh[i] = f.xl[i] = 0;
+}
+
+// One 16-row tile x one EXEC148 block (row offsets r0, r1 of the block in the
+// stage, 4-byte aligned): adds the rows' partial dot products (windows t and
+// 4 + t of this lane) to y0 and y1.  w = d*sc*q - dmin*mn as for Q4_K
+// (shaders/q4_down_exec148_serial.comp:6 computes the same per element).
+__device__ __forceinline__ void e148_tile(const uint8_t* st, uint32_t r0, uint32_t r1, uint32_t t, const XFrag& f,
+                                          float& y0, float& y1) {
+    constexpr uint32_t K = 0x0F0F0F0Fu;
+    int D1[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, D2[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const uint32_t o = 20u + 32u * p + 8u * t;
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(st + r0 + o);
+        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(st + r0 + o + 4u);
+        const uint32_t a1 = *reinterpret_cast<const uint32_t*>(st + r1 + o);
+        const uint32_t a3 = *reinterpret_cast<const uint32_t*>(st + r1 + o + 4u);
+        const int i = p >> 1;
+        imma(D1[i], a0 & K, a1 & K, a2 & K, a3 & K, f.b1[2 * p][0], f.b1[2 * p][1]);
+        imma(D2[i], a0 & K, a1 & K, a2 & K, a3 & K, f.b2[2 * p][0], f.b2[2 * p][1]);
+        imma(D1[i], (a0 >> 4) & K, (a1 >> 4) & K, (a2 >> 4) & K, (a3 >> 4) & K, f.b1[2 * p + 1][0],
+             f.b1[2 * p + 1][1]);
+        imma(D2[i], (a0 >> 4) & K, (a1 >> 4) & K, (a2 >> 4) & K, (a3 >> 4) & K, f.b2[2 * p + 1][0],
+             f.b2[2 * p + 1][1]);
+    }
+    float out[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint8_t* blk = st + (r ? r1 : r0);
+        const uint32_t hd = *reinterpret_cast<const uint32_t*>(blk);
+        const float d = __half2float(__ushort_as_half((unsigned short)(hd & 0xffffu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd >> 16)));
+        const uint32_t s0 = *reinterpret_cast<const unsigned short*>(blk + 4u + 2u * t);   // (sc, mn) of window t
+        const uint32_t s1 = *reinterpret_cast<const unsigned short*>(blk + 12u + 2u * t);  // window 4 + t
+        const float F0 = combine(D1[0][2 * r], D1[0][2 * r + 1], D2[0][2 * r], 0, 0);
+        const float F1 = combine(D1[1][2 * r], D1[1][2 * r + 1], D2[1][2 * r], 0, 0);
+        const float tt = fmaf((float)(s0 & 255u) * f.sx[0], F0, ((float)(s1 & 255u) * f.sx[1]) * F1);
+        const float uu = fmaf((float)(s0 >> 8), f.xs[0], (float)(s1 >> 8) * f.xs[1]);
+        out[r] = fmaf(d, tt, -dmin * uu);
+    }
+    y0 += out[0];
+    y1 += out[1];
 }
 
 // The four 4-code words of one (ql word a, ql word b = a + 32 bytes, qh word)

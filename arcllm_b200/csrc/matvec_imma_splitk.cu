@@ -174,11 +174,17 @@ __device__ __forceinline__ void ks_close(const MvParams& p, const KSlice& q, uin
     }
 }
 
+// Block bytes and tensor-map super-row height per format: Q4_K 144 B rows of
+// 16-byte multiples (Rs 1), Q6_K 210 B (rows 4 mod 16: Rs 4), the EXEC148
+// image 148 B (rows of 74 blocks are 8 mod 16: Rs 2).
+__host__ __device__ constexpr uint32_t ks_bsz(int fmt) { return fmt == 12 ? 144u : fmt == 14 ? 210u : 148u; }
+__host__ __device__ constexpr uint32_t ks_rs(int fmt) { return fmt == 12 ? 1u : fmt == 14 ? 4u : 2u; }
+
 template <int FMT>
 __global__ void __launch_bounds__((kNW + 1) * 32, 1)
     matvec_imma_kslice_kernel(const MvParams p, const __grid_constant__ KSlice q, const __grid_constant__ KMaps maps) {
-    constexpr uint32_t bsz = FMT == 12 ? 144u : 210u;
-    constexpr uint32_t Rs = FMT == 12 ? 1u : 4u;  // rows per tensor-map super-row
+    constexpr uint32_t bsz = ks_bsz(FMT);
+    constexpr uint32_t Rs = ks_rs(FMT);  // rows per tensor-map super-row
     constexpr uint32_t J = kG / Rs;               // box rows
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -312,7 +318,10 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1)
         float* kc = reinterpret_cast<float*>(xs + 768);
         quantize8<FMT>(v, lane, xs, kc);
         __syncwarp();
-        gather_xfrag<FMT>(xs, kc, xs, kc, lane, f);
+        if (FMT == ARC_TYPE_EXEC148)
+            gather_xfrag_e148(xs, kc, lane, f);
+        else
+            gather_xfrag<FMT>(xs, kc, xs, kc, lane, f);
     }
     // this warp's column of the slice (Q6_K columns split at even blocks, so
     // blocks w and w^1 share one), and where a row of it sits in a stage:
@@ -352,6 +361,8 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1)
             const uint32_t row0 = rowA[m], row1 = rowB[m];
             if (FMT == 12)
                 q4_tile(st, row0 + offA, row1 + offA, t, f, y[m][0], y[m][1]);
+            else if (FMT == ARC_TYPE_EXEC148)
+                e148_tile(st, row0 + offA, row1 + offA, t, f, y[m][0], y[m][1]);
             else if (oddA)
                 q6_tile_lowreg<true>(st, row0, row1, offA, offB, t, f, y[m][0], y[m][1]);
             else
@@ -398,9 +409,9 @@ struct KsPlan {
 // (Q4_K: 8 or 24 words mod 32 for the 64-bit half-warp reads; Q6_K: an odd
 // multiple of 4 words for rows 4 apart).
 uint32_t ks_box_bytes(int fmt, uint32_t wb) {
-    const uint32_t bsz = fmt == 12 ? 144u : 210u;
+    const uint32_t bsz = ks_bsz(fmt);
     uint32_t bw = (wb * bsz + (fmt == 12 ? 0u : 12u) + 15u) & ~15u;
-    if (fmt == 12)
+    if (fmt != 14)
         while ((bw / 4u) % 32u != 8u && (bw / 4u) % 32u != 24u) bw += 16u;
     else
         while (((bw / 16u) & 1u) == 0u) bw += 16u;
@@ -459,15 +470,19 @@ KsPlan ks_plan(int fmt, uint32_t rows, uint32_t k, uint32_t sms) {
     }
     // box columns: Q4_K one (14 x 144 B = 2016 B fits a box row), Q6_K up to
     // two of <= 8 blocks, split in pairs as evenly as possible
-    const uint32_t colmax = fmt == 12 ? kNW : 8u;
+    const uint32_t colmax = fmt == 12 ? kNW : fmt == 14 ? 8u : 13u;  // box rows of <= 2 KB
     uint32_t stage = 0;
     for (uint32_t s = 0; s < pl.q.P; ++s) {
         const uint32_t Wd = pl.q.W[s];
         const uint32_t ncol = (Wd + colmax - 1u) / colmax;
         uint32_t wcol[2] = {Wd, 0u};
         if (ncol == 2) {
-            const uint32_t pairs = Wd / 2u;
-            wcol[0] = 2u * ((pairs + 1u) / 2u);
+            if (fmt == 14) {
+                const uint32_t pairs = Wd / 2u;
+                wcol[0] = 2u * ((pairs + 1u) / 2u);
+            } else {
+                wcol[0] = (Wd + 1u) / 2u;
+            }
             wcol[1] = Wd - wcol[0];
         }
         pl.q.ncol[s] = (uint8_t)ncol;
@@ -574,17 +589,20 @@ int matvec_splitk_prepare() {
     if (done[dev & 63]) return ARC_OK;
     cudaError_t e = set_attr_ks<12>();
     if (e == cudaSuccess) e = set_attr_ks<14>();
+    if (e == cudaSuccess) e = set_attr_ks<ARC_TYPE_EXEC148>();
     if (e != cudaSuccess) return set_cuda_error(e, "matvec split-K prepare");
     done[dev & 63] = true;
     return ARC_OK;
 }
 
 // Single matrix, K > 3584; Q6_K: an even number of super-blocks and a
-// multiple of 4 rows (the tensor-map super-rows).
+// multiple of 4 rows (the tensor-map super-rows).  The EXEC148 image (no
+// whole-row form): any K, an even number of rows.
 bool matvec_splitk_supported(int fmt, bool dual, uint32_t rows, uint32_t k) {
-    if ((fmt != 12 && fmt != 14) || dual || rows == 0 || k % 256u) return false;
+    if ((fmt != 12 && fmt != 14 && fmt != ARC_TYPE_EXEC148) || dual || rows == 0 || k % 256u) return false;
     const uint32_t nb = k / 256u;
-    if (nb <= 14 || (fmt == 14 && ((nb & 1u) || (rows & 3u)))) return false;
+    if (fmt == ARC_TYPE_EXEC148 && (rows & 1u)) return false;
+    if ((fmt != ARC_TYPE_EXEC148 && nb <= 14) || (fmt == 14 && ((nb & 1u) || (rows & 3u)))) return false;
     if (nb > kNW * kMaxSlices) return false;
     return ks_plan_cached(fmt, rows, k, 148).ok;
 }
@@ -604,7 +622,7 @@ int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, cons
     EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(ARC_E_CUDA, "matvec split-K: cuTensorMapEncodeTiled unavailable");
     // the matrix as u64 words in super-rows of Rs rows (Rs * row bytes is a multiple of 16)
-    const uint32_t nb = k / 256u, rb = nb * (fmt == 12 ? 144u : 210u), Rs = fmt == 12 ? 1u : 4u;
+    const uint32_t nb = k / 256u, rb = nb * ks_bsz(fmt), Rs = ks_rs(fmt);
     KMaps maps;
     std::memset(&maps, 0, sizeof maps);
     for (uint32_t i = 0; i < pl.nmaps; ++i) {
@@ -644,8 +662,10 @@ int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, cons
     p.early = pdl_enabled() ? 1u : 0u;
     const dim3 block((kNW + 1) * 32);
     const cudaError_t e =
-        fmt == 12 ? launch_kernel(matvec_imma_kslice_kernel<12>, dim3(pl.grid), block, pl.smem, stream, p, pl.q, maps)
-                  : launch_kernel(matvec_imma_kslice_kernel<14>, dim3(pl.grid), block, pl.smem, stream, p, pl.q, maps);
+        fmt == 12   ? launch_kernel(matvec_imma_kslice_kernel<12>, dim3(pl.grid), block, pl.smem, stream, p, pl.q, maps)
+        : fmt == 14 ? launch_kernel(matvec_imma_kslice_kernel<14>, dim3(pl.grid), block, pl.smem, stream, p, pl.q, maps)
+                    : launch_kernel(matvec_imma_kslice_kernel<ARC_TYPE_EXEC148>, dim3(pl.grid), block, pl.smem, stream,
+                                    p, pl.q, maps);
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "matvec split-K launch");
 }
 

@@ -69,6 +69,13 @@ struct arcllm_cuda_model {
     uint16_t *pf_xb = nullptr, *pf_attn = nullptr, *pf_s = nullptr;
     uint32_t launches_prefill_batched = 0;
     uint32_t begun_prompt = 0;  // prompt length of the last begin() (0: none)
+
+    // tensor parallelism (tp.n_ranks > 1): this rank's FFN gate/up rows [ffn_r0, +ffn_rows) and
+    // FFN down rows [hid_r0, +hid_rows) (its LM-head rows are lm_row0/lm_rows), the ranks'
+    // exchange buffers, the gathered greedy records (4 words per rank)
+    arc::ExchangeRanks tp{};
+    uint32_t ffn_r0 = 0, ffn_rows = 0, hid_r0 = 0, hid_rows = 0;
+    uint32_t* tp_recs = nullptr;
 };
 
 namespace arc {
@@ -77,6 +84,16 @@ namespace {
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 bool quant_ok(int t) { return t == ARC_GGML_Q4_K || t == ARC_GGML_Q6_K; }
+
+// Bytes of one row of k weights (Q4_K, Q6_K or the EXEC148 image).
+uint64_t row_bytes(int type, uint32_t k) {
+    const uint64_t blk = type == ARC_GGML_Q4_K ? 144u : type == ARC_GGML_Q6_K ? 210u : 148u;
+    return (uint64_t)(k / 256u) * blk;
+}
+
+// Rows of a tensor-parallel shard are whole 32-row groups (the matvecs' row
+// groups; keeps every shard's weight rows and vector slices 16-byte aligned).
+constexpr uint32_t kTpRowAlign = 32;
 
 int check_layer(const arcllm_cuda_model_config& c, const arcllm_cuda_layer& L) {
     if (!L.attn_norm || !L.ffn_norm || !L.wq || !L.wk || !L.wv || !L.wo || !L.w_gate || !L.w_up || !L.w_down)
@@ -168,16 +185,44 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
                      1.0f / std::sqrt((float)c.head_dim)};
         ARC_TRY(launch_attention(m->q, m->kc, m->vc, &m->state->pos, as, m->part, m->attn, st));
         ARC_TRY(mv(L.type_o, L.wo, H, H, m->attn, nullptr, 0.f, nullptr, hc, hm, st));
-        ARC_TRY(matvec_any(ARC_GGML_Q4_K, true, L.w_gate, L.w_up, c.ffn, H, hm, L.ffn_norm, c.rms_eps, nullptr,
-                           nullptr, m->s, st));
-        ARC_TRY(mv(L.type_down, L.w_down, H, c.ffn, m->s, nullptr, 0.f, nullptr, hm, hc, st));
-        n += 6 + (uint32_t)attention_launches(m->attn_splits, c.n_heads, c.n_kv_heads);  // Q K V (attn) O gate/up down
+        n += 4 + (uint32_t)attention_launches(m->attn_splits, c.n_heads, c.n_kv_heads);  // Q K V (attn) O
+        if (m->tp.n_ranks > 1) {
+            // this rank's gate/up rows -> its slice of s; all-gather s; its down rows (+ residual)
+            // -> its slice of the hidden state; all-gather the hidden state
+            const uint64_t rb_gu = row_bytes(ARC_GGML_Q4_K, H), rb_dn = row_bytes(L.type_down, c.ffn);
+            const uint8_t* wg = static_cast<const uint8_t*>(L.w_gate) + (uint64_t)m->ffn_r0 * rb_gu;
+            const uint8_t* wu = static_cast<const uint8_t*>(L.w_up) + (uint64_t)m->ffn_r0 * rb_gu;
+            const uint8_t* wd = static_cast<const uint8_t*>(L.w_down) + (uint64_t)m->hid_r0 * rb_dn;
+            ARC_TRY(matvec_any(ARC_GGML_Q4_K, true, wg, wu, m->ffn_rows, H, hm, L.ffn_norm, c.rms_eps, nullptr,
+                               nullptr, m->s + m->ffn_r0, st));
+            ARC_TRY(exchange_gather(m->tp, m->s + m->ffn_r0, m->ffn_rows, m->ffn_r0, m->s, c.ffn, st));
+            ARC_TRY(mv(L.type_down, wd, m->hid_rows, c.ffn, m->s, nullptr, 0.f, nullptr, hm + m->hid_r0,
+                       hc + m->hid_r0, st));
+            ARC_TRY(exchange_gather(m->tp, hc + m->hid_r0, m->hid_rows, m->hid_r0, hc, H, st));
+            n += 4;
+        } else {
+            ARC_TRY(matvec_any(ARC_GGML_Q4_K, true, L.w_gate, L.w_up, c.ffn, H, hm, L.ffn_norm, c.rms_eps, nullptr,
+                               nullptr, m->s, st));
+            ARC_TRY(mv(L.type_down, L.w_down, H, c.ffn, m->s, nullptr, 0.f, nullptr, hm, hc, st));
+            n += 2;
+        }
     }
     if (with_head) {
-        ARC_TRY(mv(m->out_type, m->out_w, m->lm_rows, H, hc, m->out_norm, c.rms_eps, nullptr, nullptr,
+        const uint8_t* wo = static_cast<const uint8_t*>(m->out_w) + (uint64_t)m->lm_row0 * row_bytes(m->out_type, H);
+        ARC_TRY(mv(m->out_type, wo, m->lm_rows, H, hc, m->out_norm, c.rms_eps, nullptr, nullptr,
                    m->logits + m->lm_row0, st));
-        ARC_TRY(launch_argmax(m->logits, c.vocab, &m->state->argmax_key, &m->state->nonfinite, st));
         n += 2;
+        if (m->tp.n_ranks > 1) {
+            // the shard's argmax over global row indices, then the ranks' records gathered and combined
+            ARC_TRY(launch_argmax(m->logits + m->lm_row0, m->lm_rows, &m->state->argmax_key, &m->state->nonfinite,
+                                  st, m->lm_row0));
+            ARC_TRY(exchange_gather(m->tp, reinterpret_cast<const uint32_t*>(m->state) + 4, 4u, 4u * m->tp.rank,
+                                    m->tp_recs, 4u * m->tp.n_ranks, st));
+            ARC_TRY(launch_greedy_combine(m->state, m->tp_recs, m->tp.n_ranks, st));
+            n += 2;
+        } else {
+            ARC_TRY(launch_argmax(m->logits, c.vocab, &m->state->argmax_key, &m->state->nonfinite, st));
+        }
     }
     ARC_TRY(launch_greedy_finalize(m->state, m->prompt, m->out_tokens, c.max_ctx, st));
     ++n;
@@ -341,6 +386,7 @@ int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
     // FFN down scratch for the K-slice kernel, before any graph capture (either format)
     ARC_TRY(matvec_splitk_reserve(ARC_GGML_Q4_K, cfg->hidden, cfg->ffn));
     ARC_TRY(matvec_splitk_reserve(ARC_GGML_Q6_K, cfg->hidden, cfg->ffn));
+    ARC_TRY(matvec_splitk_reserve(ARC_TYPE_EXEC148, cfg->hidden, cfg->ffn));
     ARC_TRY(decode_ops_prepare());
     if (!dev_error_word()) return set_error(ARC_E_CUDA, "model_create: device error word unavailable");
     auto* m = new (std::nothrow) arcllm_cuda_model();
@@ -443,6 +489,59 @@ int model_set_endpoints(arcllm_cuda_model* m, const void* tok_embd, int tok_embd
     m->out_w = out_w;
     m->out_type = out_type;
     m->endpoints_set = true;
+    return ARC_OK;
+}
+
+int model_tp_exchange_words(const arcllm_cuda_model_config* cfg, uint32_t n_ranks, uint32_t* out) {
+    if (!cfg || !out || n_ranks == 0 || n_ranks > 8) return set_error(ARC_E_INVALID_ARGUMENT, "tp words: bad argument");
+    *out = std::max(std::max(cfg->ffn, cfg->hidden), 4u * n_ranks);
+    return ARC_OK;
+}
+
+int model_set_tensor_parallel(arcllm_cuda_model* m, void* const* rank_bufs, uint32_t n_ranks, uint32_t rank,
+                              uint32_t timeout_us) {
+    if (!m || n_ranks == 0 || n_ranks > 8 || rank >= n_ranks || (n_ranks > 1 && !rank_bufs))
+        return set_error(ARC_E_INVALID_ARGUMENT, "tensor parallel: 1..8 ranks, rank < n_ranks, buffers");
+    const arcllm_cuda_model_config& c = m->cfg;
+    ExchangeRanks tp{};
+    uint32_t fr0 = 0, frows = c.ffn, hr0 = 0, hrows = c.hidden, lr0 = 0, lrows = c.vocab;
+    if (n_ranks > 1) {
+        if (c.ffn % kTpRowAlign || c.hidden % kTpRowAlign || c.vocab % kTpRowAlign)
+            return set_error(ARC_E_UNSUPPORTED_SHAPE, "tensor parallel: ffn, hidden and vocab must be multiples of 32");
+        ARC_TRY(shard_rows(c.ffn, kTpRowAlign, n_ranks, rank, &fr0, &frows));
+        ARC_TRY(shard_rows(c.hidden, kTpRowAlign, n_ranks, rank, &hr0, &hrows));
+        ARC_TRY(shard_rows(c.vocab, kTpRowAlign, n_ranks, rank, &lr0, &lrows));
+        uint32_t words = 0;
+        ARC_TRY(model_tp_exchange_words(&c, n_ranks, &words));
+        for (uint32_t q = 0; q < n_ranks; ++q) {
+            if (!rank_bufs[q] || (reinterpret_cast<uintptr_t>(rank_bufs[q]) & 255u))
+                return set_error(ARC_E_ALIGNMENT, "tensor parallel: rank buffers must be 256-byte aligned");
+            tp.bufs[q] = rank_bufs[q];
+        }
+        tp.n_ranks = n_ranks;
+        tp.rank = rank;
+        tp.max_words = words;
+        tp.timeout_us = timeout_us;
+        if (!m->tp_recs) {
+            const cudaError_t e = cudaMalloc(&m->tp_recs, 4u * 4u * 8u);
+            if (e != cudaSuccess) {
+                m->tp_recs = nullptr;
+                return set_cuda_error(e, "tensor parallel: greedy records");
+            }
+        }
+    }
+    m->tp = tp;
+    m->ffn_r0 = fr0, m->ffn_rows = frows, m->hid_r0 = hr0, m->hid_rows = hrows;
+    m->lm_row0 = lr0, m->lm_rows = lrows;
+    // the captured step graphs hold the previous layout: re-capture on next use
+    if (m->g_prefill) {
+        cudaGraphExecDestroy(m->g_prefill);
+        m->g_prefill = nullptr;
+    }
+    if (m->g_decode) {
+        cudaGraphExecDestroy(m->g_decode);
+        m->g_decode = nullptr;
+    }
     return ARC_OK;
 }
 
@@ -608,6 +707,7 @@ int model_destroy(arcllm_cuda_model* m) {
     if (m->g_decode) cudaGraphExecDestroy(m->g_decode);
     if (m->arena) cudaFree(m->arena);
     if (m->pf_arena) cudaFree(m->pf_arena);
+    if (m->tp_recs) cudaFree(m->tp_recs);
     for (int i = 0; i < 2; ++i) {
         if (m->side[i]) cudaStreamDestroy(m->side[i]);
         if (m->ev_join[i]) cudaEventDestroy(m->ev_join[i]);

@@ -1,4 +1,6 @@
-"""Rank exchange buffers for the NVLink all-gather form of the LM-head matvec.
+"""Rank exchange buffers for the NVLink all-gather form of the LM-head matvec
+(RankGather) and for the vector exchange of the tensor-parallel decode
+(ExchangeBuffers).
 
 One process per GPU.  Each rank allocates one exchange buffer (fp32 logits of
 all rows, then the per-rank flag array and its CTA counter), shares a CUDA IPC
@@ -99,3 +101,63 @@ class RankGather:
         for own in self._own:
             call("arcllm_cuda_free", own)
         self._own = []
+
+
+class ExchangeBuffers:
+    """One exchange buffer per rank for arcllm_cuda_exchange_gather and the
+    tensor-parallel model (arcllm_cuda_model_set_tensor_parallel).
+
+    Each rank allocates `arcllm_cuda_exchange_buffer_bytes(max_words)` bytes,
+    zero-fills them, shares a CUDA IPC handle through `exchange` (the caller's
+    host all-gather of bytes, as for RankGather) and maps the peers' buffers;
+    `ptrs` is then the rank-ordered array of device addresses the C ABI takes.
+    The sequence numbers and flags of the exchanges live inside the buffers,
+    so nothing else needs to be carried between calls.
+    """
+
+    def __init__(self, max_words, n_ranks, rank, exchange):
+        if not (1 <= n_ranks <= 8 and 0 <= rank < n_ranks):
+            raise ValueError("ExchangeBuffers: 1 <= n_ranks <= 8 and 0 <= rank < n_ranks")
+        L = lib()
+        self.max_words, self.n_ranks, self.rank = max_words, n_ranks, rank
+        n = C.c_uint64(0)
+        call("arcllm_cuda_exchange_buffer_bytes", max_words, C.byref(n))
+        self.nbytes = n.value
+        own = C.c_void_p()
+        call("arcllm_cuda_malloc", self.nbytes, C.byref(own))
+        self._own, self._opened = own, []
+        zeros = (C.c_uint8 * self.nbytes)()
+        call("arcllm_cuda_memcpy_h2d", own, C.cast(zeros, C.c_void_p), self.nbytes, None)
+        call("arcllm_cuda_stream_synchronize", None)
+        h = (C.c_uint8 * HANDLE_BYTES)()
+        call("arcllm_cuda_ipc_get_handle", own, C.cast(h, C.c_void_p))
+        everyone = exchange(bytes(h))
+        if len(everyone) != n_ranks:
+            raise RuntimeError("ExchangeBuffers: exchange returned %d entries for %d ranks" % (len(everyone), n_ranks))
+        ptrs = []
+        for r, hb in enumerate(everyone):
+            if r == rank:
+                ptrs.append(own.value)
+                continue
+            p = C.c_void_p()
+            hbuf = (C.c_uint8 * HANDLE_BYTES).from_buffer_copy(hb[:HANDLE_BYTES])
+            call("arcllm_cuda_ipc_open_handle", C.cast(hbuf, C.c_void_p), C.byref(p))
+            self._opened.append(p)
+            ptrs.append(p.value)
+        self.ptrs = (C.c_void_p * n_ranks)(*ptrs)
+        self._L = L
+
+    def gather(self, src, n_local, offset, dst, n_total, stream, timeout_us=2000000):
+        """dst[0, n_total) = every rank's 32-bit-word slice at its offset."""
+        call("arcllm_cuda_exchange_gather", self.ptrs, self.n_ranks, self.rank, self.max_words, src, n_local, offset,
+             dst, n_total, timeout_us, stream)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's.  Call only after
+        every rank finished its last exchange (a host barrier)."""
+        for p in self._opened:
+            call("arcllm_cuda_ipc_close_handle", p)
+        self._opened = []
+        if self._own is not None:
+            call("arcllm_cuda_free", self._own)
+            self._own = None

@@ -166,6 +166,19 @@ class SyntheticModel:
         pa = (C.c_uint32 * len(prompt))(*prompt)
         call("arcllm_cuda_model_begin", self.h, pa, len(prompt), max_new, self.stream)
 
+    def set_tensor_parallel(self, ptrs, n_ranks, rank, timeout_us=2000000):
+        """Shard the FFN and LM head over n_ranks (ptrs: ExchangeBuffers.ptrs
+        with max_words from tp_exchange_words); n_ranks 1 turns it off."""
+        call("arcllm_cuda_model_set_tensor_parallel", self.h, ptrs, n_ranks, rank, timeout_us)
+
+    def tp_exchange_words(self, n_ranks):
+        c = self.cfg
+        mc = ModelConfig(c["n_layers"], c["hidden"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["ffn"],
+                         c["vocab"], c["max_ctx"], c["rms_eps"], c["rope_theta"])
+        out = C.c_uint32(0)
+        call("arcllm_cuda_model_tp_exchange_words", C.byref(mc), n_ranks, C.byref(out))
+        return out.value
+
     def prefill(self):
         """after begin(): consume the prompt but its last token as generate() does"""
         call("arcllm_cuda_model_prefill", self.h, self.stream)

@@ -350,6 +350,24 @@ def main(argv=None):
                         "matvec")
         graph.replay()  # upload; an untimed pass like the warm-up steps
         torch.cuda.synchronize()
+    elif args.launch == "graph" and rg is not None:
+        # N>1 with the fused all-gather: every launch carries its own epoch, so the K timed launches are
+        # captured with epochs e+K+1 .. e+2K after an untimed graph of epochs e+1 .. e+K, and each graph is
+        # replayed exactly once (every rank captures the same sequence).  Host launch gaps, which the flag
+        # handshake would otherwise turn into waits of the other ranks, stay out of the timed region.
+        graphs = []
+        for _ in range(2):
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_, capture_error_mode="thread_local"):
+                cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+                for _ in range(args.steps):
+                    rg.step(wp, rows_per, K, xp, r0, cs, TY)
+            graphs.append(g_)
+        barrier()
+        graphs[0].replay()
+        torch.cuda.synchronize()
+        del graphs[0]
+        graph = graphs[0]
     clk = ClockSampler(gpu_smi_id(torch, local_rank))
     clk.start()
     time.sleep(0.1)
@@ -438,6 +456,28 @@ def main(argv=None):
     extra = {}
     if world == 1 and headline and not args.no_extra:
         extra = run_extra(A, L, torch, dev, sp, hbm_peak)
+    if world > 1 and headline:
+        # every rank's gathered logits against the single-GPU matvec of the whole head (447 MB, filled here)
+        wf = torch.empty(ROWS * rb + 16, dtype=torch.uint8, device=dev)
+        A.call("arcllm_cuda_fill_" + fmt, C.c_void_p(wf.data_ptr()), 0, ROWS * (K // 256), 0x1A4D, sp)
+        yf = torch.empty(ROWS, dtype=torch.float32, device=dev)
+        A.check(L.arcllm_cuda_matvec(TY, C.c_void_p(wf.data_ptr()), ROWS, K, xp, None, C.c_float(0.0), None, None,
+                                     C.c_void_p(yf.data_ptr()), sp), "matvec")
+        if rg is not None:
+            got = torch.empty(ROWS, dtype=torch.float32, device=dev)
+            A.check(L.arcllm_cuda_memcpy_d2h(C.c_void_p(lh.data_ptr()), C.c_void_p(rg.logits_ptr), 4 * ROWS, sp))
+            A.check(L.arcllm_cuda_stream_synchronize(sp))
+            got.copy_(lh)
+        else:
+            got = logits
+        torch.cuda.synchronize()
+        same = torch.tensor([int(torch.equal(got.view(torch.int32), yf.view(torch.int32)))], device=dev)
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        extra["gather_bit_exact"] = bool(same.item())
+        del wf, yf
+        torch.cuda.empty_cache()
+        if not args.no_extra:
+            extra.update(run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier))
 
     if rank == 0:
         cpu = None if args.no_cpu or world > 1 or not headline else cpu_baseline()
@@ -474,7 +514,7 @@ def main(argv=None):
                                                              if rg is not None else ""),
                 "kernel_ms": round(kern_ms, 5), "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
                 "timing": ("mean launch time over one CUDA-graph replay of the %d timed launches" % args.steps
-                           if args.launch == "graph" and world == 1 else
+                           if args.launch == "graph" and (world == 1 or rg is not None) else
                            "CUDA events around each launch on its stream, mean over the timed launches"),
             },
             "e2e": {"value": None if e2e_val is None else round(e2e_val, 2), "unit": "GB/s",
@@ -500,6 +540,174 @@ def main(argv=None):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
+    """The sharded configurations at N > 1 (every time the max over ranks):
+    config 1b (Q6_K FFN down 3584x18944) row-sharded with the rows
+    re-assembled on every rank by the NVLink exchange kernel, checked against
+    the single-GPU matvec; config 4's gate GEMM (256x18944x3584) with its
+    output rows (the weight rows) sharded and the shards all-gathered with
+    NCCL; config 3's greedy decode of the Qwen2.5-7B-shaped model with the FFN
+    and LM head sharded over the ranks (tensor-parallel generate())."""
+    from arcllm_b200.rank_gather import ExchangeBuffers
+    out = {}
+
+    def exchange(h):
+        res = [None] * world
+        dist.all_gather_object(res, h)
+        return res
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def shard(n, align=32):
+        r0, rows = C.c_uint32(0), C.c_uint32(0)
+        A.call("arcllm_cuda_shard_rows", n, align, world, rank, C.byref(r0), C.byref(rows))
+        return r0.value, rows.value
+
+    # ---- config 1b: Q6_K 3584 x 18944, rows sharded, exchange-gathered ----
+    h0, hr = shard(HIDDEN)
+    rb = q_bytes("q6k", 1, FFN)
+    ncop = max(2, -(-3 * L2_BYTES // (hr * rb)))
+    ws = []
+    for c in range(ncop):
+        t = torch.empty(hr * rb + 16, dtype=torch.uint8, device=dev)
+        A.call("arcllm_cuda_fill_q6k", C.c_void_p(t.data_ptr()), h0 * (FFN // 256), hr * (FFN // 256), 0x1B00 + c, sp)
+        ws.append(t)
+    x18 = torch.empty(FFN, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(x18.data_ptr()), 0, FFN, 0x1B77, C.c_float(0), C.c_float(1), sp)
+    part = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    full = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    ex = ExchangeBuffers(FFN, world, rank, exchange)
+    barrier()
+
+    def step1b(i):
+        A.check(L.arcllm_cuda_matvec(A.GGML_Q6_K, C.c_void_p(ws[i % ncop].data_ptr()), hr, FFN,
+                                     C.c_void_p(x18.data_ptr()), None, C.c_float(0), None, None,
+                                     C.c_void_p(part.data_ptr() + 4 * h0), sp), "matvec")
+        ex.gather(C.c_void_p(part.data_ptr() + 4 * h0), hr, h0, C.c_void_p(full.data_ptr()), HIDDEN, sp)
+
+    for i in range(10):
+        step1b(i)
+    barrier()
+    n_it = 200
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(n_it):
+        step1b(i)
+    b.record()
+    barrier()
+    ms = max_over_ranks(a.elapsed_time(b) / n_it)
+    # check: the last step used copy (n_it - 1) % ncop; the full matrix of that seed on one GPU
+    wf = torch.empty(HIDDEN * rb + 16, dtype=torch.uint8, device=dev)
+    A.call("arcllm_cuda_fill_q6k", C.c_void_p(wf.data_ptr()), 0, HIDDEN * (FFN // 256), 0x1B00 + (n_it - 1) % ncop, sp)
+    yf = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    A.check(L.arcllm_cuda_matvec(A.GGML_Q6_K, C.c_void_p(wf.data_ptr()), HIDDEN, FFN, C.c_void_p(x18.data_ptr()), None,
+                                 C.c_float(0), None, None, C.c_void_p(yf.data_ptr()), sp), "matvec")
+    torch.cuda.synchronize()
+    diff = float((full.double() - yf.double()).norm() / yf.double().norm())
+    alg = matvec_alg_bytes("q6k", HIDDEN, FFN)
+    out["config1b_q6k_3584x18944_rowshard"] = {
+        "GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_step": round(ms * 1e3, 2),
+        "rows_per_rank": hr, "collective": "exchange kernel (NVLink peer stores + flags)",
+        "rel_l2_vs_1gpu": float("%.3g" % max_over_ranks(diff)),
+        "bit_exact_vs_1gpu": bool(max_over_ranks(diff) == 0.0)}
+    del ws, wf
+    torch.cuda.synchronize()
+    barrier()
+    ex.close()
+    torch.cuda.empty_cache()
+
+    # ---- config 4: prefill gate GEMM, output rows sharded + NCCL all-gather ----
+    _, tflops_peak, _ = measured_peaks()
+    m = 256
+    f0, fr = shard(FFN, 128)
+    ncop = max(2, -(-3 * L2_BYTES // q_bytes("q4k", fr, HIDDEN)))
+    ws = []
+    for c in range(ncop):
+        t = torch.empty(q_bytes("q4k", fr, HIDDEN) + 16, dtype=torch.uint8, device=dev)
+        A.call("arcllm_cuda_fill_q4k", C.c_void_p(t.data_ptr()), f0 * (HIDDEN // 256), fr * (HIDDEN // 256),
+               0x1C00 + c, sp)
+        ws.append(t)
+    xf = torch.empty(m * HIDDEN, dtype=torch.float32, device=dev)
+    A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(xf.data_ptr()), 0, m * HIDDEN, 0x1C7A, C.c_float(0),
+           C.c_float(1), sp)
+    xb = xf.to(torch.bfloat16)
+    y = torch.empty(m * fr, dtype=torch.float32, device=dev)
+    sizes = [None] * world
+    dist.all_gather_object(sizes, fr)
+    equal = len(set(sizes)) == 1
+    yall = torch.empty(world * m * fr, dtype=torch.float32, device=dev) if equal else None
+
+    def step4(i):
+        A.check(L.arcllm_cuda_gemm_q4k_bf16(C.c_void_p(ws[i % ncop].data_ptr()), fr, HIDDEN,
+                                            C.c_void_p(xb.data_ptr()), m, C.c_void_p(y.data_ptr()), sp), "gemm")
+        if equal:
+            dist.all_gather_into_tensor(yall, y)
+        else:
+            ys = [torch.empty(m * s_, dtype=torch.float32, device=dev) for s_ in sizes]
+            dist.all_gather(ys, y)
+
+    for i in range(5):
+        step4(i)
+    barrier()
+    n_it = 50
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(n_it):
+        step4(i)
+    b.record()
+    barrier()
+    ms = max_over_ranks(a.elapsed_time(b) / n_it)
+    tf = 2.0 * m * FFN * HIDDEN / (ms * 1e-3) / 1e12
+    out["config4_prefill_gate_256x18944x3584_rowshard"] = {
+        "TFLOP/s": round(tf, 1), "frac_of_bf16_peak_per_gpu": round(tf / world / tflops_peak, 4) if tflops_peak else None,
+        "us_per_step": round(ms * 1e3, 2), "rows_per_rank": fr, "collective": "NCCL all-gather of the Y shards"}
+    del ws, xf, xb, y, yall
+    torch.cuda.empty_cache()
+    barrier()
+
+    # ---- config 3: tensor-parallel greedy decode ----
+    from arcllm_b200.synthetic import QWEN25_7B, SyntheticModel
+    md = SyntheticModel(QWEN25_7B, seed=0xC3)
+    exd = ExchangeBuffers(md.tp_exchange_words(world), world, rank, exchange)
+    md.set_tensor_parallel(exd.ptrs, world, rank)
+    barrier()
+    prompt = [int(splitmix_token(i, QWEN25_7B["vocab"])) for i in range(256)]
+    md.generate(prompt[:8], 4)  # warm-up: captures the step graphs
+    barrier()
+    t0 = time.perf_counter()
+    toks, st = md.generate(prompt, 128)
+    wall = time.perf_counter() - t0
+    dec_ms = max_over_ranks(st.decode_ms)
+    pf_ms = max_over_ranks(st.prefill_ms)
+    same = [None] * world
+    dist.all_gather_object(same, toks)
+    tps = st.decode_steps / (dec_ms * 1e-3)
+    bpt = md.bytes_per_token()
+    out["config3_decode_tp"] = {
+        "tok/s": round(tps, 1), "ms_per_token": round(dec_ms / st.decode_steps, 4),
+        "weight_GB/s_whole_job": round(bpt * tps / 1e9, 1), "prefill_ms_256_tokens": round(pf_ms, 2),
+        "e2e_generate_s": round(max_over_ranks(wall), 4), "launches_per_token": st.decode_launches_per_step,
+        "ranks_agree": all(t == toks for t in same), "first_tokens": toks[:4],
+        "sharding": "FFN gate/up rows, FFN down rows and LM-head rows over %d ranks; attention replicated; "
+                    "s, hidden state and greedy records exchanged by the NVLink exchange kernel" % world}
+    torch.cuda.synchronize()
+    barrier()
+    md.close()
+    exd.close()
+    torch.cuda.empty_cache()
+    # the 1-GPU tokens of the same request, on rank 0 (after the ranks are done with NVLink)
+    if rank == 0:
+        m1 = SyntheticModel(QWEN25_7B, seed=0xC3)
+        out["config3_decode_tp"]["tokens_equal_1gpu"] = m1.generate(prompt, 128)[0] == toks
+        m1.close()
+        torch.cuda.empty_cache()
+    barrier()
+    return out
 
 
 def run_extra(A, L, torch, dev, sp, hbm_peak, which="all"):

@@ -15,7 +15,13 @@
 #include <string>
 #include <vector>
 
+#if defined(ARCLLM_BINDING_FROM_REFERENCE)
+// a program built against the reference's own policy layer takes the adapter
+// interface from there (same names, layouts and values as the restatement)
+#include "arcllm/v1/generic_backend_binding_v4.h"
+#else
 #include "arcllm/v1/backend_adapter_v4.h"
+#endif
 
 namespace arcllm::v1::cuda {
 

@@ -147,6 +147,33 @@ ARCLLM_CUDA_API int arcllm_cuda_ipc_get_handle(const void *dev_ptr, void *handle
 ARCLLM_CUDA_API int arcllm_cuda_ipc_open_handle(const void *handle, void **dev_ptr_out);
 ARCLLM_CUDA_API int arcllm_cuda_ipc_close_handle(void *dev_ptr);
 
+/* ---- rank exchange (all-gather of a vector over NVLink peer stores) ------
+ * Not in the reference (it decodes on one device, src/arcllm_v1_runtime.cpp:
+ * 371-421); the reassembly step of row-sharded matvecs.  One CTA per rank
+ * stores this rank's slice src[0, n_local) (32-bit words) at word `offset`
+ * into every rank's exchange buffer (NVLink peer stores; nothing reads another
+ * GPU's memory), publishes a sequence number in every rank's flag array and
+ * waits (bounded by timeout_us, 0: 2 s) for all ranks' numbers, then copies
+ * the assembled vector dst[0, n_total) out of its own buffer.
+ *   rank_bufs[q]: rank q's buffer as this process maps it (own allocation for
+ *   q == rank, an IPC mapping otherwise), arcllm_cuda_exchange_buffer_bytes
+ *   (max_words) bytes, 256-byte aligned, zero-filled before first use.
+ * Every rank must issue the same sequence of exchanges (the sequence numbers
+ * live in the buffers, so a CUDA graph of exchanges replays unchanged).  A
+ * wait that runs out sets the device error word's timeout bit (ARC_E_DEVICE_
+ * TIMEOUT from arcllm_cuda_device_error); the buffers must then be zeroed on
+ * every rank before further use. */
+ARCLLM_CUDA_API int arcllm_cuda_exchange_buffer_bytes(uint32_t max_words, uint64_t *out);
+ARCLLM_CUDA_API int arcllm_cuda_exchange_gather(void *const *rank_bufs, uint32_t n_ranks, uint32_t rank,
+                                                uint32_t max_words, const void *src, uint32_t n_local,
+                                                uint32_t offset, void *dst, uint32_t n_total, uint32_t timeout_us,
+                                                void *stream);
+/* The contiguous row shard [*row0, *row0 + *rows) of n rows that `rank` of
+ * n_ranks owns: whole units of `align` rows (n % align == 0), the remainder
+ * units one each to the first ranks.  Host-only arithmetic. */
+ARCLLM_CUDA_API int arcllm_cuda_shard_rows(uint32_t n, uint32_t align, uint32_t n_ranks, uint32_t rank,
+                                           uint32_t *row0, uint32_t *rows);
+
 /* ---- fused gate/up projection with SiLU-multiply (Q4_K) -------------------
  * s[r] = silu(g[r]) * u[r],  g = W_gate . xn,  u = W_up . xn,  xn as above.
  * Replaces the I002 pair of shaders/sa1_q4k_subgroup_splitk.comp dispatches
@@ -368,9 +395,29 @@ ARCLLM_CUDA_API int arcllm_cuda_model_set_prefill_down(arcllm_cuda_model *m, uin
 /* Device pointers to the last logits [vocab] and to the K / V caches. */
 ARCLLM_CUDA_API int arcllm_cuda_model_logits(arcllm_cuda_model *m, const float **out);
 ARCLLM_CUDA_API int arcllm_cuda_model_kv_cache(arcllm_cuda_model *m, const uint16_t **k, const uint16_t **v);
-/* Restrict the LM head to rows [row0, row0+rows) (row sharding across GPUs;
- * the other rows of the logits must be filled by the caller, e.g. all-gather). */
+/* Restrict the LM head to rows [row0, row0+rows) of the output matrix given
+ * to set_endpoints (row sharding across GPUs; the other rows of the logits
+ * must be filled by the caller, e.g. all-gather, before the argmax reads all
+ * vocab rows). */
 ARCLLM_CUDA_API int arcllm_cuda_model_shard_lm_head(arcllm_cuda_model *m, uint32_t row0, uint32_t rows);
+/* Tensor-parallel decode over n_ranks GPUs, one process and one model per
+ * GPU, every rank holding the whole set of weights (the reference decodes on
+ * one device, src/arcllm_v1_runtime.cpp:371-421).  Each rank runs the
+ * attention half of every layer in full (replicated), its shard of the FFN
+ * gate/up rows, its shard of the FFN down rows (+ residual) and its shard of
+ * the LM-head rows; after gate/up, after down and after its shard's greedy
+ * argmax the ranks exchange the vector over NVLink peer stores
+ * (arcllm_cuda_exchange_gather), so every rank holds the full s, the full
+ * hidden state and the global greedy token, and all ranks produce the same
+ * tokens.  rank_bufs as for arcllm_cuda_exchange_gather with max_words from
+ * arcllm_cuda_model_tp_exchange_words.  Every rank must call generate() (or
+ * the same begin/prefill/step sequence) with the same arguments.  The logits
+ * buffer (arcllm_cuda_model_logits) then holds this rank's LM-head rows only.
+ * n_ranks == 1 turns it off. */
+ARCLLM_CUDA_API int arcllm_cuda_model_tp_exchange_words(const arcllm_cuda_model_config *cfg, uint32_t n_ranks,
+                                                        uint32_t *out);
+ARCLLM_CUDA_API int arcllm_cuda_model_set_tensor_parallel(arcllm_cuda_model *m, void *const *rank_bufs,
+                                                          uint32_t n_ranks, uint32_t rank, uint32_t timeout_us);
 
 #ifdef __cplusplus
 }

@@ -90,3 +90,21 @@ def test_allgather_layout_and_argument_validation():
     ]
     for args, want in cases:
         assert name(ag(*args)) == want, args
+
+
+def test_shard_rows_cover_and_align():
+    """arcllm_cuda_shard_rows (host-only): the tensor-parallel row shards tile
+    [0, n) in rank order, in whole aligned units, balanced to one unit."""
+    for n, align in ((18944, 32), (3584, 32), (152064, 32), (1024, 32)):
+        for world in (1, 2, 3, 4, 8):
+            if n // align < world:
+                continue
+            spans = []
+            for r in range(world):
+                r0, rows = C.c_uint32(0), C.c_uint32(0)
+                A.call("arcllm_cuda_shard_rows", n, align, world, r, C.byref(r0), C.byref(rows))
+                spans.append((r0.value, rows.value))
+            assert spans[0][0] == 0 and sum(s[1] for s in spans) == n
+            assert all(a[0] + a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert all(s[0] % align == 0 and s[1] % align == 0 for s in spans)
+            assert max(s[1] for s in spans) - min(s[1] for s in spans) <= align

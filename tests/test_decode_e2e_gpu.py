@@ -2,7 +2,8 @@
 28 layers (q/k/o/gate/up Q4_K; v, down and the LM head Q6_K; fp16 embedding
 and KV cache) -- the bench's decode model (seed 0xC3) and the first 16 tokens
 of its prompt stream -- against the CPU oracle's fp32 forward pass
-(tests/oracle_decode.py, the order of src/arcllm_v1_runtime.cpp:371-421).
+(tests/oracle_decode.py, the order of src/arcllm_v1_runtime.cpp:371-421),
+with its cache rows rounded to fp16 as the model's cache holds them.
 
 The prompt goes through the default batched tensor-core prefill (15 rows),
 then five decode steps run as the captured step graph.  The oracle steps
@@ -56,10 +57,10 @@ def test_config3_28_layers_batched_prefill_then_decode_against_oracle():
 
     ref = OracleModel(cfg, specs, threads=max(8, os.cpu_count() or 8))
     for pos, t in enumerate(prompt[:-1]):
-        ref.step(t, pos, head=False)
+        ref.step(t, pos, fp16_cache=True, head=False)
     feed, rels, match = prompt[-1], [], 0
     for i in range(N_NEW):
-        y = ref.step(feed, N_PROMPT - 1 + i)
+        y = ref.step(feed, N_PROMPT - 1 + i, fp16_cache=True)
         rels.append(rel(logits[i], y))
         match += int(O.argmax(y)[0] == toks[i])
         feed = toks[i]

@@ -51,9 +51,15 @@ def test_validate_exact_and_corrupted(rows, k):
     G.check_device_error()
 
 
-@pytest.mark.parametrize("rows,k,with_res", [(3584, 18944, True), (5000, 3584, False), (37, 512, True),
-                                             (1, 256, False)])
-def test_exec148_matvec_parity(rows, k, with_res):
+@pytest.mark.parametrize("rows,k,with_res,impl", [(3584, 18944, True, ""), (3584, 18944, True, "cuda"),
+                                                  (5000, 3584, False, ""), (64, 2560, True, ""), (2, 18944, False, ""),
+                                                  (37, 512, True, ""), (1, 256, False, "")])
+def test_exec148_matvec_parity(rows, k, with_res, impl, monkeypatch):
+    """Even row counts run on the K-slice integer-MMA kernel (the image read
+    in 2-row tensor-map super-rows, codes as element pairs), odd ones and
+    ARCLLM_MATVEC_IMPL=cuda on the CUDA-core kernel."""
+    if impl:
+        monkeypatch.setenv("ARCLLM_MATVEC_IMPL", impl)
     seed = 77 + rows
     src = gpu_fill("q4k", rows, k, seed)
     img = materialize(src, rows * (k // 256))

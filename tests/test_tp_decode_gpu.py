@@ -1,0 +1,158 @@
+"""Tensor-parallel decode (arcllm_cuda_model_set_tensor_parallel) and the rank
+exchange under it (arcllm_cuda_exchange_gather).
+
+One GPU: the exchange with one rank is a copy, repeats over sequence numbers
+of both parities, and a rank that never arrives ends the wait with the device
+timeout bit after the 50 ms bound (no hang, the context stays usable).
+
+Two GPUs (spawned processes, one per GPU, gloo only to swap the IPC handles;
+skipped with fewer GPUs): the FFN gate/up, FFN down and LM-head rows sharded
+over the ranks, attention replicated, s / hidden state / greedy records
+exchanged over NVLink peer stores -- every rank produces the same greedy
+tokens as the single-GPU model, with the batched prefill and with the token
+path (whose prefill graph runs the exchanges too).  No test runs two waiting
+launches on one GPU.
+"""
+import ctypes as C
+import datetime
+import multiprocessing as mp
+import socket
+
+import numpy as np
+import pytest
+
+import arcllm_b200 as A
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+from tests import gpu_util as G  # noqa: E402
+
+CFG = dict(n_layers=2, hidden=3584, n_heads=28, n_kv_heads=4, head_dim=128, ffn=18944, vocab=152064, max_ctx=4096,
+           rms_eps=1e-6, rope_theta=1.0e6)
+
+
+def _error_bits():
+    bits = C.c_uint32(0)
+    st = A.lib().arcllm_cuda_device_error(G.stream(), C.byref(bits))
+    assert st in (0, 6), st
+    return bits.value
+
+
+def test_exchange_single_rank_is_a_copy_over_both_parities():
+    from arcllm_b200.rank_gather import ExchangeBuffers
+    ex = ExchangeBuffers(18944, 1, 0, lambda h: [h])
+    try:
+        for i, (n, off, total) in enumerate(((18944, 0, 18944), (3584, 0, 3584), (7, 0, 7), (4, 0, 4),
+                                             (18944, 0, 18944))):
+            src = torch.from_numpy(O.normal_f32(n, 40 + i)).to(G.dev())
+            dst = torch.full((total,), float("nan"), dtype=torch.float32, device=G.dev())
+            ex.gather(G.ptr(src), n, off, G.ptr(dst), total, G.stream())
+            assert np.array_equal(G.host(dst).view(np.uint32), G.host(src).view(np.uint32))
+        assert _error_bits() == 0
+    finally:
+        torch.cuda.synchronize()
+        ex.close()
+
+
+def test_exchange_wait_times_out_when_a_rank_never_arrives():
+    """Rank 0 of two whose rank-1 buffer is a local allocation nothing ever
+    signals: the wait gives up after 50 ms, sets the timeout bit, skips the
+    copy, and the next call (one rank) works."""
+    n = C.c_uint64(0)
+    A.call("arcllm_cuda_exchange_buffer_bytes", 3584, C.byref(n))
+    bufs = [torch.zeros(n.value // 4 + 64, dtype=torch.int32, device=G.dev()) for _ in range(2)]
+    ptrs = (C.c_void_p * 2)(*[(b.data_ptr() + 255) // 256 * 256 for b in bufs])
+    src = torch.from_numpy(O.normal_f32(1792, 50)).to(G.dev())
+    dst = torch.full((3584,), float("nan"), dtype=torch.float32, device=G.dev())
+    assert _error_bits() == 0
+    A.call("arcllm_cuda_exchange_gather", ptrs, 2, 0, 3584, G.ptr(src), 1792, 0, G.ptr(dst), 3584, 50000, G.stream())
+    torch.cuda.synchronize()
+    assert _error_bits() & 1, "the flag wait should have timed out"
+    assert np.isnan(G.host(dst)).all()  # no copy after a timeout
+    one = (C.c_void_p * 1)(ptrs[0])
+    A.call("arcllm_cuda_exchange_gather", one, 1, 0, 3584, G.ptr(src), 1792, 0, G.ptr(dst), 1792, 50000, G.stream())
+    assert np.array_equal(G.host(dst)[:1792].view(np.uint32), G.host(src).view(np.uint32))
+    assert _error_bits() == 0
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _tp_worker(rank, world, port, prompt, n_new, q):
+    try:
+        import torch
+        import torch.distributed as dist
+
+        from arcllm_b200.rank_gather import ExchangeBuffers
+        from arcllm_b200.synthetic import SyntheticModel
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+
+        m = SyntheticModel(CFG, seed=0x5EED + 40)
+        ex = ExchangeBuffers(m.tp_exchange_words(world), world, rank, exchange)
+        m.set_tensor_parallel(ex.ptrs, world, rank, timeout_us=5000000)
+        dist.barrier()
+        res = {}
+        for mode in (1, 0):  # batched prefill, then the token path (exchanges in the prefill graph)
+            m.set_prefill_mode(mode)
+            toks, st = m.generate(prompt, n_new)
+            res[mode] = (toks, st.decode_launches_per_step)
+            dist.barrier()
+        bits = C.c_uint32(0)
+        A.lib().arcllm_cuda_device_error(C.c_void_p(torch.cuda.current_stream().cuda_stream), C.byref(bits))
+        ref = None
+        if rank == 0:  # the single-GPU model on the same GPU
+            m1 = SyntheticModel(CFG, seed=0x5EED + 40)
+            ref = m1.generate(prompt, n_new)[0]
+            m1.close()
+        dist.barrier()
+        m.close()
+        ex.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res, ref, bits.value, ""))
+    except Exception as e:  # reported to the parent
+        q.put((rank, None, None, -1, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_generate_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    prompt = [int(t) for t in O.tokens(12, 0x91, CFG["vocab"])]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, prompt, 8, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=600) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    ref = res[0][2]
+    for rank, out, _, bits, msg in res:
+        assert msg == "", "rank %d: %s" % (rank, msg)
+        assert bits == 0, "rank %d device error %#x" % (rank, bits)
+        for mode in (1, 0):
+            toks, launches = out[mode]
+            print("rank %d mode %d: tokens %s (1 GPU %s), %d launches per step" % (rank, mode, toks, ref, launches))
+            assert toks == ref
+            # 1 embedding + per layer (Q, K, V, attention, O, gate/up, exchange, down, exchange) + LM head,
+            # argmax, exchange, combine + finalize
+            assert launches == 1 + 9 * CFG["n_layers"] + 5
