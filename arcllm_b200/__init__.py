@@ -43,7 +43,8 @@ SIGNATURES = {
     "arcllm_cuda_gemm_q4k_bf16": [_vp, _u32, _u32, _vp, _u32, _vp, _vp],
     "arcllm_cuda_gemm_bf16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],
     "arcllm_cuda_gemm_f16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],
-    "arcllm_cuda_rmsnorm_rows": [_vp, _vp, _f32, _u32, _u32, _i32, _vp, _vp],
+    "arcllm_cuda_gemm_f16x3": [_i32, _vp, _u32, _u32, _vp, _vp, _u32, _vp, _vp, _vp],
+    "arcllm_cuda_rmsnorm_rows": [_vp, _vp, _f32, _u32, _u32, _i32, _vp, _vp, _vp],
     "arcllm_cuda_rope_kv_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
                                  _vp],
     "arcllm_cuda_attention_prefill": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _vp],

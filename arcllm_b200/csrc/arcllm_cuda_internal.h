@@ -142,9 +142,10 @@ int gemm_q4k_bf16_prepare();
 int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,
                   cudaStream_t stream);
 // Q4_K (12) or Q6_K (14) weights; y = residual + x W^T when residual is non-null.
-// x and the dequantised W in bf16, or in fp16 when `fp16` (x then holds fp16).
+// mode 0: x and the dequantised W in bf16; 1: both fp16 (x holds fp16);
+// 2: fp16 hi + lo of both, y = (x + x_lo)(W_hi + W_lo)^T without the lo*lo term.
 int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
-                 const float* residual, float* y, cudaStream_t stream, bool fp16 = false);
+                 const float* residual, float* y, cudaStream_t stream, int mode = 0, const uint16_t* x_lo = nullptr);
 
 std::vector<float> rope_table(uint32_t max_ctx, uint32_t head_dim, float theta);
 int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out);

@@ -312,15 +312,24 @@ int arcllm_cuda_gemm_bf16(int type, const void* w, uint32_t n, uint32_t k, const
 int arcllm_cuda_gemm_f16(int type, const void* w, uint32_t n, uint32_t k, const uint16_t* x_f16, uint32_t m,
                          const float* residual, float* y, void* stream) {
     ARC_GUARD_BEGIN
-    return arc::gemm_kq_bf16(type, w, n, k, x_f16, m, residual, y, static_cast<cudaStream_t>(stream), true);
+    return arc::gemm_kq_bf16(type, w, n, k, x_f16, m, residual, y, static_cast<cudaStream_t>(stream), 1);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_gemm_f16x3(int type, const void* w, uint32_t n, uint32_t k, const uint16_t* x_hi,
+                           const uint16_t* x_lo, uint32_t m, const float* residual, float* y, void* stream) {
+    ARC_GUARD_BEGIN
+    if (!x_lo) return arc::set_error(ARC_E_INVALID_ARGUMENT, "gemm f16x3: null x_lo");
+    return arc::gemm_kq_bf16(type, w, n, k, x_hi, m, residual, y, static_cast<cudaStream_t>(stream), 2, x_lo);
     ARC_GUARD_END
 }
 
 int arcllm_cuda_rmsnorm_rows(const float* x, const float* gamma, float eps, uint32_t rows, uint32_t h, int out_fp16,
-                             uint16_t* out, void* stream) {
+                             uint16_t* out, uint16_t* out_lo, void* stream) {
     ARC_GUARD_BEGIN
+    if (out_lo && !out_fp16) return arc::set_error(ARC_E_INVALID_ARGUMENT, "rmsnorm rows: out_lo needs fp16 output");
     return arc::launch_rmsnorm_rows_bf16(x, gamma, eps, rows, h, out, static_cast<cudaStream_t>(stream),
-                                         out_fp16 != 0);
+                                         out_fp16 != 0, out_lo);
     ARC_GUARD_END
 }
 

@@ -18,9 +18,10 @@
 //               ahead), then read the accumulators back with tcgen05.ld
 //               (warp w serves TMEM lanes 32*(w%4)..) and store Y.
 // Both MMAs of a K step share the dequantised B tile, so each weight is
-// dequantised once per CTA.  The operands are bf16, or fp16 (same rate, 11
-// instead of 8 significant bits) for the projections whose outputs feed the
-// attention scores.  When N/128 tiles leave SMs idle (the FFN-down
+// dequantised once per CTA.  The operands are bf16, fp16 (same rate, 11
+// instead of 8 significant bits), or fp16 hi + lo pairs of both X and W with
+// three MMAs per K step (~22 bits: the projections whose outputs feed the
+// attention scores).  When N/128 tiles leave SMs idle (the FFN-down
 // shape, N = 3584), K is split across CTAs, the CTAs store partial tiles and
 // a grid-wide reduce kernel adds them in split order (deterministic; the
 // last CTA of each column tile adding them alone was the slowest part of the
@@ -47,13 +48,27 @@ constexpr uint32_t kBTile = kBN * kBK * 2;   // 16 KB: dequantised W tile
 constexpr uint32_t kDqWarps = 8;                         // dequantising warps: 2 threads per W row
 constexpr uint32_t kThreads = (2 + kDqWarps) * 32;
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kStages = 4;
-constexpr uint32_t kStageBytes = 2 * kAHalf + kBTile;  // 48 KB
+constexpr uint32_t kMaxStages = 4;
+
+// Operand modes: bf16 (0), fp16 (1), fp16 x3 (2): X = X_hi + X_lo and
+// W = W_hi + W_lo as fp16 pairs (W_hi = fp16(w), W_lo = fp16(w - W_hi) of the
+// exactly dequantised fp32 weight), accumulated as X_hi W_hi + X_lo W_hi +
+// X_hi W_lo -- ~22 significant bits of each operand, at three MMAs per K step.
+// Modes 0/1 stage two 128-row boxes of X and one W tile (48 KB, 4 stages);
+// mode 2 four boxes (hi and lo) and two W tiles (96 KB, 2 stages).
+template <int MODE>
+struct GemmStage {
+    static constexpr uint32_t kABoxes = MODE == 2 ? 4u : 2u;
+    static constexpr uint32_t kBTiles = MODE == 2 ? 2u : 1u;
+    static constexpr uint32_t kStages = MODE == 2 ? 2u : 4u;
+    static constexpr uint32_t kBOff = kABoxes * kAHalf;
+    static constexpr uint32_t kBytes = kBOff + kBTiles * kBTile;
+};
 
 struct GemmSmemTail {
-    uint64_t full_a[kStages];
-    uint64_t full_b[kStages];
-    uint64_t empty[kStages];
+    uint64_t full_a[kMaxStages];
+    uint64_t full_b[kMaxStages];
+    uint64_t empty[kMaxStages];
     uint64_t done;
     uint32_t tmem_base;
     int abort_flag;
@@ -67,7 +82,11 @@ struct SplitKWs {
     uint32_t ks;
 };
 
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + sizeof(GemmSmemTail) + 1024;  // + alignment slack
+template <int MODE>
+constexpr uint32_t smem_bytes() {  // + alignment slack
+    return GemmStage<MODE>::kStages * GemmStage<MODE>::kBytes + (uint32_t)sizeof(GemmSmemTail) + 1024u;
+}
+static_assert(smem_bytes<0>() <= 232448u && smem_bytes<2>() <= 232448u, "GEMM stages exceed 227 KB");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -275,15 +294,100 @@ __device__ __forceinline__ void dequant_q6_quarter(const Raw9& ql, uint32_t shl,
     }
 }
 
-// F16: X and the dequantised W tile in fp16 (11 significant bits) instead of
-// bf16 (8): the scale and offset of each sub-block, q*f - o and X all round
-// 8x more finely, at the same tensor-core rate.
-template <int FMT, bool F16>
+// Mode 2: the fp16 hi / lo halves of 8 fp32 weights (elements 8*chunk .. +7
+// of row n of the stage) into the W_hi and W_lo tiles (same swizzled place).
+__device__ __forceinline__ void store_hi_lo8(const float (&w)[8], uint32_t n, uint32_t chunk, uint8_t* bh,
+                                             uint8_t* bl) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        h[i] = f16x2(w[2 * i], w[2 * i + 1]);
+        const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&h[i]));
+        l[i] = f16x2(w[2 * i] - hf.x, w[2 * i + 1] - hf.y);  // w - hi is exact in fp32
+    }
+    const uint32_t off = (n >> 3) * 1024u + (n & 7u) * 128u + ((chunk ^ (n & 7u)) << 4);
+    *reinterpret_cast<uint4*>(bh + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(bl + off) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Mode 2, Q4_K: the per-sub-block scale f = d*sc and offset o = -(dmin*mn)
+// in fp32 (both exact: fp16 times a 6-bit integer) for sub-blocks 2c + hi.
+__device__ __forceinline__ void subblock_consts_f32(uint4 hd, uint32_t hi, float (&f)[4], float (&o)[4]) {
+    const uint32_t S[3] = {hd.y, hd.z, hd.w};
+    auto sbyte = [&](uint32_t i) { return (S[i >> 2] >> (8u * (i & 3u))) & 0xFFu; };
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+#pragma unroll
+    for (uint32_t c = 0; c < 4; ++c) {
+        const uint32_t j = 2u * c + hi;
+        uint32_t sc, mn;
+        if (j < 4) {
+            sc = sbyte(j) & 63u;
+            mn = sbyte(j + 4) & 63u;
+        } else {
+            sc = (sbyte(j + 4) & 15u) | ((sbyte(j - 4) >> 6) << 4);
+            mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
+        }
+        f[c] = d * (float)sc;
+        o[c] = -(dmin * (float)mn);
+    }
+}
+
+// Mode 2, Q4_K: the 32 weights of sub-block 2c + hi as fp32 exactly as the
+// reference dequantises them (f*q is exact, so fmaf(f, q, o) rounds once like
+// (d*sc)*q - dmin*mn, src/p8c_segmented_access_correctness.cpp:1166-1181),
+// split into fp16 hi / lo tiles.
+__device__ __forceinline__ void dequant_subblock_x3(uint4 q0, uint4 q1, float f, float o, uint32_t n, uint32_t hi,
+                                                    uint8_t* bh, uint8_t* bl) {
+    const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+        float w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t byte = (w8[2 * ch + (j >> 2)] >> (8 * (j & 3))) & 0xFFu;
+            const uint32_t q = hi ? (byte >> 4) : (byte & 15u);
+            w[j] = fmaf(f, (float)q, o);
+        }
+        store_hi_lo8(w, n, 4u * hi + ch, bh, bl);
+    }
+}
+
+// Mode 2, Q6_K: quarter q of half h of a super-block row (see dequant_q6_quarter),
+// w = (d*sc) * (c - 32) in fp32 (src/p8c_segmented_access_correctness.cpp:944-956),
+// split into fp16 hi / lo tiles.
+__device__ __forceinline__ void dequant_q6_quarter_x3(const Raw9& ql, uint32_t shl, const Raw9& qh, uint32_t shh,
+                                                      uint32_t lo_shift, uint32_t qh_shift, float f0, float f1,
+                                                      uint32_t n, uint32_t hi, uint8_t* bh, uint8_t* bl) {
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+        float w[8];
+#pragma unroll
+        for (int wi = 0; wi < 2; ++wi) {
+            const int i = 2 * ch + wi;
+            const uint32_t c4 = ((raw9_word(ql, i, shl) >> lo_shift) & 0x0F0F0F0Fu) |
+                                (((raw9_word(qh, i, shh) >> qh_shift) & 0x03030303u) << 4);
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                w[4 * wi + b] = __fmul_rn(ch < 2 ? f0 : f1, (float)((int)((c4 >> (8 * b)) & 0xFFu) - 32));
+        }
+        store_hi_lo8(w, n, 4u * hi + ch, bh, bl);
+    }
+}
+
+// MODE 0: bf16 operands; 1: fp16 (11 significant bits instead of 8: the
+// scale and offset of each sub-block, q*f - o and X all round 8x more finely,
+// at the same tensor-core rate); 2: fp16 hi + lo of both operands, three MMAs
+// per K step (xmap_lo: the X_lo tensor).
+template <int FMT, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kq_bf16_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w, uint32_t n_total,
-                        uint32_t k, uint32_t m, const float* __restrict__ residual, float* __restrict__ y,
-                        unsigned int* err, const SplitKWs sk) {
-    constexpr uint32_t kBOff = 2 * kAHalf;
+    gemm_kq_bf16_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
+                        const uint8_t* __restrict__ w, uint32_t n_total, uint32_t k, uint32_t m,
+                        const float* __restrict__ residual, float* __restrict__ y, unsigned int* err,
+                        const SplitKWs sk) {
+    constexpr bool F16 = MODE >= 1;
+    constexpr uint32_t kStages = GemmStage<MODE>::kStages, kStageBytes = GemmStage<MODE>::kBytes;
+    constexpr uint32_t kBOff = GemmStage<MODE>::kBOff;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_align_up<1024>(smem_raw, 0);
     GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + kStages * kStageBytes);
@@ -329,9 +433,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (*abort_flag) break;
                 uint8_t* st = smem + s * kStageBytes;
-                mbar_arrive_expect_tx(&tail->full_a[s], 2 * kAHalf);
+                mbar_arrive_expect_tx(&tail->full_a[s], GemmStage<MODE>::kABoxes * kAHalf);
                 tma_load_2d(smem_u32(st), &xmap, (int)((kbase + kb) * kBK), 0, &tail->full_a[s]);
                 tma_load_2d(smem_u32(st + kAHalf), &xmap, (int)((kbase + kb) * kBK), 128, &tail->full_a[s]);
+                if (MODE == 2) {  // boxes 2, 3: X_lo of the same rows
+                    tma_load_2d(smem_u32(st + 2 * kAHalf), &xmap_lo, (int)((kbase + kb) * kBK), 0, &tail->full_a[s]);
+                    tma_load_2d(smem_u32(st + 3 * kAHalf), &xmap_lo, (int)((kbase + kb) * kBK), 128,
+                                &tail->full_a[s]);
+                }
                 ++issued;
             }
             if (*abort_flag)  // no copy may still be landing at exit
@@ -353,6 +462,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t acc = (kb | kk) != 0u;
                     umma_16<F16>(tmem, sw128_desc(st + 32u * kk), db, acc);
                     umma_16<F16>(tmem + 128u, sw128_desc(st + kAHalf + 32u * kk), db, acc);
+                    if (MODE == 2) {  // + X_lo W_hi + X_hi W_lo into the same accumulators
+                        const uint64_t dbl = sw128_desc(st + kBOff + kBTile + 32u * kk);
+                        umma_16<true>(tmem, sw128_desc(st + 2 * kAHalf + 32u * kk), db, 1u);
+                        umma_16<true>(tmem + 128u, sw128_desc(st + 3 * kAHalf + 32u * kk), db, 1u);
+                        umma_16<true>(tmem, sw128_desc(st + 32u * kk), dbl, 1u);
+                        umma_16<true>(tmem + 128u, sw128_desc(st + kAHalf + 32u * kk), dbl, 1u);
+                    }
                 }
                 umma_commit(&tail->empty[s]);  // stage free once these MMAs have read it
             }
@@ -396,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kb + kPf < nkb) load6(kb + kPf, pql[slot], pqh[slot], psc[slot]);
                 const float d = __half2float(__ushort_as_half((unsigned short)(scd >> 16)));
                 const float s0 = d * (float)(int8_t)(scd & 0xFFu), s1 = d * (float)(int8_t)((scd >> 8) & 0xFFu);
-                const uint32_t f0 = pack2<F16>(s0, s0), f1 = pack2<F16>(s1, s1);
+                const uint32_t f0 = pack2<F16 && MODE != 2>(s0, s0), f1 = pack2<F16 && MODE != 2>(s1, s1);
                 const uint32_t s = kb % kStages;
                 bool ok = true;
                 if (kb >= kStages) {
@@ -408,8 +524,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     stop6 = true;
                     break;
                 }
-                dequant_q6_quarter<F16>(ql, shl, qh, shh, 4u * (sub & 1u), 2u * q, f0, f1, nrow, hi,
-                                        smem + s * kStageBytes + kBOff);
+                if (MODE == 2)
+                    dequant_q6_quarter_x3(ql, shl, qh, shh, 4u * (sub & 1u), 2u * q, s0, s1, nrow, hi,
+                                          smem + s * kStageBytes + kBOff, smem + s * kStageBytes + kBOff + kBTile);
+                else
+                    dequant_q6_quarter<F16>(ql, shl, qh, shh, 4u * (sub & 1u), 2u * q, f0, f1, nrow, hi,
+                                            smem + s * kStageBytes + kBOff);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tail->full_b[s]);
@@ -431,9 +551,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (i < nkb) load_codes(i, pq0[i], pq1[i]);
             uint4 hd_next = ld_nc_v4(row);
             uint32_t fb[4], ob[4];
+            float ff[4], of[4];
             bool stop = false;
             for (uint32_t kb0 = 0; kb0 < nkb && !stop; kb0 += kPrefetch) {  // kPrefetch == 4: one super-block
-                subblock_consts<F16>(hd_next, hi, fb, ob);
+                if (MODE == 2)
+                    subblock_consts_f32(hd_next, hi, ff, of);
+                else
+                    subblock_consts<F16>(hd_next, hi, fb, ob);
                 if (kb0 + 4u < nkb) hd_next = ld_nc_v4(row + ((kb0 >> 2) + 1u) * 144u);
     #pragma unroll
                 for (uint32_t i = 0; i < kPrefetch; ++i) {
@@ -452,7 +576,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         stop = true;
                         break;
                     }
-                    dequant_subblock<F16>(c0, c1, fb[i], ob[i], nrow, hi, smem + s * kStageBytes + kBOff);
+                    if (MODE == 2)
+                        dequant_subblock_x3(c0, c1, ff[i], of[i], nrow, hi, smem + s * kStageBytes + kBOff,
+                                            smem + s * kStageBytes + kBOff + kBTile);
+                    else
+                        dequant_subblock<F16>(c0, c1, fb[i], ob[i], nrow, hi, smem + s * kStageBytes + kBOff);
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tail->full_b[s]);
@@ -559,45 +687,54 @@ int gemm_q4k_bf16_prepare() {
     if (done[dev].load(std::memory_order_acquire)) return ARC_OK;
     std::lock_guard<std::mutex> lock(prep_mutex);
     if (done[dev].load(std::memory_order_relaxed)) return ARC_OK;
-    cudaError_t e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<12, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<14, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kSmemBytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<12, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kSmemBytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_kq_bf16_kernel<14, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kSmemBytes);
+    cudaError_t e = cudaSuccess;
+    auto attr = [&](auto kern, uint32_t bytes) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    };
+    attr(gemm_kq_bf16_kernel<12, 0>, smem_bytes<0>());
+    attr(gemm_kq_bf16_kernel<14, 0>, smem_bytes<0>());
+    attr(gemm_kq_bf16_kernel<12, 1>, smem_bytes<1>());
+    attr(gemm_kq_bf16_kernel<14, 1>, smem_bytes<1>());
+    attr(gemm_kq_bf16_kernel<12, 2>, smem_bytes<2>());
+    attr(gemm_kq_bf16_kernel<14, 2>, smem_bytes<2>());
     if (e != cudaSuccess) return set_cuda_error(e, "gemm prepare");
     done[dev].store(true, std::memory_order_release);
     return ARC_OK;
 }
 
+namespace {
+// Tensor map of an m x k row-major 16-bit activation, 64 x 128 boxes, 128-byte swizzle.
+int encode_x_map(EncodeTiledFn enc, const uint16_t* x, uint32_t k, uint32_t m, bool fp16, CUtensorMap* map) {
+    const cuuint64_t dims[2] = {k, m};
+    const cuuint64_t strides[1] = {(cuuint64_t)k * 2u};
+    const cuuint32_t box[2] = {kBK, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                           const_cast<uint16_t*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? ARC_OK : set_error(ARC_E_INVALID_ARGUMENT, "gemm: tensor map for X rejected");
+}
+}  // namespace
+
 int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
-                 const float* residual, float* y, cudaStream_t stream, bool fp16) {
+                 const float* residual, float* y, cudaStream_t stream, int mode, const uint16_t* x_lo) {
     if (fmt != 12 && fmt != 14) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: weights must be Q4_K or Q6_K");
-    if (!w || !x || !y) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: null pointer");
+    if (mode < 0 || mode > 2) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: operand mode 0 (bf16), 1 or 2 (fp16)");
+    if (!w || !x || !y || (mode == 2 && !x_lo)) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: null pointer");
     if (m == 0 || m > 256 || n == 0 || n % kBN || k == 0 || k % 256u)
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "gemm: needs 1 <= M <= 256, N % 128 == 0, K % 256 == 0");
     if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
-         reinterpret_cast<uintptr_t>(residual)) & 15u)
+         reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(x_lo)) & 15u)
         return set_error(ARC_E_ALIGNMENT, "gemm: W, X, residual and Y must be 16-byte aligned");
     int st = gemm_q4k_bf16_prepare();
     if (st != ARC_OK) return st;
     EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(ARC_E_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {k, m};
-    const cuuint64_t strides[1] = {(cuuint64_t)k * 2u};
-    const cuuint32_t box[2] = {kBK, 128};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(&map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                           const_cast<uint16_t*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: tensor map for X rejected");
+    CUtensorMap map, map_lo;
+    st = encode_x_map(enc, x, k, m, mode >= 1, &map);
+    if (st == ARC_OK) st = encode_x_map(enc, mode == 2 ? x_lo : x, k, m, mode >= 1, &map_lo);
+    if (st != ARC_OK) return st;
     // split K so that about one CTA per SM is busy (whole super-blocks per split)
     int dev = 0;
     cudaGetDevice(&dev);
@@ -619,16 +756,14 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
     const dim3 grid(tiles, ks), block(kThreads);
     unsigned int* err = dev_error_word();
     cudaError_t e;
-    if (fp16)
-        e = fmt == 12 ? launch_kernel(gemm_kq_bf16_kernel<12, true>, grid, block, kSmemBytes, stream, map, wb, n, k, m,
-                                      residual, y, err, sk)
-                      : launch_kernel(gemm_kq_bf16_kernel<14, true>, grid, block, kSmemBytes, stream, map, wb, n, k, m,
-                                      residual, y, err, sk);
+#define ARC_GEMM_LAUNCH(F, M)                                                                                   \
+    launch_kernel(gemm_kq_bf16_kernel<F, M>, grid, block, smem_bytes<M>(), stream, map, map_lo, wb, n, k, m, \
+                  residual, y, err, sk)
+    if (fmt == 12)
+        e = mode == 0 ? ARC_GEMM_LAUNCH(12, 0) : mode == 1 ? ARC_GEMM_LAUNCH(12, 1) : ARC_GEMM_LAUNCH(12, 2);
     else
-        e = fmt == 12 ? launch_kernel(gemm_kq_bf16_kernel<12, false>, grid, block, kSmemBytes, stream, map, wb, n, k,
-                                      m, residual, y, err, sk)
-                      : launch_kernel(gemm_kq_bf16_kernel<14, false>, grid, block, kSmemBytes, stream, map, wb, n, k,
-                                      m, residual, y, err, sk);
+        e = mode == 0 ? ARC_GEMM_LAUNCH(14, 0) : mode == 1 ? ARC_GEMM_LAUNCH(14, 1) : ARC_GEMM_LAUNCH(14, 2);
+#undef ARC_GEMM_LAUNCH
     if (e == cudaSuccess && ks > 1) {
         const uint64_t n4 = (uint64_t)m * n / 4u;
         const uint32_t blocks = (uint32_t)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)sms * 8u);

@@ -13,7 +13,7 @@
 // + residual.  Then output RMSNorm fused into the LM head, argmax, finalize.
 // The prompt (all but its last token) is consumed in batches of up to 256
 // rows on the tensor cores (enqueue_prefill_chunk: tcgen05 GEMMs for every
-// projection, fp16 operands for Q/K/V and bf16 for the rest, batched RMSNorm / RoPE + KV store / causal attention /
+// projection, fp16 hi + lo operands for Q/K/V and bf16 for the rest, batched RMSNorm / RoPE + KV store / causal attention /
 // SiLU kernels -- the reference's prefill chain, src/arcllm_v1_runtime.cpp:
 // 340-369), or, in prefill mode 0, token by token through the decode layer
 // chain without the LM head (the prefill graph, fp32 throughout).
@@ -66,7 +66,7 @@ struct arcllm_cuda_model {
     void* pf_arena = nullptr;
     float *pf_h = nullptr, *pf_h2 = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_g = nullptr,
           *pf_u = nullptr;
-    uint16_t *pf_xb = nullptr, *pf_attn = nullptr, *pf_s = nullptr;
+    uint16_t *pf_xb = nullptr, *pf_xb_lo = nullptr, *pf_attn = nullptr, *pf_s = nullptr;
     uint32_t launches_prefill_batched = 0;
     uint32_t begun_prompt = 0;  // prompt length of the last begin() (0: none)
 
@@ -295,7 +295,7 @@ int prefill_alloc(arcllm_cuda_model* m) {
     };
     const size_t o_h = take(4 * T * H), o_h2 = take(4 * T * H), o_q = take(4 * T * H), o_k = take(4 * T * KV),
                  o_v = take(4 * T * KV), o_g = take(4 * T * F), o_u = take(4 * T * F), o_xb = take(2 * T * H),
-                 o_attn = take(2 * T * H), o_s = take(2 * T * F);
+                 o_xb_lo = take(2 * T * H), o_attn = take(2 * T * H), o_s = take(2 * T * F);
     const cudaError_t e = cudaMalloc(&m->pf_arena, off);
     if (e != cudaSuccess) {
         m->pf_arena = nullptr;
@@ -310,6 +310,7 @@ int prefill_alloc(arcllm_cuda_model* m) {
     m->pf_g = reinterpret_cast<float*>(a + o_g);
     m->pf_u = reinterpret_cast<float*>(a + o_u);
     m->pf_xb = reinterpret_cast<uint16_t*>(a + o_xb);
+    m->pf_xb_lo = reinterpret_cast<uint16_t*>(a + o_xb_lo);
     m->pf_attn = reinterpret_cast<uint16_t*>(a + o_attn);
     m->pf_s = reinterpret_cast<uint16_t*>(a + o_s);
     return ARC_OK;
@@ -328,13 +329,13 @@ int enqueue_prefill_chunk(arcllm_cuda_model* m, uint32_t pos0, uint32_t T, cudaS
         int type_down = 0;
         const void* w_down = prefill_down_w(m, l, &type_down);
         // Q, K and V feed the attention scores, which the synthetic models make nearly one-hot
-        // (q.k/sqrt(d) of 1e3-1e4): their GEMMs run on fp16 operands (11 significant bits;
-        // bf16's rounding of the sub-block scales moved near-tied positions), the other
-        // GEMMs on bf16
-        ARC_TRY(launch_rmsnorm_rows_bf16(m->pf_h, L.attn_norm, c.rms_eps, T, H, m->pf_xb, st, true));
-        ARC_TRY(gemm_kq_bf16(L.type_q, L.wq, H, H, m->pf_xb, T, nullptr, m->pf_q, st, true));
-        ARC_TRY(gemm_kq_bf16(L.type_k, L.wk, KV, H, m->pf_xb, T, nullptr, m->pf_k, st, true));
-        ARC_TRY(gemm_kq_bf16(L.type_v, L.wv, KV, H, m->pf_xb, T, nullptr, m->pf_v, st, true));
+        // (q.k/sqrt(d) of 1e3-1e4): their GEMMs take fp16 hi + lo halves of both operands
+        // (~22 bits; bf16's or a single fp16's rounding of the weights moved near-tied
+        // positions of long prompts), the other GEMMs bf16
+        ARC_TRY(launch_rmsnorm_rows_bf16(m->pf_h, L.attn_norm, c.rms_eps, T, H, m->pf_xb, st, true, m->pf_xb_lo));
+        ARC_TRY(gemm_kq_bf16(L.type_q, L.wq, H, H, m->pf_xb, T, nullptr, m->pf_q, st, 2, m->pf_xb_lo));
+        ARC_TRY(gemm_kq_bf16(L.type_k, L.wk, KV, H, m->pf_xb, T, nullptr, m->pf_k, st, 2, m->pf_xb_lo));
+        ARC_TRY(gemm_kq_bf16(L.type_v, L.wv, KV, H, m->pf_xb, T, nullptr, m->pf_v, st, 2, m->pf_xb_lo));
         RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
         ARC_TRY(launch_rope_kv_rows(m->pf_q, m->pf_k, m->pf_v, L.bq, L.bk, L.bv, m->rope, pos0, T, m->kc, m->vc, rs,
                                     st));

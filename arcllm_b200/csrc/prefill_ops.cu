@@ -39,7 +39,8 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
 template <bool FP16>
 __global__ void __launch_bounds__(256) rmsnorm_rows_bf16_kernel(const float* __restrict__ x,
                                                                 const float* __restrict__ gamma, float eps, uint32_t h,
-                                                                uint16_t* __restrict__ out, unsigned int* err) {
+                                                                uint16_t* __restrict__ out,
+                                                                uint16_t* __restrict__ out_lo, unsigned int* err) {
     __shared__ double red[8];
     const float* xr = x + (uint64_t)blockIdx.x * h;
     double ss = 0.0;
@@ -55,6 +56,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_bf16_kernel(const float* __r
     for (int w = 0; w < 8; ++w) tot += red[w];
     const float inv = 1.0f / sqrtf((float)(tot / (double)h) + eps);
     uint16_t* o = out + (uint64_t)blockIdx.x * h;
+    uint16_t* ol = out_lo ? out_lo + (uint64_t)blockIdx.x * h : nullptr;
     bool range = false;
     for (uint32_t i = threadIdx.x; i < h; i += 256u) {
         const float v = (xr[i] * inv) * gamma[i];
@@ -62,6 +64,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_bf16_kernel(const float* __r
             const __half hv = __float2half_rn(v);
             range |= __hisinf(hv) != 0 && isfinite(v);
             o[i] = __half_as_ushort(hv);
+            if (ol) ol[i] = __half_as_ushort(__float2half_rn(v - __half2float(hv)));
         } else {
             o[i] = f2bf(v);
         }
@@ -348,14 +351,14 @@ int launch_prefill_done(GreedyState* st, const uint32_t* prompt, uint32_t n_prom
 }
 
 int launch_rmsnorm_rows_bf16(const float* x, const float* gamma, float eps, uint32_t rows, uint32_t h, uint16_t* out,
-                             cudaStream_t stream, bool fp16) {
+                             cudaStream_t stream, bool fp16, uint16_t* out_lo) {
     if (rows == 0) return ARC_OK;
     if (!x || !gamma || !out || h == 0) return set_error(ARC_E_INVALID_ARGUMENT, "rmsnorm rows: null pointer or h 0");
     const cudaError_t e =
         fp16 ? launch_kernel(rmsnorm_rows_bf16_kernel<true>, dim3(rows), dim3(256), 0, stream, x, gamma, eps, h, out,
-                             dev_error_word())
+                             out_lo, dev_error_word())
              : launch_kernel(rmsnorm_rows_bf16_kernel<false>, dim3(rows), dim3(256), 0, stream, x, gamma, eps, h, out,
-                             dev_error_word());
+                             static_cast<uint16_t*>(nullptr), dev_error_word());
     return launch_checked(e, "rmsnorm rows launch");
 }
 

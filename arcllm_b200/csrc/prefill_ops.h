@@ -9,9 +9,10 @@
 namespace arc {
 
 // out[r][i] = v rounded to bf16 (or fp16 when `fp16`; an overflow sets the
-// device error word's range bit), v = (x[r][i] * rsqrt(mean_i(x[r]^2) + eps)) * gamma[i]
+// device error word's range bit), v = (x[r][i] * rsqrt(mean_i(x[r]^2) + eps)) * gamma[i];
+// fp16 only: out_lo (nullable) = fp16(v - out)
 int launch_rmsnorm_rows_bf16(const float* x, const float* gamma, float eps, uint32_t rows, uint32_t h, uint16_t* out,
-                             cudaStream_t stream, bool fp16 = false);
+                             cudaStream_t stream, bool fp16 = false, uint16_t* out_lo = nullptr);
 // rows t of q[rows][q_heads*hd], k, v[rows][kv_dim] (+ biases, nullable): RoPE
 // at position pos0+t, q and k rotated in place, k and v stored to the fp16 cache
 int launch_rope_kv_rows(float* q, float* k, const float* v, const float* bq, const float* bk, const float* bv,

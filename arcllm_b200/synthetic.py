@@ -86,12 +86,20 @@ def tensor_bytes(s):
 class SyntheticModel:
     """A synthetic model resident on one GPU, wired into the C-ABI model."""
 
-    def __init__(self, cfg=None, types=None, seed=0xA2C11, device=0, torch=None):
+    def __init__(self, cfg=None, types=None, seed=0xA2C11, device=None, torch=None):
+        """device: the CUDA device index (default: the current device, the one
+        the library launches on -- tensors elsewhere would be another GPU's
+        memory to the kernels)."""
         if torch is None:
             import torch
         self.torch = torch
         self.cfg = dict(QWEN25_7B if cfg is None else cfg)
         self.specs = tensor_specs(self.cfg, types, seed)
+        if device is None:
+            device = torch.cuda.current_device()
+        elif device != torch.cuda.current_device():
+            raise ValueError("SyntheticModel: device %d is not the current device %d" %
+                             (device, torch.cuda.current_device()))
         self.dev = torch.device("cuda", device)
         L = lib()
         self.L = L

@@ -219,13 +219,28 @@ ARCLLM_CUDA_API int arcllm_cuda_gemm_bf16(int type, const void *w, uint32_t n, u
  * inside the fp16 range (|x| < 65504). */
 ARCLLM_CUDA_API int arcllm_cuda_gemm_f16(int type, const void *w, uint32_t n, uint32_t k, const uint16_t *x_f16,
                                          uint32_t m, const float *residual, float *y, void *stream);
+/* The same GEMM with ~22 significant bits of both operands: the activation as
+ * fp16 halves x_hi = fp16(x), x_lo = fp16(x - x_hi), each weight dequantised
+ * exactly in fp32 (as src/p8c_segmented_access_correctness.cpp:1166-1181 and
+ * :944-956 do) and split into fp16 halves, y = residual + x_hi W_hi^T +
+ * x_lo W_hi^T + x_hi W_lo^T (three MMAs per K step, fp32 accumulation).
+ * generate() uses it for the prefill Q/K/V projections
+ * (src/arcllm_v1_runtime.cpp:349-353): in the synthetic 7B-shape models the
+ * attention scores run to 1e4, near-tied prompt positions are common over a
+ * 255-row prompt, and one-operand fp16 rounding (~3.5e-4) moved whole cache
+ * rows.  Same shapes and alignment as arcllm_cuda_gemm_bf16; |x| < 65504. */
+ARCLLM_CUDA_API int arcllm_cuda_gemm_f16x3(int type, const void *w, uint32_t n, uint32_t k, const uint16_t *x_hi,
+                                           const uint16_t *x_lo, uint32_t m, const float *residual, float *y,
+                                           void *stream);
 /* Batched RMSNorm of the prefill chain (shaders/p7_rmsnorm_seq.comp per row,
  * src/arcllm_v1_runtime.cpp:347,355; sum of squares in double as
  * src/p8c_segmented_access_correctness.cpp:958-969): out[r][i] = v rounded to
- * bf16 (out_fp16 == 0) or fp16, v = x[r][i] * rsqrt(mean(x[r]^2) + eps) * gamma[i].
- * An fp16 value that overflows sets bit 2 of the device error word. */
+ * bf16 (out_fp16 == 0) or fp16, v = x[r][i] * rsqrt(mean(x[r]^2) + eps) * gamma[i];
+ * with fp16 output and a non-null out_lo also out_lo[r][i] = fp16(v - out[r][i])
+ * (the x_lo of arcllm_cuda_gemm_f16x3).  An fp16 value that overflows sets bit 2
+ * of the device error word. */
 ARCLLM_CUDA_API int arcllm_cuda_rmsnorm_rows(const float *x, const float *gamma, float eps, uint32_t rows, uint32_t h,
-                                             int out_fp16, uint16_t *out, void *stream);
+                                             int out_fp16, uint16_t *out, uint16_t *out_lo, void *stream);
 
 /* ---- synthetic fixture streams -------------------------------------------
  * Deterministic, counter-based generators (element n of a splitmix64

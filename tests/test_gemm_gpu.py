@@ -186,7 +186,9 @@ def test_rmsnorm_rows(fp16):
     g = O.normal_f32(h, 78, 1.0, 0.1)
     xd, gd = G.to_dev(x), G.to_dev(g)
     out = torch.empty(rows * h, dtype=torch.int16, device=G.dev())
-    A.call("arcllm_cuda_rmsnorm_rows", G.ptr(xd), G.ptr(gd), C.c_float(eps), rows, h, fp16, G.ptr(out), G.stream())
+    lo = torch.zeros(rows * h, dtype=torch.int16, device=G.dev()) if fp16 else None
+    A.call("arcllm_cuda_rmsnorm_rows", G.ptr(xd), G.ptr(gd), C.c_float(eps), rows, h, fp16, G.ptr(out), G.ptr(lo),
+           G.stream())
     raw = G.host(out).view(np.uint16)
     got = raw.view(np.float16).astype(np.float32) if fp16 else (raw.astype(np.uint32) << 16).view(np.float32)
     ss = (x.astype(np.float64) ** 2).sum(axis=1)
@@ -195,4 +197,40 @@ def test_rmsnorm_rows(fp16):
     want = bf16_round(v, torch.float16 if fp16 else torch.bfloat16)
     assert np.mean(got.reshape(rows, h) == want) > 0.999
     assert np.abs(got.reshape(rows, h) - v).max() <= 2.0 ** (-10 if fp16 else -7) * np.abs(v).max()
+    if fp16:  # hi + lo carries ~22 bits of v
+        lv = G.host(lo).view(np.uint16).view(np.float16).astype(np.float64).reshape(rows, h)
+        err = np.abs(got.reshape(rows, h).astype(np.float64) + lv - v)
+        assert err.max() <= 2.0 ** -20 * np.abs(v).max()
     G.check_device_error()
+
+
+@pytest.mark.parametrize("fmt,m,n,k,res", [("q4k", 255, 3584, 3584, False), ("q4k", 255, 512, 3584, True),
+                                           ("q6k", 255, 512, 3584, False), ("q6k", 100, 384, 1024, True),
+                                           ("q4k", 256, 128, 18944, False), ("q4k", 1, 128, 512, False)])
+def test_gemm_f16x3_near_fp32(fmt, m, n, k, res):
+    """arcllm_cuda_gemm_f16x3: fp16 hi + lo halves of the activation and of the
+    exactly dequantised weights, three products into fp32.  Within 2e-6 of the
+    fp32-activation, fp32-weight product (the reference's fp32 dequant GEMM;
+    the bf16 form is ~2.4e-3 from it, the single-fp16 form ~3.6e-4)."""
+    seed = 2500 + m + n + k
+    w_host = O.fill_weights(fmt, n, k, seed)
+    w = G.to_dev(w_host)
+    x32 = O.normal_f32(m * k, seed + 1).reshape(m, k)
+    xh = torch.from_numpy(x32).to(torch.float16)
+    xl = torch.from_numpy((x32 - xh.float().numpy()).astype(np.float32)).to(torch.float16)
+    xh, xl = xh.to(G.dev()), xl.to(G.dev())
+    r = torch.from_numpy(O.normal_f32(m * n, seed + 2).reshape(m, n)).to(G.dev()) if res else None
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device=G.dev())
+    A.call("arcllm_cuda_gemm_f16x3", 12 if fmt == "q4k" else 14, G.ptr(w), n, k, C.c_void_p(xh.data_ptr()),
+           C.c_void_p(xl.data_ptr()), m, C.c_void_p(r.data_ptr()) if res else None, C.c_void_p(y.data_ptr()),
+           G.stream())
+    torch.cuda.synchronize()
+    G.check_device_error()
+    yv = y.cpu().numpy().astype(np.float64)
+    wd = O.dequant(fmt, w_host, n, k).reshape(n, k).astype(np.float64)
+    rr = r.cpu().numpy().astype(np.float64) if res else 0.0
+    y_f = x32.astype(np.float64) @ wd.T
+    rel = np.linalg.norm(yv - rr - y_f) / np.linalg.norm(y_f)
+    print("f16x3 gemm %s %dx%dx%d res=%d: rel-L2 %.2e vs fp32 x and W" % (fmt, m, n, k, res, rel))
+    assert np.isfinite(yv).all()
+    assert rel <= 2e-6

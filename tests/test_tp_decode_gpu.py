@@ -84,6 +84,86 @@ def _free_port():
     return p
 
 
+def _device_status():
+    """(status, error bits) of the device after a synchronise: a CUDA fault or
+    a device-side timeout shows up here, at the step that caused it."""
+    bits = C.c_uint32(0)
+    st = A.lib().arcllm_cuda_device_error(C.c_void_p(torch.cuda.current_stream().cuda_stream), C.byref(bits))
+    msg = A.lib().arcllm_cuda_last_error_message().decode() if st else ""
+    return st, bits.value, msg
+
+
+def _ex_worker(rank, world, port, q):
+    """Exchanges shaped like the decode step's (s, hidden state, greedy
+    records), each checked on the spot."""
+    try:
+        import torch
+        import torch.distributed as dist
+
+        from arcllm_b200.rank_gather import ExchangeBuffers
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+
+        def exchange(h):
+            out = [None] * world
+            dist.all_gather_object(out, h)
+            return out
+
+        ex = ExchangeBuffers(18944, world, rank, exchange)
+        dist.barrier()
+        sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        bad = []
+        for e in range(12):
+            n_total = (18944, 3584, 4 * world)[e % 3]
+            if n_total == 4 * world:
+                off, n_local = 4 * rank, 4
+            else:
+                r0, rows = C.c_uint32(0), C.c_uint32(0)
+                A.call("arcllm_cuda_shard_rows", n_total, 32, world, rank, C.byref(r0), C.byref(rows))
+                off, n_local = r0.value, rows.value
+            want = (torch.arange(n_total, dtype=torch.int64) * 7 + e * 100003).to(torch.int32)
+            src = want[off:off + n_local].clone().to("cuda")
+            dst = torch.zeros(n_total, dtype=torch.int32, device="cuda")
+            ex.gather(C.c_void_p(src.data_ptr()), n_local, off, C.c_void_p(dst.data_ptr()), n_total, sp,
+                      timeout_us=5000000)
+            st, bits, msg = _device_status()
+            if st or bits:
+                raise RuntimeError("exchange %d: status %d bits %#x %s" % (e, st, bits, msg))
+            if not torch.equal(dst.cpu(), want):
+                bad.append(e)
+        dist.barrier()
+        ex.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, bad, ""))
+    except Exception as exc:  # reported to the parent
+        q.put((rank, None, repr(exc)))
+
+
+@pytest.mark.parametrize("world", [2])
+def test_exchange_two_ranks(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ex_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = sorted(q.get(timeout=300) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    msgs = ["rank %d: %s" % (r, m) for r, _, m in res if m]
+    assert not msgs, "; ".join(msgs)
+    for rank, bad, _ in res:
+        assert bad == [], "rank %d: exchanges %s assembled a wrong vector" % (rank, bad)
+
+
 def _tp_worker(rank, world, port, prompt, n_new, q):
     try:
         import torch
@@ -100,14 +180,22 @@ def _tp_worker(rank, world, port, prompt, n_new, q):
             dist.all_gather_object(out, h)
             return out
 
+        def checked(what):
+            st, bits, msg = _device_status()
+            if st or bits:
+                raise RuntimeError("%s: status %d bits %#x %s" % (what, st, bits, msg))
+
         m = SyntheticModel(CFG, seed=0x5EED + 40)
+        checked("model")
         ex = ExchangeBuffers(m.tp_exchange_words(world), world, rank, exchange)
         m.set_tensor_parallel(ex.ptrs, world, rank, timeout_us=5000000)
+        checked("tensor-parallel set-up")
         dist.barrier()
         res = {}
         for mode in (1, 0):  # batched prefill, then the token path (exchanges in the prefill graph)
             m.set_prefill_mode(mode)
             toks, st = m.generate(prompt, n_new)
+            checked("generate, prefill mode %d" % mode)
             res[mode] = (toks, st.decode_launches_per_step)
             dist.barrier()
         bits = C.c_uint32(0)
@@ -145,9 +233,10 @@ def test_tp_generate_matches_single_gpu(world):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
+    msgs = ["rank %d: %s" % (r, m) for r, _, _, _, m in res if m]
+    assert not msgs, "; ".join(msgs)
     ref = res[0][2]
     for rank, out, _, bits, msg in res:
-        assert msg == "", "rank %d: %s" % (rank, msg)
         assert bits == 0, "rank %d device error %#x" % (rank, bits)
         for mode in (1, 0):
             toks, launches = out[mode]
