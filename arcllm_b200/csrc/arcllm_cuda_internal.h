@@ -101,6 +101,12 @@ int matvec_splitk_reserve(int fmt, uint32_t rows, uint32_t k);
 bool matvec_splitk_supported(int fmt, bool dual, uint32_t rows, uint32_t k);
 int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, const float* x, const float* gamma,
                          float eps, const float* bias, const float* residual, float* y, cudaStream_t stream);
+// The K-slice kernel over super-blocks [kb_base, kb_base + nb_win) of every row (x indexed by
+// the full K; no RMSNorm): the tensor-parallel FFN down projection of a rank's slice of s.
+int matvec_kwindow_launch(int fmt, const void* w, uint32_t rows, uint32_t k, uint32_t kb_base, uint32_t nb_win,
+                          const float* x, const float* gamma, float eps, const float* bias, const float* residual,
+                          float* y, cudaStream_t stream);
+int matvec_kwindow_reserve(int fmt, uint32_t rows, uint32_t nb_win);
 // Pick the kernel for a matvec: the integer tensor-core forms where they
 // apply (whole rows for K <= 3584, K slices for K > 3584), else the CUDA-core
 // streaming form (ARCLLM_MATVEC_IMPL=cuda forces the CUDA-core form).
@@ -122,6 +128,10 @@ uint64_t exchange_buffer_bytes(uint32_t max_words);
 // contributes at its offset `off` (32-bit words).
 int exchange_gather(const ExchangeRanks& ex, const void* src, uint32_t n_local, uint32_t off, void* dst,
                     uint32_t n_total, cudaStream_t stream);
+// dst[i] = residual[i] (nullable) + sum over ranks r (in rank order) of rank r's src[i], i < n,
+// on every rank; needs n_ranks * n <= max_words.
+int exchange_reduce(const ExchangeRanks& ex, const float* src, uint32_t n, const float* residual, float* dst,
+                    cudaStream_t stream);
 int shard_rows(uint32_t n, uint32_t align, uint32_t n_ranks, uint32_t rank, uint32_t* row0, uint32_t* rows);
 
 // cuTensorMapEncodeTiled (driver entry point), or null (gemm_tcgen05.cu).

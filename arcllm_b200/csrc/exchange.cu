@@ -9,12 +9,15 @@
 // state h (3584 floats) and the greedy-selection records (4 words per rank).
 //
 // exchange_gather_kernel is one CTA per rank.  It stores this rank's slice of
-// the vector into every rank's exchange buffer (its own with local stores,
+// the vector (or, in the reduce form, its whole partial vector into slot
+// `rank`) into every rank's exchange buffer (its own with local stores,
 // the others with NVLink peer stores -- stores only, nothing reads another
 // GPU's memory), fences at system scope, publishes the exchange's sequence
 // number in its slot of every rank's flag array (release) and waits (acquire,
 // bounded by %globaltimer) until every slot of its own array has reached it;
-// then it copies the assembled vector out of its own buffer into `dst`.
+// then it copies the assembled vector out of its own buffer into `dst` (reduce
+// form: adds the ranks' slots in rank order, plus an optional residual -- the
+// all-reduce of the K-sharded FFN down projection).
 //
 // Buffer of one rank (32-bit words; W = the largest vector rounded up to 4):
 //   [0, 2W)        two data regions, picked by the parity of the sequence number
@@ -47,6 +50,10 @@ struct ExParams {
     uint32_t W, n_local, off, n_total, n_ranks, rank;
     unsigned long long wait_ns;
     unsigned int* err;
+    // reduce form: every rank contributes a whole n_total-float vector (slot `rank` of the
+    // region) and dst = residual (nullable) + the slots added in rank order
+    uint32_t reduce;
+    const float* residual;
 };
 
 __global__ void __launch_bounds__(1024) exchange_gather_kernel(const ExParams p) {
@@ -97,6 +104,16 @@ __global__ void __launch_bounds__(1024) exchange_gather_kernel(const ExParams p)
     if (!s_ok) return;
     // the peers' stores landed in this GPU's memory; read them from L2, not a stale L1 line
     const uint32_t* own = p.data[p.rank] + region;
+    if (p.reduce) {  // the same sum, in the same order, on every rank
+        const float* slots = reinterpret_cast<const float*>(own);
+        float* out = reinterpret_cast<float*>(p.dst);
+        for (uint32_t i = tid; i < p.n_total; i += nt) {
+            float t = __ldcg(slots + i);
+            for (uint32_t q = 1; q < p.n_ranks; ++q) t += __ldcg(slots + (uint64_t)q * p.n_total + i);
+            out[i] = p.residual ? p.residual[i] + t : t;
+        }
+        return;
+    }
     if ((p.n_total & 3u) == 0u && (reinterpret_cast<uintptr_t>(p.dst) & 15u) == 0u) {
         const uint4* s4 = reinterpret_cast<const uint4*>(own);
         uint4* d4 = reinterpret_cast<uint4*>(p.dst);
@@ -115,12 +132,9 @@ uint64_t exchange_buffer_bytes(uint32_t max_words) {
     return ((uint64_t)(2u * region_words(max_words) + kFlagWords + 8u) * 4u + 255u) / 256u * 256u;
 }
 
-int exchange_gather(const ExchangeRanks& ex, const void* src, uint32_t n_local, uint32_t off, void* dst,
-                    uint32_t n_total, cudaStream_t stream) {
-    if (ex.n_ranks == 0 || ex.n_ranks > kMaxExRanks || ex.rank >= ex.n_ranks)
-        return set_error(ARC_E_INVALID_ARGUMENT, "exchange: 1..8 ranks, rank < n_ranks");
-    if (!src || !dst || n_total == 0 || n_total > ex.max_words || off + n_local > n_total)
-        return set_error(ARC_E_INVALID_ARGUMENT, "exchange: bad slice or vector size");
+namespace {
+int exchange_launch(const ExchangeRanks& ex, const void* src, uint32_t n_local, uint32_t off, void* dst,
+                    uint32_t n_total, const float* residual, bool reduce, cudaStream_t stream) {
     if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 3u)
         return set_error(ARC_E_ALIGNMENT, "exchange: src and dst must be 4-byte aligned");
     ExParams p{};
@@ -141,7 +155,29 @@ int exchange_gather(const ExchangeRanks& ex, const void* src, uint32_t n_local, 
     p.rank = ex.rank;
     p.wait_ns = (unsigned long long)(ex.timeout_us ? ex.timeout_us : 2000000u) * 1000ull;
     p.err = dev_error_word();
+    p.reduce = reduce ? 1u : 0u;
+    p.residual = residual;
     return launch_checked(launch_kernel(exchange_gather_kernel, dim3(1), dim3(1024), 0, stream, p), "exchange launch");
+}
+}  // namespace
+
+int exchange_gather(const ExchangeRanks& ex, const void* src, uint32_t n_local, uint32_t off, void* dst,
+                    uint32_t n_total, cudaStream_t stream) {
+    if (ex.n_ranks == 0 || ex.n_ranks > kMaxExRanks || ex.rank >= ex.n_ranks)
+        return set_error(ARC_E_INVALID_ARGUMENT, "exchange: 1..8 ranks, rank < n_ranks");
+    if (!src || !dst || n_total == 0 || n_total > ex.max_words || off + n_local > n_total)
+        return set_error(ARC_E_INVALID_ARGUMENT, "exchange: bad slice or vector size");
+    return exchange_launch(ex, src, n_local, off, dst, n_total, nullptr, false, stream);
+}
+
+int exchange_reduce(const ExchangeRanks& ex, const float* src, uint32_t n, const float* residual, float* dst,
+                    cudaStream_t stream) {
+    if (ex.n_ranks == 0 || ex.n_ranks > kMaxExRanks || ex.rank >= ex.n_ranks)
+        return set_error(ARC_E_INVALID_ARGUMENT, "exchange: 1..8 ranks, rank < n_ranks");
+    if (!src || !dst || n == 0 || (uint64_t)n * ex.n_ranks > ex.max_words)
+        return set_error(ARC_E_INVALID_ARGUMENT, "exchange reduce: n_ranks * n exceeds the buffer");
+    if (dst == residual || dst == src) return set_error(ARC_E_INVALID_ARGUMENT, "exchange reduce: dst must not alias");
+    return exchange_launch(ex, src, n, ex.rank * n, dst, n, residual, true, stream);
 }
 
 // Contiguous shard [row0, row0 + rows) of n rows for `rank` of n_ranks: whole

@@ -50,6 +50,9 @@ struct MvParams {
     float* peer_y[kMaxRanks];
     uint32_t* peer_flags[kMaxRanks];
     uint32_t* done_ctr;
+    // K-slice kernel only: the first super-block of the K window this launch covers
+    // (the matrix rows keep their full length rb; nb counts the window's blocks)
+    uint32_t kb_base;
 };
 
 // Fold N per-row partial sums over the warp: afterwards lane L holds the full

@@ -248,8 +248,9 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1)
                         const uint32_t bw = sv.cbw[c];
 #pragma unroll
                         for (uint32_t i = 0; i < Rs; ++i) {
-                            const uint32_t xb =
-                                (uint32_t)(((uint64_t)i * p.rb + (uint64_t)(kb0 + sv.cst[c]) * bsz) & ~(uint64_t)15);
+                            const uint32_t xb = (uint32_t)(((uint64_t)i * p.rb +
+                                                            (uint64_t)(p.kb_base + kb0 + sv.cst[c]) * bsz) &
+                                                           ~(uint64_t)15);
                             tma_box_2d(stg + sv.coff[c] + i * J * bw, mp, (int)(xb / 8u), (int)(grp * J), &full[s],
                                        pol);
                         }
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1)
     if (warp >= W) return;  // narrower slice: this warp has no super-block
 
     // this warp's super-block(s) of the slice: x slice, quantised, routed fragments
-    const uint32_t bA = kb0 + warp, bB = FMT == 14 ? kb0 + (warp ^ 1u) : bA;
+    const uint32_t bA = p.kb_base + kb0 + warp, bB = FMT == 14 ? p.kb_base + kb0 + (warp ^ 1u) : bA;
     XFrag f;
     {
         const uint32_t e0 = 256u * (jw < 4 ? bA : bB) + 32u * jw + 8u * qd;
@@ -340,7 +341,7 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const uint32_t r = r2[h], i = r % Rs;
-            const uint32_t mis = (uint32_t)(((uint64_t)i * p.rb + (uint64_t)(kb0 + cs) * bsz) & 15u);
+            const uint32_t mis = (uint32_t)(((uint64_t)i * p.rb + (uint64_t)(p.kb_base + kb0 + cs) * bsz) & 15u);
             o[h] = coff + (i * J + r / Rs) * bw + mis;
         }
         rowA[m] = o[0];
@@ -552,9 +553,19 @@ cudaError_t set_attr_ks() {
 
 }  // namespace
 
+int ks_reserve(int fmt, uint32_t rows, uint32_t k);
+
 int matvec_splitk_reserve(int fmt, uint32_t rows, uint32_t k) {
     if (!matvec_splitk_supported(fmt, false, rows, k)) return ARC_OK;  // another kernel serves this shape
+    return ks_reserve(fmt, rows, k);
+}
+
+int matvec_kwindow_reserve(int fmt, uint32_t rows, uint32_t nb_win) { return ks_reserve(fmt, rows, 256u * nb_win); }
+
+// Scratch for the plan of (fmt, rows, k); k is the covered K (a window's width).
+int ks_reserve(int fmt, uint32_t rows, uint32_t k) {
     const KsPlan pl = ks_plan_cached(fmt, rows, k, (uint32_t)ks_sm_count());
+    if (!pl.ok) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec split-K: no plan fits shared memory");
     const size_t need_part = (size_t)pl.q.P * rows, need_cnt = pl.n_groups;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -611,13 +622,29 @@ int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, cons
                          float eps, const float* bias, const float* residual, float* y, cudaStream_t stream) {
     if (!matvec_splitk_supported(fmt, false, rows, k))
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec split-K: shape not supported");
+    return matvec_kwindow_launch(fmt, w, rows, k, 0, k / 256u, x, gamma, eps, bias, residual, y, stream);
+}
+
+// Super-blocks [kb_base, kb_base + nb_win) of every row of a rows x k matrix:
+// y[r] = residual[r] + bias[r] + sum over the window of W[r][.] * x[.] (x indexed
+// by the full K).  The tensor-parallel decode runs the FFN down projection of
+// its own slice of s this way.  Q6_K: kb_base and nb_win even, rows % 4 == 0;
+// EXEC148: even rows.  No fused RMSNorm with a window.
+int matvec_kwindow_launch(int fmt, const void* w, uint32_t rows, uint32_t k, uint32_t kb_base, uint32_t nb_win,
+                          const float* x, const float* gamma, float eps, const float* bias, const float* residual,
+                          float* y, cudaStream_t stream) {
+    if ((fmt != 12 && fmt != 14 && fmt != ARC_TYPE_EXEC148) || rows == 0 || k % 256u || nb_win == 0 ||
+        kb_base + nb_win > k / 256u || nb_win > kNW * kMaxSlices || (gamma && nb_win != k / 256u) ||
+        (fmt == 14 && ((kb_base | nb_win) & 1u || (rows & 3u))) || (fmt == ARC_TYPE_EXEC148 && (rows & 1u)))
+        return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec K window: shape not supported");
+    const uint32_t kw = 256u * nb_win;
     if (!w || !x || !y) return set_error(ARC_E_INVALID_ARGUMENT, "matvec: null pointer");
     if (reinterpret_cast<uintptr_t>(w) & 15u)
         return set_error(ARC_E_ALIGNMENT, "matvec: weight pointers must be 16-byte aligned");
     int st = matvec_splitk_prepare();
-    if (st == ARC_OK) st = matvec_splitk_reserve(fmt, rows, k);
+    if (st == ARC_OK) st = ks_reserve(fmt, rows, kw);
     if (st != ARC_OK) return st;
-    KsPlan pl = ks_plan_cached(fmt, rows, k, (uint32_t)ks_sm_count());
+    KsPlan pl = ks_plan_cached(fmt, rows, kw, (uint32_t)ks_sm_count());
     if (!pl.ok) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec split-K: no plan fits shared memory");
     EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(ARC_E_CUDA, "matvec split-K: cuTensorMapEncodeTiled unavailable");
@@ -652,9 +679,10 @@ int matvec_splitk_launch(int fmt, const void* w, uint32_t rows, uint32_t k, cons
     p.y = y;
     p.err = dev_error_word();
     p.rows = rows;
-    p.k = k;
-    p.nb = nb;
+    p.k = kw;
+    p.nb = nb_win;
     p.rb = rb;
+    p.kb_base = kb_base;
     p.G = kG;
     p.n_groups = pl.n_groups;
     p.stages = pl.S;

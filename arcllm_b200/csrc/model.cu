@@ -70,11 +70,13 @@ struct arcllm_cuda_model {
     uint32_t launches_prefill_batched = 0;
     uint32_t begun_prompt = 0;  // prompt length of the last begin() (0: none)
 
-    // tensor parallelism (tp.n_ranks > 1): this rank's FFN gate/up rows [ffn_r0, +ffn_rows) and
-    // FFN down rows [hid_r0, +hid_rows) (its LM-head rows are lm_row0/lm_rows), the ranks'
-    // exchange buffers, the gathered greedy records (4 words per rank)
+    // tensor parallelism (tp.n_ranks > 1): this rank's FFN gate/up rows [ffn_r0, +ffn_rows) --
+    // the same range of s is its K window of the FFN down projection -- (its LM-head rows are
+    // lm_row0/lm_rows), the ranks' exchange buffers, the down projection's partial sums and
+    // the gathered greedy records (4 words per rank)
     arc::ExchangeRanks tp{};
-    uint32_t ffn_r0 = 0, ffn_rows = 0, hid_r0 = 0, hid_rows = 0;
+    uint32_t ffn_r0 = 0, ffn_rows = 0;
+    float* tp_part = nullptr;
     uint32_t* tp_recs = nullptr;
 };
 
@@ -94,6 +96,7 @@ uint64_t row_bytes(int type, uint32_t k) {
 // Rows of a tensor-parallel shard are whole 32-row groups (the matvecs' row
 // groups; keeps every shard's weight rows and vector slices 16-byte aligned).
 constexpr uint32_t kTpRowAlign = 32;
+constexpr uint32_t kTpFfnAlign = 512;  // FFN shards: pairs of 256-weight super-blocks
 
 int check_layer(const arcllm_cuda_model_config& c, const arcllm_cuda_layer& L) {
     if (!L.attn_norm || !L.ffn_norm || !L.wq || !L.wk || !L.wv || !L.wo || !L.w_gate || !L.w_up || !L.w_down)
@@ -187,19 +190,18 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
         ARC_TRY(mv(L.type_o, L.wo, H, H, m->attn, nullptr, 0.f, nullptr, hc, hm, st));
         n += 4 + (uint32_t)attention_launches(m->attn_splits, c.n_heads, c.n_kv_heads);  // Q K V (attn) O
         if (m->tp.n_ranks > 1) {
-            // this rank's gate/up rows -> its slice of s; all-gather s; its down rows (+ residual)
-            // -> its slice of the hidden state; all-gather the hidden state
-            const uint64_t rb_gu = row_bytes(ARC_GGML_Q4_K, H), rb_dn = row_bytes(L.type_down, c.ffn);
+            // this rank's gate/up rows -> its slice of s; the FFN down over the same K window
+            // (every output row, this slice's super-blocks) -> partial sums; the ranks' partials
+            // added in rank order plus the residual on every rank (one exchange per layer)
+            const uint64_t rb_gu = row_bytes(ARC_GGML_Q4_K, H);
             const uint8_t* wg = static_cast<const uint8_t*>(L.w_gate) + (uint64_t)m->ffn_r0 * rb_gu;
             const uint8_t* wu = static_cast<const uint8_t*>(L.w_up) + (uint64_t)m->ffn_r0 * rb_gu;
-            const uint8_t* wd = static_cast<const uint8_t*>(L.w_down) + (uint64_t)m->hid_r0 * rb_dn;
             ARC_TRY(matvec_any(ARC_GGML_Q4_K, true, wg, wu, m->ffn_rows, H, hm, L.ffn_norm, c.rms_eps, nullptr,
                                nullptr, m->s + m->ffn_r0, st));
-            ARC_TRY(exchange_gather(m->tp, m->s + m->ffn_r0, m->ffn_rows, m->ffn_r0, m->s, c.ffn, st));
-            ARC_TRY(mv(L.type_down, wd, m->hid_rows, c.ffn, m->s, nullptr, 0.f, nullptr, hm + m->hid_r0,
-                       hc + m->hid_r0, st));
-            ARC_TRY(exchange_gather(m->tp, hc + m->hid_r0, m->hid_rows, m->hid_r0, hc, H, st));
-            n += 4;
+            ARC_TRY(matvec_kwindow_launch(L.type_down, L.w_down, H, c.ffn, m->ffn_r0 / 256u, m->ffn_rows / 256u,
+                                          m->s, nullptr, 0.f, nullptr, nullptr, m->tp_part, st));
+            ARC_TRY(exchange_reduce(m->tp, m->tp_part, H, hm, hc, st));
+            n += 3;
         } else {
             ARC_TRY(matvec_any(ARC_GGML_Q4_K, true, L.w_gate, L.w_up, c.ffn, H, hm, L.ffn_norm, c.rms_eps, nullptr,
                                nullptr, m->s, st));
@@ -495,7 +497,7 @@ int model_set_endpoints(arcllm_cuda_model* m, const void* tok_embd, int tok_embd
 
 int model_tp_exchange_words(const arcllm_cuda_model_config* cfg, uint32_t n_ranks, uint32_t* out) {
     if (!cfg || !out || n_ranks == 0 || n_ranks > 8) return set_error(ARC_E_INVALID_ARGUMENT, "tp words: bad argument");
-    *out = std::max(std::max(cfg->ffn, cfg->hidden), 4u * n_ranks);
+    *out = std::max(n_ranks * cfg->hidden, 4u * n_ranks);  // the partials of every rank; the greedy records
     return ARC_OK;
 }
 
@@ -505,12 +507,13 @@ int model_set_tensor_parallel(arcllm_cuda_model* m, void* const* rank_bufs, uint
         return set_error(ARC_E_INVALID_ARGUMENT, "tensor parallel: 1..8 ranks, rank < n_ranks, buffers");
     const arcllm_cuda_model_config& c = m->cfg;
     ExchangeRanks tp{};
-    uint32_t fr0 = 0, frows = c.ffn, hr0 = 0, hrows = c.hidden, lr0 = 0, lrows = c.vocab;
+    uint32_t fr0 = 0, frows = c.ffn, lr0 = 0, lrows = c.vocab;
     if (n_ranks > 1) {
-        if (c.ffn % kTpRowAlign || c.hidden % kTpRowAlign || c.vocab % kTpRowAlign)
-            return set_error(ARC_E_UNSUPPORTED_SHAPE, "tensor parallel: ffn, hidden and vocab must be multiples of 32");
-        ARC_TRY(shard_rows(c.ffn, kTpRowAlign, n_ranks, rank, &fr0, &frows));
-        ARC_TRY(shard_rows(c.hidden, kTpRowAlign, n_ranks, rank, &hr0, &hrows));
+        // s in whole pairs of super-blocks (512 rows): a K window of the Q6_K down projection
+        // must start and end on an even block
+        if (c.ffn % kTpFfnAlign || c.vocab % kTpRowAlign || c.hidden % 4u)
+            return set_error(ARC_E_UNSUPPORTED_SHAPE, "tensor parallel: ffn % 512 == 0, vocab % 32 == 0");
+        ARC_TRY(shard_rows(c.ffn, kTpFfnAlign, n_ranks, rank, &fr0, &frows));
         ARC_TRY(shard_rows(c.vocab, kTpRowAlign, n_ranks, rank, &lr0, &lrows));
         uint32_t words = 0;
         ARC_TRY(model_tp_exchange_words(&c, n_ranks, &words));
@@ -523,16 +526,19 @@ int model_set_tensor_parallel(arcllm_cuda_model* m, void* const* rank_bufs, uint
         tp.rank = rank;
         tp.max_words = words;
         tp.timeout_us = timeout_us;
-        if (!m->tp_recs) {
-            const cudaError_t e = cudaMalloc(&m->tp_recs, 4u * 4u * 8u);
-            if (e != cudaSuccess) {
-                m->tp_recs = nullptr;
-                return set_cuda_error(e, "tensor parallel: greedy records");
-            }
+        if (!m->tp_part) {
+            void* p = nullptr;
+            const cudaError_t e = cudaMalloc(&p, 4ull * c.hidden + 256u);
+            if (e != cudaSuccess) return set_cuda_error(e, "tensor parallel: partial sums and greedy records");
+            m->tp_part = static_cast<float*>(p);
+            m->tp_recs = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(p) + 4ull * c.hidden);
         }
+        // split-K scratch for the down projection's K window, before any graph capture
+        const int down_types[3] = {ARC_GGML_Q4_K, ARC_GGML_Q6_K, ARC_TYPE_EXEC148};
+        for (int t : down_types) ARC_TRY(matvec_kwindow_reserve(t, c.hidden, frows / 256u));
     }
     m->tp = tp;
-    m->ffn_r0 = fr0, m->ffn_rows = frows, m->hid_r0 = hr0, m->hid_rows = hrows;
+    m->ffn_r0 = fr0, m->ffn_rows = frows;
     m->lm_row0 = lr0, m->lm_rows = lrows;
     // the captured step graphs hold the previous layout: re-capture on next use
     if (m->g_prefill) {
@@ -708,7 +714,7 @@ int model_destroy(arcllm_cuda_model* m) {
     if (m->g_decode) cudaGraphExecDestroy(m->g_decode);
     if (m->arena) cudaFree(m->arena);
     if (m->pf_arena) cudaFree(m->pf_arena);
-    if (m->tp_recs) cudaFree(m->tp_recs);
+    if (m->tp_part) cudaFree(m->tp_part);
     for (int i = 0; i < 2; ++i) {
         if (m->side[i]) cudaStreamDestroy(m->side[i]);
         if (m->ev_join[i]) cudaEventDestroy(m->ev_join[i]);

@@ -693,8 +693,9 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
         "weight_GB/s_whole_job": round(bpt * tps / 1e9, 1), "prefill_ms_256_tokens": round(pf_ms, 2),
         "e2e_generate_s": round(max_over_ranks(wall), 4), "launches_per_token": st.decode_launches_per_step,
         "ranks_agree": all(t == toks for t in same), "first_tokens": toks[:4],
-        "sharding": "FFN gate/up rows, FFN down rows and LM-head rows over %d ranks; attention replicated; "
-                    "s, hidden state and greedy records exchanged by the NVLink exchange kernel" % world}
+        "sharding": "FFN gate/up rows and the same K window of the FFN down projection over %d ranks (down "
+                    "partials all-reduced by the NVLink exchange kernel), LM-head rows sharded (greedy records "
+                    "exchanged); attention replicated" % world}
     torch.cuda.synchronize()
     barrier()
     md.close()

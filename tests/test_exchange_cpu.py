@@ -110,6 +110,35 @@ class FakeLib:
         C.memmove(dst, bufs[rank] + region, 4 * n_total)
         return 0
 
+    def exchange_reduce(self, bufs, n_ranks, rank, max_words, src, n, residual, dst, timeout_us):
+        """The reduce form: the whole vector into slot `rank`, then the slots summed in rank order."""
+        W = self._w(max_words)
+        flags = [bufs[q] + 8 * W for q in range(n_ranks)]
+        seq_addr = flags[rank] + 32
+        seq = (struct.unpack("<I", C.string_at(seq_addr, 4))[0] + 1) & 0xFFFFFFFF
+        region = 4 * W * (seq & 1)
+        for q in range(n_ranks):
+            C.memmove(bufs[q] + region + 4 * n * rank, src, 4 * n)
+        for q in range(n_ranks):
+            C.memmove(flags[q] + 4 * rank, struct.pack("<I", seq), 4)
+        t0 = time.time()
+        while True:
+            slots = struct.unpack("<%dI" % n_ranks, C.string_at(flags[rank], 4 * n_ranks))
+            if all(((s - seq) & 0xFFFFFFFF) < 0x80000000 for s in slots):
+                break
+            if time.time() - t0 > timeout_us * 1e-6:
+                C.memmove(seq_addr, struct.pack("<I", seq), 4)
+                return 6
+            time.sleep(0.0002)
+        C.memmove(seq_addr, struct.pack("<I", seq), 4)
+        parts = np.frombuffer(C.string_at(bufs[rank] + region, 4 * n * n_ranks), np.float32).reshape(n_ranks, n)
+        t = parts[0].copy()
+        for q in range(1, n_ranks):
+            t = (t + parts[q]).astype(np.float32)
+        out = (residual + t).astype(np.float32) if residual is not None else t
+        C.memmove(dst, out.ctypes.data, 4 * n)
+        return 0
+
     def call(self, name, *args):
         st = getattr(self, name)(*args)
         if st:
@@ -143,6 +172,20 @@ def _worker(rank, world, port, n_ex, q):
         ex = RG.ExchangeBuffers(MAX_WORDS, world, rank, exchange)
         bad = []
         for e in range(1, n_ex + 1):
+            if e % 4 == 0:  # the all-reduce of the K-sharded down projection, between the gathers
+                n = 3584
+                part = (np.arange(n, dtype=np.float32) * np.float32(rank + 1) + np.float32(e)).astype(np.float32)
+                res = np.full(n, 0.5, np.float32)
+                out = np.zeros(n, np.float32)
+                st = fake.exchange_reduce(ex.ptrs, world, rank, MAX_WORDS, part.ctypes.data, n, res, out.ctypes.data,
+                                          20000000)
+                want = np.zeros(n, np.float32)
+                for r in range(world):
+                    want = (want + (np.arange(n, dtype=np.float32) * np.float32(r + 1) + np.float32(e))).astype(
+                        np.float32) if r else (np.arange(n, dtype=np.float32) * np.float32(r + 1) + np.float32(e))
+                if st or not np.array_equal(out, (res + want).astype(np.float32)):
+                    bad.append(e)
+                continue
             n_total = (18944, 3584, 4 * world)[e % 3]
             if n_total == 4 * world:
                 off, n_local = 4 * rank, 4

@@ -6,12 +6,13 @@ of both parities, and a rank that never arrives ends the wait with the device
 timeout bit after the 50 ms bound (no hang, the context stays usable).
 
 Two GPUs (spawned processes, one per GPU, gloo only to swap the IPC handles;
-skipped with fewer GPUs): the FFN gate/up, FFN down and LM-head rows sharded
-over the ranks, attention replicated, s / hidden state / greedy records
-exchanged over NVLink peer stores -- every rank produces the same greedy
-tokens as the single-GPU model, with the batched prefill and with the token
-path (whose prefill graph runs the exchanges too).  No test runs two waiting
-launches on one GPU.
+skipped with fewer GPUs): the FFN gate/up rows and the matching K window of
+the FFN down projection sharded over the ranks (the down partials all-reduced
+over NVLink peer stores), the LM-head rows sharded (greedy records exchanged),
+attention replicated -- every rank produces the same greedy tokens as the
+single-GPU model, with the batched prefill and with the token path (whose
+prefill graph runs the exchanges too), for Q6_K and Q4_K down projections.
+No test runs two waiting launches on one GPU.
 """
 import ctypes as C
 import datetime
@@ -164,7 +165,7 @@ def test_exchange_two_ranks(world):
         assert bad == [], "rank %d: exchanges %s assembled a wrong vector" % (rank, bad)
 
 
-def _tp_worker(rank, world, port, prompt, n_new, q):
+def _tp_worker(rank, world, port, prompt, n_new, types, q):
     try:
         import torch
         import torch.distributed as dist
@@ -185,7 +186,7 @@ def _tp_worker(rank, world, port, prompt, n_new, q):
             if st or bits:
                 raise RuntimeError("%s: status %d bits %#x %s" % (what, st, bits, msg))
 
-        m = SyntheticModel(CFG, seed=0x5EED + 40)
+        m = SyntheticModel(CFG, types=types, seed=0x5EED + 40)
         checked("model")
         ex = ExchangeBuffers(m.tp_exchange_words(world), world, rank, exchange)
         m.set_tensor_parallel(ex.ptrs, world, rank, timeout_us=5000000)
@@ -202,7 +203,7 @@ def _tp_worker(rank, world, port, prompt, n_new, q):
         A.lib().arcllm_cuda_device_error(C.c_void_p(torch.cuda.current_stream().cuda_stream), C.byref(bits))
         ref = None
         if rank == 0:  # the single-GPU model on the same GPU
-            m1 = SyntheticModel(CFG, seed=0x5EED + 40)
+            m1 = SyntheticModel(CFG, types=types, seed=0x5EED + 40)
             ref = m1.generate(prompt, n_new)[0]
             m1.close()
         dist.barrier()
@@ -215,15 +216,16 @@ def _tp_worker(rank, world, port, prompt, n_new, q):
         q.put((rank, None, None, -1, repr(e)))
 
 
-@pytest.mark.parametrize("world", [2])
-def test_tp_generate_matches_single_gpu(world):
+@pytest.mark.parametrize("world,down", [(2, "q6k"), (2, "q4k")])
+def test_tp_generate_matches_single_gpu(world, down):
     if torch.cuda.device_count() < world:
         pytest.skip("needs %d GPUs" % world)
+    types = None if down == "q6k" else dict(w_down=A.GGML_Q4_K)
     prompt = [int(t) for t in O.tokens(12, 0x91, CFG["vocab"])]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, prompt, 8, q)) for r in range(world)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, prompt, 8, types, q)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -242,6 +244,6 @@ def test_tp_generate_matches_single_gpu(world):
             toks, launches = out[mode]
             print("rank %d mode %d: tokens %s (1 GPU %s), %d launches per step" % (rank, mode, toks, ref, launches))
             assert toks == ref
-            # 1 embedding + per layer (Q, K, V, attention, O, gate/up, exchange, down, exchange) + LM head,
+            # 1 embedding + per layer (Q, K, V, attention, O, gate/up, down window, all-reduce) + LM head,
             # argmax, exchange, combine + finalize
-            assert launches == 1 + 9 * CFG["n_layers"] + 5
+            assert launches == 1 + 8 * CFG["n_layers"] + 5
