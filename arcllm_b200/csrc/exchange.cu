@@ -8,7 +8,7 @@
 // (the SiLU*up product, 18944 floats at the Qwen2.5-7B shape), the new hidden
 // state h (3584 floats) and the greedy-selection records (4 words per rank).
 //
-// exchange_gather_kernel is one CTA per rank.  It stores this rank's slice of
+// exchange_gather_kernel is one 128-thread CTA per rank.  It stores this rank's slice of
 // the vector (or, in the reduce form, its whole partial vector into slot
 // `rank`) into every rank's exchange buffer (its own with local stores,
 // the others with NVLink peer stores -- stores only, nothing reads another
@@ -56,7 +56,13 @@ struct ExParams {
     const float* residual;
 };
 
-__global__ void __launch_bounds__(1024) exchange_gather_kernel(const ExParams p) {
+// 128 threads of at most 32 registers: 4096 registers, which fit beside one CTA
+// of the matvec kernels (480 threads x <= 128 registers), so the exchange is
+// resident -- launched early by programmatic dependent launch, parked in
+// griddepcontrol.wait -- when the kernel producing its slice ends.
+constexpr uint32_t kExThreads = 128;
+
+__global__ void __launch_bounds__(kExThreads, 16) exchange_gather_kernel(const ExParams p) {
     __shared__ uint32_t s_seq;
     __shared__ int s_ok;
     pdl_trigger();
@@ -157,7 +163,8 @@ int exchange_launch(const ExchangeRanks& ex, const void* src, uint32_t n_local, 
     p.err = dev_error_word();
     p.reduce = reduce ? 1u : 0u;
     p.residual = residual;
-    return launch_checked(launch_kernel(exchange_gather_kernel, dim3(1), dim3(1024), 0, stream, p), "exchange launch");
+    return launch_checked(launch_kernel(exchange_gather_kernel, dim3(1), dim3(kExThreads), 0, stream, p),
+                          "exchange launch");
 }
 }  // namespace
 
