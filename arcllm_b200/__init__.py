@@ -60,6 +60,7 @@ SIGNATURES = {
     "arcllm_cuda_attention_decode_noalloc": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _vp, _vp],
     "arcllm_cuda_embed": [_i32, _vp, _vp, _u32, _u32, _vp, _vp],
     "arcllm_cuda_argmax": [_vp, _u32, _vp, C.POINTER(_u32), C.POINTER(_i32), _vp],
+    "arcllm_cuda_set_launch_overlap": [_i32],
     "arcllm_cuda_set_device": [_i32],
     "arcllm_cuda_device_count": [C.POINTER(C.c_int)],
     "arcllm_cuda_malloc": [_u64, C.POINTER(_vp)],

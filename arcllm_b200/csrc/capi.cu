@@ -455,6 +455,13 @@ int arcllm_cuda_argmax(const float* logits, uint32_t n, void* scratch_dev, uint3
     ARC_GUARD_END
 }
 
+int arcllm_cuda_set_launch_overlap(int on) {
+    ARC_GUARD_BEGIN
+    arc::g_pdl = on != 0;
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_set_device(int device) {
     const cudaError_t e = cudaSetDevice(device);
     return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "set_device");

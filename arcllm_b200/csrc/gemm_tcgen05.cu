@@ -33,7 +33,6 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdlib>
-#include <cstring>
 #include <mutex>
 
 #include "arcllm_cuda_internal.h"
@@ -57,28 +56,19 @@ constexpr uint32_t kMaxStages = 4;
 // X_hi W_lo -- ~22 significant bits of each operand, at three MMAs per K step.
 // Modes 0/1 stage two 128-row boxes of X and one W tile (48 KB, 4 stages);
 // mode 2 four boxes (hi and lo) and two W tiles (96 KB, 2 stages).
-// TW (Q4_K, modes 0/1): the raw 144-byte super-blocks of the CTA's 128 W rows are
-// staged in shared memory by TMA, one super-block column (18 KB) per slot of a
-// two-slot ring, instead of each dequantising thread loading its code bytes
-// from global memory; the X/W stages drop to 3 to make room.
-constexpr uint32_t kWSlot = 128u * 144u;  // 128 rows x one Q4_K super-block
-constexpr uint32_t kWSlots = 2;
-template <int MODE, bool TW = false>
+template <int MODE>
 struct GemmStage {
     static constexpr uint32_t kABoxes = MODE == 2 ? 4u : 2u;
     static constexpr uint32_t kBTiles = MODE == 2 ? 2u : 1u;
-    static constexpr uint32_t kStages = MODE == 2 ? 2u : (TW ? 3u : 4u);
+    static constexpr uint32_t kStages = MODE == 2 ? 2u : 4u;
     static constexpr uint32_t kBOff = kABoxes * kAHalf;
     static constexpr uint32_t kBytes = kBOff + kBTiles * kBTile;
-    static constexpr uint32_t kWRing = TW ? kWSlots * kWSlot : 0u;  // after the stages
 };
 
 struct GemmSmemTail {
     uint64_t full_a[kMaxStages];
     uint64_t full_b[kMaxStages];
     uint64_t empty[kMaxStages];
-    uint64_t full_w[kWSlots];
-    uint64_t empty_w[kWSlots];
     uint64_t done;
     uint32_t tmem_base;
     int abort_flag;
@@ -92,13 +82,11 @@ struct SplitKWs {
     uint32_t ks;
 };
 
-template <int MODE, bool TW = false>
+template <int MODE>
 constexpr uint32_t smem_bytes() {  // + alignment slack
-    return GemmStage<MODE, TW>::kStages * GemmStage<MODE, TW>::kBytes + GemmStage<MODE, TW>::kWRing +
-           (uint32_t)sizeof(GemmSmemTail) + 1024u;
+    return GemmStage<MODE>::kStages * GemmStage<MODE>::kBytes + (uint32_t)sizeof(GemmSmemTail) + 1024u;
 }
-static_assert(smem_bytes<0>() <= 232448u && smem_bytes<2>() <= 232448u && smem_bytes<0, true>() <= 232448u,
-              "GEMM stages exceed 227 KB");
+static_assert(smem_bytes<0>() <= 232448u && smem_bytes<2>() <= 232448u, "GEMM stages exceed 227 KB");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -391,20 +379,18 @@ __device__ __forceinline__ void dequant_q6_quarter_x3(const Raw9& ql, uint32_t s
 // scale and offset of each sub-block, q*f - o and X all round 8x more finely,
 // at the same tensor-core rate); 2: fp16 hi + lo of both operands, three MMAs
 // per K step (xmap_lo: the X_lo tensor).
-template <int FMT, int MODE, bool TW>
+template <int FMT, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kq_bf16_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xmap_lo,
-                        const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ w, uint32_t n_total,
-                        uint32_t k, uint32_t m, const float* __restrict__ residual, float* __restrict__ y,
-                        unsigned int* err, const SplitKWs sk) {
-    static_assert(!TW || (FMT == 12 && MODE != 2), "TMA-staged W: Q4_K, modes 0 and 1");
+                        const uint8_t* __restrict__ w, uint32_t n_total, uint32_t k, uint32_t m,
+                        const float* __restrict__ residual, float* __restrict__ y, unsigned int* err,
+                        const SplitKWs sk) {
     constexpr bool F16 = MODE >= 1;
-    constexpr uint32_t kStages = GemmStage<MODE, TW>::kStages, kStageBytes = GemmStage<MODE, TW>::kBytes;
-    constexpr uint32_t kBOff = GemmStage<MODE, TW>::kBOff;
+    constexpr uint32_t kStages = GemmStage<MODE>::kStages, kStageBytes = GemmStage<MODE>::kBytes;
+    constexpr uint32_t kBOff = GemmStage<MODE>::kBOff;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_align_up<1024>(smem_raw, 0);
-    uint8_t* wring = smem + kStages * kStageBytes;  // TW: the raw super-block slots
-    GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(wring + GemmStage<MODE, TW>::kWRing);
+    GemmSmemTail* tail = reinterpret_cast<GemmSmemTail*>(smem + kStages * kStageBytes);
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t n0 = blockIdx.x * kBN;
     const uint32_t nsb = k / 256u, split = blockIdx.y;
@@ -419,10 +405,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&tail->full_a[s], 1);
             mbar_init(&tail->full_b[s], kDqWarps);
             mbar_init(&tail->empty[s], 1);
-        }
-        for (uint32_t s = 0; s < kWSlots; ++s) {
-            mbar_init(&tail->full_w[s], 1);
-            mbar_init(&tail->empty_w[s], kDqWarps);
         }
         mbar_init(&tail->done, 1);
         tail->abort_flag = 0;
@@ -441,25 +423,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         // ---------------- TMA producer (X) ----------------
-        uint32_t issued = 0, w_issued = 0;
-        const uint32_t nsbl = nkb / 4u;  // super-blocks of this CTA
-        // TW: super-block column j of the CTA's W rows into slot j % 2 (after its previous use ended)
-        auto issue_w = [&](uint32_t j) {
-            const uint32_t slot = j % kWSlots;
-            if (j >= kWSlots && !mbar_wait(&tail->empty_w[slot], ((j / kWSlots) - 1u) & 1u, err)) return false;
-            mbar_arrive_expect_tx(&tail->full_w[slot], kWSlot);
-            tma_load_2d(smem_u32(wring + slot * kWSlot), &wmap, (int)((sb_begin + j) * 144u), (int)n0,
-                        &tail->full_w[slot]);
-            ++w_issued;
-            return true;
-        };
+        uint32_t issued = 0;
         if (lane == 0) {
-            if (TW && nsbl > 0 && !issue_w(0)) *abort_flag = 1;
-            for (uint32_t kb = 0; kb < nkb && !*abort_flag; ++kb) {
-                if (TW && (kb & 3u) == 0u && kb / 4u + 1u < nsbl && !issue_w(kb / 4u + 1u)) {
-                    *abort_flag = 1;
-                    break;
-                }
+            for (uint32_t kb = 0; kb < nkb; ++kb) {
                 const uint32_t s = kb % kStages;
                 if (kb >= kStages && !mbar_wait(&tail->empty[s], ((kb / kStages) - 1u) & 1u, err)) {
                     *abort_flag = 1;
@@ -477,12 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 ++issued;
             }
-            if (*abort_flag) {  // no copy may still be landing at exit
+            if (*abort_flag)  // no copy may still be landing at exit
                 for (uint32_t j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
                     mbar_wait(&tail->full_a[j % kStages], (j / kStages) & 1u, err);
-                for (uint32_t j = w_issued > kWSlots ? w_issued - kWSlots : 0; j < w_issued; ++j)
-                    mbar_wait(&tail->full_w[j % kWSlots], (j / kWSlots) & 1u, err);
-            }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -571,45 +534,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tail->full_b[s]);
               }
-            }
-        } else if (TW) {
-            // Q4_K from the TMA-staged super-block slots: row nrow of slot j % 2 holds the
-            // row's super-block j of this CTA's K range (header, then the 128 code bytes)
-            bool stop = false;
-            for (uint32_t kb0 = 0; kb0 < nkb && !stop; kb0 += 4u) {
-                const uint32_t j = kb0 / 4u, slot = j % kWSlots;
-                bool okw = true;
-                if (lane == 0) okw = mbar_wait(&tail->full_w[slot], (j / kWSlots) & 1u, err);
-                okw = __shfl_sync(0xffffffffu, okw, 0);
-                if (!okw) *abort_flag = 1;
-                if (*abort_flag) break;
-                const uint8_t* srow = wring + slot * kWSlot + nrow * 144u;
-                uint32_t fb[4], ob[4];
-                subblock_consts<F16>(*reinterpret_cast<const uint4*>(srow), hi, fb, ob);
-#pragma unroll
-                for (uint32_t i = 0; i < 4u; ++i) {
-                    const uint32_t kb = kb0 + i;
-                    if (kb >= nkb) break;
-                    const uint4 c0 = *reinterpret_cast<const uint4*>(srow + 16u + 32u * i);
-                    const uint4 c1 = *reinterpret_cast<const uint4*>(srow + 32u + 32u * i);
-                    const uint32_t s = kb % kStages;
-                    bool ok = true;
-                    if (kb >= kStages) {
-                        if (lane == 0) ok = mbar_wait(&tail->empty[s], ((kb / kStages) - 1u) & 1u, err);
-                        ok = __shfl_sync(0xffffffffu, ok, 0);
-                    }
-                    if (!ok) *abort_flag = 1;
-                    if (*abort_flag) {
-                        stop = true;
-                        break;
-                    }
-                    dequant_subblock<F16>(c0, c1, fb[i], ob[i], nrow, hi, smem + s * kStageBytes + kBOff);
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tail->full_b[s]);
-                }
-                __syncwarp();  // every lane has read the slot
-                if (lane == 0) mbar_arrive(&tail->empty_w[slot]);
             }
         } else {
             // the code bytes of stage kb are loaded kPrefetch stages ahead, so
@@ -767,14 +691,12 @@ int gemm_q4k_bf16_prepare() {
     auto attr = [&](auto kern, uint32_t bytes) {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     };
-    attr(gemm_kq_bf16_kernel<12, 0, false>, smem_bytes<0>());
-    attr(gemm_kq_bf16_kernel<14, 0, false>, smem_bytes<0>());
-    attr(gemm_kq_bf16_kernel<12, 1, false>, smem_bytes<1>());
-    attr(gemm_kq_bf16_kernel<14, 1, false>, smem_bytes<1>());
-    attr(gemm_kq_bf16_kernel<12, 2, false>, smem_bytes<2>());
-    attr(gemm_kq_bf16_kernel<14, 2, false>, smem_bytes<2>());
-    attr(gemm_kq_bf16_kernel<12, 0, true>, smem_bytes<0, true>());
-    attr(gemm_kq_bf16_kernel<12, 1, true>, smem_bytes<1, true>());
+    attr(gemm_kq_bf16_kernel<12, 0>, smem_bytes<0>());
+    attr(gemm_kq_bf16_kernel<14, 0>, smem_bytes<0>());
+    attr(gemm_kq_bf16_kernel<12, 1>, smem_bytes<1>());
+    attr(gemm_kq_bf16_kernel<14, 1>, smem_bytes<1>());
+    attr(gemm_kq_bf16_kernel<12, 2>, smem_bytes<2>());
+    attr(gemm_kq_bf16_kernel<14, 2>, smem_bytes<2>());
     if (e != cudaSuccess) return set_cuda_error(e, "gemm prepare");
     done[dev].store(true, std::memory_order_release);
     return ARC_OK;
@@ -809,25 +731,10 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
     if (st != ARC_OK) return st;
     EncodeTiledFn enc = encode_tiled_fn();
     if (!enc) return set_error(ARC_E_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
-    CUtensorMap map, map_lo, wmap;
+    CUtensorMap map, map_lo;
     st = encode_x_map(enc, x, k, m, mode >= 1, &map);
     if (st == ARC_OK) st = encode_x_map(enc, mode == 2 ? x_lo : x, k, m, mode >= 1, &map_lo);
     if (st != ARC_OK) return st;
-    // Q4_K W through TMA-staged super-block slots (ARCLLM_GEMM_TMA_W=0: per-thread global loads)
-    bool tw = fmt == 12 && mode != 2;
-    if (const char* ev = std::getenv("ARCLLM_GEMM_TMA_W"))
-        if (ev[0] == '0') tw = false;
-    std::memset(&wmap, 0, sizeof wmap);
-    if (tw) {
-        const cuuint64_t wdims[2] = {(cuuint64_t)(k / 256u) * 144u, n};
-        const cuuint64_t wstrides[1] = {(cuuint64_t)(k / 256u) * 144u};
-        const cuuint32_t wbox[2] = {144u, 128u};
-        const cuuint32_t westr[2] = {1, 1};
-        const CUresult r = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), wdims, wstrides, wbox,
-                               westr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: tensor map for W rejected");
-    }
     // split K so that about one CTA per SM is busy (whole super-blocks per split)
     int dev = 0;
     cudaGetDevice(&dev);
@@ -849,19 +756,13 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
     const dim3 grid(tiles, ks), block(kThreads);
     unsigned int* err = dev_error_word();
     cudaError_t e;
-#define ARC_GEMM_LAUNCH(F, M, T)                                                                          \
-    launch_kernel(gemm_kq_bf16_kernel<F, M, T>, grid, block, smem_bytes<M, T>(), stream, map, map_lo, wmap, wb, \
-                  n, k, m, residual, y, err, sk)
-    if (fmt == 12 && tw)
-        e = mode == 0 ? ARC_GEMM_LAUNCH(12, 0, true) : ARC_GEMM_LAUNCH(12, 1, true);
-    else if (fmt == 12)
-        e = mode == 0   ? ARC_GEMM_LAUNCH(12, 0, false)
-            : mode == 1 ? ARC_GEMM_LAUNCH(12, 1, false)
-                        : ARC_GEMM_LAUNCH(12, 2, false);
+#define ARC_GEMM_LAUNCH(F, M)                                                                                   \
+    launch_kernel(gemm_kq_bf16_kernel<F, M>, grid, block, smem_bytes<M>(), stream, map, map_lo, wb, n, k, m, \
+                  residual, y, err, sk)
+    if (fmt == 12)
+        e = mode == 0 ? ARC_GEMM_LAUNCH(12, 0) : mode == 1 ? ARC_GEMM_LAUNCH(12, 1) : ARC_GEMM_LAUNCH(12, 2);
     else
-        e = mode == 0   ? ARC_GEMM_LAUNCH(14, 0, false)
-            : mode == 1 ? ARC_GEMM_LAUNCH(14, 1, false)
-                        : ARC_GEMM_LAUNCH(14, 2, false);
+        e = mode == 0 ? ARC_GEMM_LAUNCH(14, 0) : mode == 1 ? ARC_GEMM_LAUNCH(14, 1) : ARC_GEMM_LAUNCH(14, 2);
 #undef ARC_GEMM_LAUNCH
     if (e == cudaSuccess && ks > 1) {
         const uint64_t n4 = (uint64_t)m * n / 4u;

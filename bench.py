@@ -245,6 +245,8 @@ def main(argv=None):
     ap.add_argument("--collective", default="nvlink", choices=["nvlink", "nccl"],
                     help="N>1: logits all-gather fused into the matvec over NVLink peer stores (default) or the "
                          "matvec followed by ncclAllGather")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="graph mode without programmatic dependent launch between the timed launches")
     ap.add_argument("--decode-prompt", type=int, default=256)
     ap.add_argument("--decode-new", type=int, default=128)
     args = ap.parse_args(argv)
@@ -341,6 +343,11 @@ def main(argv=None):
     # still streams all weights from HBM).  The epochs of the N>1 all-gather change per launch, so
     # those run as stream launches.
     graph = None
+    # graph mode: consecutive launches overlap (programmatic dependent launch: a launch streams its weights
+    # while its predecessor drains, then waits for it before reading x or writing the logits)
+    overlap = args.launch == "graph" and not args.no_overlap
+    if overlap:
+        A.check(L.arcllm_cuda_set_launch_overlap(1), "launch overlap")
     if args.launch == "graph" and dist is None:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, capture_error_mode="thread_local"):
@@ -368,6 +375,8 @@ def main(argv=None):
         torch.cuda.synchronize()
         del graphs[0]
         graph = graphs[0]
+    if overlap:
+        A.check(L.arcllm_cuda_set_launch_overlap(0), "launch overlap")
     clk = ClockSampler(gpu_smi_id(torch, local_rank))
     clk.start()
     time.sleep(0.1)
@@ -513,7 +522,9 @@ def main(argv=None):
                                                              "includes the peer stores and the rank handshake"
                                                              if rg is not None else ""),
                 "kernel_ms": round(kern_ms, 5), "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-                "timing": ("mean launch time over one CUDA-graph replay of the %d timed launches" % args.steps
+                "timing": ("mean launch time over one CUDA-graph replay of the %d timed launches%s" %
+                           (args.steps, "" if not overlap else ", consecutive launches overlapping (programmatic "
+                            "dependent launch)")
                            if args.launch == "graph" and (world == 1 or rg is not None) else
                            "CUDA events around each launch on its stream, mean over the timed launches"),
             },

@@ -325,6 +325,14 @@ ARCLLM_CUDA_API int arcllm_cuda_argmax(const float *logits, uint32_t n, void *sc
                                        int *finite_host, void *stream);
 
 /* ---- device memory and streams (for hosts that do not link the CUDA runtime) --- */
+/* Launch overlap for the calling thread (programmatic dependent launch, as the
+ * model's decode graphs use): while on, each kernel this thread launches may be
+ * scheduled while its predecessor on the stream drains, streams its weights
+ * before waiting for it, and waits for it before reading x, gamma, bias or
+ * residual or writing its outputs.  Only for launch sequences whose weights no
+ * preceding launch writes (e.g. back-to-back matvecs over constant weights,
+ * captured in a CUDA graph).  Off by default; ARCLLM_PDL=0 disables it. */
+ARCLLM_CUDA_API int arcllm_cuda_set_launch_overlap(int on);
 ARCLLM_CUDA_API int arcllm_cuda_set_device(int device);
 /* Number of visible CUDA devices (0 when none); fails only on a driver error. */
 ARCLLM_CUDA_API int arcllm_cuda_device_count(int *out);
