@@ -79,15 +79,16 @@ struct RopeEpilogue {
     const uint32_t* pos;
     uint16_t* cache;  // this layer's cache: row p at p * rows
 };
-// Rank all-gather epilogue of the whole-row kernel: y rows also go to peer_y[r] (other ranks'
-// logits, NVLink peer mappings) and the launch ends with the flag handshake of the ranks
-// (peer_flags[r]: rank r's flag array; done_ctr: this rank's CTA counter, zero between launches).
+// Rank all-gather epilogue of the whole-row kernel (fence-free): each row of this rank's shard
+// [row0, row0 + rows) goes to every rank r as one 64-bit word (epoch << 32 | fp32 bits) at
+// ll[r][row0 + i] (ll[r]: rank r's word array of rows_total words, an NVLink peer mapping for
+// r != self_rank); the launch ends once this rank's words all carry `epoch`, their values copied
+// to out[0, rows_total).
 struct RankGather {
-    uint32_t n_ranks, self_rank, epoch;
+    uint32_t n_ranks, self_rank, epoch, row0, rows_total;
     unsigned long long wait_ns;
-    float* peer_y[8];
-    uint32_t* peer_flags[8];
-    uint32_t* done_ctr;
+    unsigned long long* ll[8];
+    float* out;
 };
 int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                        const float* gamma, float eps, const float* bias, const float* residual, float* y,

@@ -159,14 +159,25 @@ int arcllm_cuda_matvec_hostio(int ggml_type, const void* w, uint32_t rows, uint3
 }
 
 // ---- rank all-gather over NVLink peer memory ----
-// Exchange buffer of one rank: fp32 logits [rows_total] at 0, then at a 256-byte boundary
-// the flag array (one u32 slot per rank) and, 64 bytes further, this rank's CTA counter.
-static uint64_t gather_flags_offset(uint32_t rows_total) { return ((uint64_t)rows_total * 4u + 255u) & ~uint64_t(255); }
+// Exchange buffer of one rank: the word array [rows_total] of 64-bit (epoch << 32 | fp32 bits)
+// words at 0, which every rank's launch stores into, then at a 256-byte boundary the fp32
+// logits [rows_total] this rank's own launches collect from it.
+static uint64_t gather_logits_offset(uint32_t rows_total) {
+    return ((uint64_t)rows_total * 8u + 255u) & ~uint64_t(255);
+}
 
 int arcllm_cuda_allgather_buffer_bytes(uint32_t rows_total, uint64_t* out) {
     ARC_GUARD_BEGIN
     if (!out || rows_total == 0) return set_error(ARC_E_INVALID_ARGUMENT, "allgather_buffer_bytes: bad argument");
-    *out = gather_flags_offset(rows_total) + 128u;
+    *out = gather_logits_offset(rows_total) + (((uint64_t)rows_total * 4u + 255u) & ~uint64_t(255));
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_allgather_logits_offset(uint32_t rows_total, uint64_t* out) {
+    ARC_GUARD_BEGIN
+    if (!out || rows_total == 0) return set_error(ARC_E_INVALID_ARGUMENT, "allgather_logits_offset: bad argument");
+    *out = gather_logits_offset(rows_total);
     return ARC_OK;
     ARC_GUARD_END
 }
@@ -183,22 +194,21 @@ int arcllm_cuda_matvec_allgather(int ggml_type, const void* w, uint32_t rows, ui
     if (!arc::matvec_imma_supported(ggml_type, false, rows, k) || (reinterpret_cast<uintptr_t>(x) & 15u))
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec_allgather: needs the whole-row tensor-core kernel "
                                                   "(K/256 <= 14, 16-byte aligned x)");
-    const uint64_t fo = gather_flags_offset(rows_total);
     arc::RankGather g{};
     g.n_ranks = n_ranks;
     g.self_rank = rank;
     g.epoch = epoch;
+    g.row0 = row0;
+    g.rows_total = rows_total;
     g.wait_ns = 1000ull * (timeout_us ? timeout_us : 2000000u);
     for (uint32_t r = 0; r < n_ranks; ++r) {
         if (!rank_bufs[r] || (reinterpret_cast<uintptr_t>(rank_bufs[r]) & 255u))
             return set_error(ARC_E_ALIGNMENT, "matvec_allgather: rank buffers must be 256-byte aligned");
-        uint8_t* b = static_cast<uint8_t*>(rank_bufs[r]);
-        g.peer_y[r] = reinterpret_cast<float*>(b) + row0;
-        g.peer_flags[r] = reinterpret_cast<uint32_t*>(b + fo);
+        g.ll[r] = static_cast<unsigned long long*>(rank_bufs[r]);
     }
-    g.done_ctr = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(rank_bufs[rank]) + fo + 64u);
+    g.out = reinterpret_cast<float*>(static_cast<uint8_t*>(rank_bufs[rank]) + gather_logits_offset(rows_total));
     return arc::matvec_imma_launch(ggml_type, false, w, nullptr, rows, k, x, nullptr, 0.f, nullptr, nullptr,
-                                   g.peer_y[rank], static_cast<cudaStream_t>(stream), nullptr, &g);
+                                   g.out + row0, static_cast<cudaStream_t>(stream), nullptr, &g);
     ARC_GUARD_END
 }
 

@@ -188,4 +188,62 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
+// Relaxed system-scope 64-bit accesses: single-copy atomic, so a word that
+// carries its own epoch tag next to its value needs no fence on either side.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Cross-rank flag handshake, run by all 32 lanes of one warp after the stores
+// it publishes (this CTA's, ordered before it by a CTA barrier, or other CTAs',
+// ordered by a counter they incremented after their own fences):
+//  1. one system-scope fence: the release for every flag below (and the
+//     acquire of a counter read just before);
+//  2. lane q < n stores `seq` into slot `self` of rank q's flag array --
+//     relaxed system-scope stores, so the n NVLink stores are in flight
+//     together instead of each waiting on a fence of its own;
+//  3. lane q polls slot q of this rank's own array (relaxed, system scope)
+//     until it reaches `seq` (wrap-safe: a peer may already be one ahead);
+//  4. one system-scope fence: the acquire, after which the peers' stores
+//     that preceded their flags are visible.
+// flags[q] is rank q's flag array as this process maps it (n <= NMAX <= 32).
+// Gives up after wait_ns, raising ARC_DEV_ERR_TIMEOUT, and returns false.
+template <uint32_t NMAX>
+__device__ __forceinline__ bool rank_flag_handshake(uint32_t* const (&flags)[NMAX], uint32_t n, uint32_t self,
+                                                    uint32_t seq, unsigned long long wait_ns, unsigned int* err) {
+    static_assert(NMAX <= 32, "one lane per rank");
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t* peer = nullptr;
+    const uint32_t* mine = nullptr;
+#pragma unroll
+    for (uint32_t q = 0; q < NMAX; ++q) {  // constant indices: the parameter array stays in param space
+        if (q == lane) peer = flags[q];
+        if (q == self) mine = flags[q];
+    }
+    __threadfence_system();
+    if (lane < n) asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(peer + self), "r"(seq) : "memory");
+    const unsigned long long t0 = globaltimer();
+    bool seen = lane >= n;
+    for (;;) {
+        if (!seen) {
+            uint32_t v;
+            asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + lane) : "memory");
+            seen = (int)(v - seq) >= 0;
+        }
+        if (__all_sync(0xffffffffu, seen)) break;
+        if (__shfl_sync(0xffffffffu, (globaltimer() - t0 > wait_ns) ? 1 : 0, 0)) {
+            if (lane == 0) raise_error(err, ARC_DEV_ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(32);
+    }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    return true;
+}
+
 }  // namespace arc

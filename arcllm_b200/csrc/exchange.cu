@@ -1,36 +1,43 @@
-// Rank exchange over NVLink peer stores: the all-gather steps of the
-// row-sharded decode (tensor-parallel generate()).
+// Rank exchange over NVLink peer stores: the cross-rank steps of the
+// tensor-parallel decode (generate() sharded over the GPUs of one node) and of
+// the row-sharded matvecs.
 //
 // The reference decodes on one device (src/arcllm_v1_runtime.cpp:371-421, one
 // Vulkan queue, src/arcllm_v1_vulkan_runtime_support.h:535).  Sharded over N
-// GPUs, the FFN gate/up rows, the FFN down rows and the LM-head rows are split
-// over the ranks, and three vectors must be reassembled on every rank: s
-// (the SiLU*up product, 18944 floats at the Qwen2.5-7B shape), the new hidden
-// state h (3584 floats) and the greedy-selection records (4 words per rank).
+// GPUs, the FFN gate/up rows and the matching K window of the FFN down
+// projection are split over the ranks, so the down projection's partial sums
+// (3584 floats at the Qwen2.5-7B shape) are all-reduced on every rank (the
+// reduce form), and the LM-head rows are split, so the ranks' greedy-selection
+// records (4 words each) are all-gathered (the gather form, which also
+// re-assembles row-sharded matvec outputs).
 //
-// exchange_gather_kernel is one 128-thread CTA per rank.  It stores this rank's slice of
-// the vector (or, in the reduce form, its whole partial vector into slot
-// `rank`) into every rank's exchange buffer (its own with local stores,
-// the others with NVLink peer stores -- stores only, nothing reads another
-// GPU's memory), fences at system scope, publishes the exchange's sequence
-// number in its slot of every rank's flag array (release) and waits (acquire,
-// bounded by %globaltimer) until every slot of its own array has reached it;
-// then it copies the assembled vector out of its own buffer into `dst` (reduce
-// form: adds the ranks' slots in rank order, plus an optional residual -- the
-// all-reduce of the K-sharded FFN down projection).
+// exchange_kernel runs kExCtas CTAs of 128 threads per rank.  Every 32-bit
+// word of this rank's slice (or, in the reduce form, of its whole partial
+// vector, into slot `rank`) is stored into every rank's exchange buffer as ONE
+// 64-bit word (seq << 32 | value) -- its own buffer with local stores, the
+// others with NVLink peer stores; stores only, nothing reads another GPU's
+// memory.  Then each CTA reads its share of the assembled vector out of its
+// own buffer, waiting (bounded by %globaltimer) until each word carries this
+// exchange's sequence number, and writes the values to `dst` (reduce form: the
+// ranks' slots added in rank order, plus an optional residual -- the
+// all-reduce of the K-sharded FFN down projection).  Every word is its own
+// flag, so no fence and no separate flag handshake is needed.
 //
-// Buffer of one rank (32-bit words; W = the largest vector rounded up to 4):
-//   [0, 2W)        two data regions, picked by the parity of the sequence number
-//   [2W, 2W+8)     flag array: slot r holds the last sequence number rank r published
-//   [2W+8]         this rank's sequence counter (local; advanced by each exchange)
-// Every rank runs the same exchanges in the same order (the decode graph), so
-// the counters agree without host involvement and a graph replays unchanged.
-// Why two regions suffice: a rank can store into a peer's region of sequence
-// e+2 only after that peer published e+1, i.e. after its exchange e (which
-// reads the same region) completed -- the exchanges of one rank are stream
-// ordered.  A wait that runs out sets the device error word's timeout bit and
-// returns without the copy; the ranks' counters may then disagree, so the
-// exchange buffers must be re-created (zeroed) before further use.
+// Buffer of one rank (W = the largest vector's word count rounded up to 4):
+//   [0, 2W) 64-bit words   two data regions, picked by the parity of the sequence number
+//   then kExCtas u32       the per-CTA sequence counters of this rank (local; CTA b
+//                          advances counter b by one per exchange)
+// Every rank runs the same exchanges in the same order (the decode graph) with
+// the same fixed grid, so all counters agree without host involvement and a
+// graph replays unchanged.  Why two regions suffice: a rank can store into a
+// peer's region of sequence e+2 only after its own exchange e+1 completed,
+// which needed that peer's e+1 words, which the peer stores only after its
+// exchange e (which reads the same region) completed -- the exchanges of one
+// rank are stream ordered.  A word of an older exchange in the same region
+// carries an older sequence number and is never taken for a newer one.  A
+// wait that runs out sets the device error word's timeout bit and returns;
+// the ranks may then disagree, so the exchange buffers must be re-created
+// (zeroed) before further use.
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
 #include "decode_ops.h"
@@ -38,15 +45,14 @@
 namespace arc {
 namespace {
 
-constexpr uint32_t kFlagWords = 8;
 constexpr uint32_t kMaxExRanks = 8;
+constexpr uint32_t kExCtas = 16;
 
 struct ExParams {
-    uint32_t* data[kMaxExRanks];   // rank q's buffer base (its data regions), as this process maps it
-    uint32_t* flags[kMaxExRanks];  // rank q's flag array
-    uint32_t* seq;                 // this rank's counter
-    const uint32_t* src;           // this rank's slice
-    uint32_t* dst;                 // the assembled vector (n_total words)
+    unsigned long long* data[kMaxExRanks];  // rank q's word regions, as this process maps them
+    uint32_t* seq;                          // this rank's per-CTA counters [kExCtas]
+    const uint32_t* src;                    // this rank's slice
+    uint32_t* dst;                          // the assembled vector (n_total words)
     uint32_t W, n_local, off, n_total, n_ranks, rank;
     unsigned long long wait_ns;
     unsigned int* err;
@@ -57,85 +63,90 @@ struct ExParams {
 };
 
 // 128 threads of at most 32 registers: 4096 registers, which fit beside one CTA
-// of the matvec kernels (480 threads x <= 128 registers), so the exchange is
-// resident -- launched early by programmatic dependent launch, parked in
-// griddepcontrol.wait -- when the kernel producing its slice ends.
+// of the matvec kernels (480 threads x <= 128 registers), so the exchange CTAs
+// are resident -- launched early by programmatic dependent launch, parked in
+// griddepcontrol.wait -- when the kernel producing the slice ends.
 constexpr uint32_t kExThreads = 128;
 
-__global__ void __launch_bounds__(kExThreads, 16) exchange_gather_kernel(const ExParams p) {
+// Wait until word i of the own region carries `tag` (bounded); false on timeout.
+__device__ __forceinline__ bool await_word(const unsigned long long* own, uint32_t i, uint32_t tag,
+                                           unsigned long long& v, unsigned long long t0, const ExParams& p) {
+    while ((uint32_t)(v >> 32) != tag) {
+        if (globaltimer() - t0 > p.wait_ns) {
+            raise_error(p.err, ARC_DEV_ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(32);
+        v = ld_relaxed_sys_u64(own + i);
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(kExThreads, 16) exchange_kernel(const ExParams p) {
     __shared__ uint32_t s_seq;
-    __shared__ int s_ok;
     pdl_trigger();
     pdl_wait();  // the slice comes from the preceding kernel
-    const uint32_t tid = threadIdx.x, nt = blockDim.x;
-    if (tid == 0) s_seq = *reinterpret_cast<volatile uint32_t*>(p.seq) + 1u;
+    const uint32_t tid = threadIdx.x, nthr = gridDim.x * blockDim.x, gtid = blockIdx.x * blockDim.x + tid;
+    if (tid == 0) {  // counter b is read and advanced only by CTA b of each exchange, in stream order
+        s_seq = *reinterpret_cast<volatile uint32_t*>(p.seq + blockIdx.x) + 1u;
+        p.seq[blockIdx.x] = s_seq;
+    }
     __syncthreads();
     const uint32_t seq = s_seq, region = (seq & 1u) * p.W;
-    const bool vec = ((p.off | p.n_local) & 3u) == 0u && (reinterpret_cast<uintptr_t>(p.src) & 15u) == 0u;
-    for (uint32_t q = 0; q < p.n_ranks; ++q) {
-        uint32_t* d = p.data[q] + region + p.off;
-        if (vec) {
-            const uint4* s4 = reinterpret_cast<const uint4*>(p.src);
-            uint4* d4 = reinterpret_cast<uint4*>(d);
-            for (uint32_t i = tid; i < p.n_local / 4u; i += nt) d4[i] = s4[i];
-        } else {
-            for (uint32_t i = tid; i < p.n_local; i += nt) d[i] = p.src[i];
-        }
+    const unsigned long long tag = (unsigned long long)seq << 32;
+    for (uint32_t i = gtid; i < p.n_local; i += nthr) {
+        const unsigned long long w = tag | p.src[i];
+#pragma unroll
+        for (uint32_t q = 0; q < kMaxExRanks; ++q)
+            if (q < p.n_ranks) st_relaxed_sys_u64(p.data[q] + region + p.off + i, w);
     }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence_system();  // this CTA's (peer) stores before the flags
-        for (uint32_t q = 0; q < p.n_ranks; ++q)
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flags[q] + p.rank), "r"(seq) : "memory");
-        const uint32_t* mine = p.flags[p.rank];
-        const unsigned long long t0 = globaltimer();
-        int ok = 1;
-        for (uint32_t q = 0; q < p.n_ranks && ok; ++q) {
-            for (;;) {
-                uint32_t v;
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + q) : "memory");
-                if ((int)(v - seq) >= 0) break;
-                if (globaltimer() - t0 > p.wait_ns) {
-                    raise_error(p.err, ARC_DEV_ERR_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(32);
-            }
-        }
-        *p.seq = seq;
-        s_ok = ok;
-    }
-    __syncthreads();
-    if (!s_ok) return;
-    // the peers' stores landed in this GPU's memory; read them from L2, not a stale L1 line
-    const uint32_t* own = p.data[p.rank] + region;
+    const unsigned long long* own = p.data[0];
+#pragma unroll
+    for (uint32_t q = 1; q < kMaxExRanks; ++q)
+        if (q == p.rank) own = p.data[q];
+    own += region;
+    const unsigned long long t0 = globaltimer();
     if (p.reduce) {  // the same sum, in the same order, on every rank
-        const float* slots = reinterpret_cast<const float*>(own);
         float* out = reinterpret_cast<float*>(p.dst);
-        for (uint32_t i = tid; i < p.n_total; i += nt) {
-            float t = __ldcg(slots + i);
-            for (uint32_t q = 1; q < p.n_ranks; ++q) t += __ldcg(slots + (uint64_t)q * p.n_total + i);
+        for (uint32_t i = gtid; i < p.n_total; i += nthr) {
+            unsigned long long v[kMaxExRanks];
+#pragma unroll
+            for (uint32_t q = 0; q < kMaxExRanks; ++q)  // every slot's word in flight before the first wait
+                if (q < p.n_ranks) v[q] = ld_relaxed_sys_u64(own + (uint64_t)q * p.n_total + i);
+            float t = 0.f;
+#pragma unroll
+            for (uint32_t q = 0; q < kMaxExRanks; ++q) {
+                if (q >= p.n_ranks) break;
+                if (!await_word(own, q * p.n_total + i, seq, v[q], t0, p)) return;
+                const float f = __uint_as_float((uint32_t)v[q]);
+                t = q ? t + f : f;
+            }
             out[i] = p.residual ? p.residual[i] + t : t;
         }
         return;
     }
-    if ((p.n_total & 3u) == 0u && (reinterpret_cast<uintptr_t>(p.dst) & 15u) == 0u) {
-        const uint4* s4 = reinterpret_cast<const uint4*>(own);
-        uint4* d4 = reinterpret_cast<uint4*>(p.dst);
-        for (uint32_t i = tid; i < p.n_total / 4u; i += nt) d4[i] = __ldcg(s4 + i);
-    } else {
-        for (uint32_t i = tid; i < p.n_total; i += nt) p.dst[i] = __ldcg(own + i);
+    for (uint32_t base = gtid; base < p.n_total; base += 4u * nthr) {
+        unsigned long long v[4];
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j)
+            if (base + j * nthr < p.n_total) v[j] = ld_relaxed_sys_u64(own + base + j * nthr);
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t i = base + j * nthr;
+            if (i >= p.n_total) break;
+            if (!await_word(own, i, seq, v[j], t0, p)) return;
+            p.dst[i] = (uint32_t)v[j];
+        }
     }
 }
 
-// Data regions are whole 16-byte units, so every region starts 16-byte aligned.
+// Data regions are whole 32-byte units.
 inline uint32_t region_words(uint32_t max_words) { return (max_words + 3u) & ~3u; }
 
 }  // namespace
 
 uint64_t exchange_buffer_bytes(uint32_t max_words) {
-    return ((uint64_t)(2u * region_words(max_words) + kFlagWords + 8u) * 4u + 255u) / 256u * 256u;
+    return ((uint64_t)2u * region_words(max_words) * 8u + kExCtas * 4u + 255u) / 256u * 256u;
 }
 
 namespace {
@@ -147,10 +158,9 @@ int exchange_launch(const ExchangeRanks& ex, const void* src, uint32_t n_local, 
     for (uint32_t q = 0; q < ex.n_ranks; ++q) {
         if (!ex.bufs[q] || (reinterpret_cast<uintptr_t>(ex.bufs[q]) & 255u))
             return set_error(ARC_E_ALIGNMENT, "exchange: rank buffers must be non-null and 256-byte aligned");
-        p.data[q] = static_cast<uint32_t*>(ex.bufs[q]);
-        p.flags[q] = p.data[q] + 2u * region_words(ex.max_words);
+        p.data[q] = static_cast<unsigned long long*>(ex.bufs[q]);
     }
-    p.seq = p.flags[ex.rank] + kFlagWords;
+    p.seq = reinterpret_cast<uint32_t*>(p.data[ex.rank] + 2u * region_words(ex.max_words));
     p.src = static_cast<const uint32_t*>(src);
     p.dst = static_cast<uint32_t*>(dst);
     p.W = region_words(ex.max_words);
@@ -163,7 +173,7 @@ int exchange_launch(const ExchangeRanks& ex, const void* src, uint32_t n_local, 
     p.err = dev_error_word();
     p.reduce = reduce ? 1u : 0u;
     p.residual = residual;
-    return launch_checked(launch_kernel(exchange_gather_kernel, dim3(1), dim3(kExThreads), 0, stream, p),
+    return launch_checked(launch_kernel(exchange_kernel, dim3(kExCtas), dim3(kExThreads), 0, stream, p),
                           "exchange launch");
 }
 }  // namespace

@@ -41,15 +41,16 @@ struct MvParams {
     uint16_t* cache;                // cache base + layer offset; row `pos` starts at pos * rows
     uint32_t max_ctx;
     // rank all-gather epilogue (whole-row integer-MMA kernel, not dual, rope_mode 0; n_ranks 0 =
-    // none): row i of this shard is also stored at peer_y[r][i] for every rank r != self_rank
-    // (NVLink peer stores into the other ranks' logits); then the CTAs count themselves on
-    // done_ctr and the last one writes `epoch` into slot self_rank of every rank's flag array
-    // and waits, at most wait_ns, until every slot of its own array has reached `epoch`
+    // none), fence-free: row i of this shard goes to every rank q as ONE 64-bit word
+    // (epoch << 32 | fp32 bits) at gather_ll[q][gather_row0 + i] (NVLink peer stores for q !=
+    // self_rank); then every CTA reads its slice of this rank's word array until each word carries
+    // `epoch` (at most wait_ns) and writes the values to gather_out[0, gather_rows_total)
     uint32_t n_ranks, self_rank, epoch;
     unsigned long long wait_ns;
-    float* peer_y[kMaxRanks];
-    uint32_t* peer_flags[kMaxRanks];
-    uint32_t* done_ctr;
+    unsigned long long* gather_ll[kMaxRanks];
+    const unsigned long long* gather_own;  // gather_ll[self_rank]
+    float* gather_out;
+    uint32_t gather_row0, gather_rows_total;
     // K-slice kernel only: the first super-block of the K window this launch covers
     // (the matrix rows keep their full length rb; nb counts the window's blocks)
     uint32_t kb_base;

@@ -119,9 +119,12 @@ __device__ __forceinline__ void finish_rows(const MvParams& p, const float* red,
             if (p.bias) a += p.bias[row];
             if (p.residual) a = p.residual[row] + a;
             p.y[row] = a;
+            if (p.n_ranks) {  // all-gather: the row, tagged with the epoch, into every rank's word array
+                const unsigned long long word = ((unsigned long long)p.epoch << 32) | __float_as_uint(a);
 #pragma unroll
-            for (uint32_t q = 0; q < kMaxRanks; ++q)  // all-gather: the same row into every other rank
-                if (q < p.n_ranks && q != p.self_rank) p.peer_y[q][row] = a;
+                for (uint32_t q = 0; q < kMaxRanks; ++q)
+                    if (q < p.n_ranks) st_relaxed_sys_u64(p.gather_ll[q] + p.gather_row0 + row, word);
+            }
         }
     }
     if (!DUAL && p.rope_mode != 0) {
@@ -159,40 +162,36 @@ __device__ __forceinline__ void finish_rows(const MvParams& p, const float* red,
 // r+1 never touches the buffer of round r being summed here.  All waits are
 // bounded; on a timeout it sets *abort_flag, stops, and waits (bounded) for
 // the copies it already issued.
-// End of the rank all-gather epilogue, run by each CTA's producer warp after
-// its last rows are stored.  Every lane fences its own (local and peer) stores
-// at system scope, lane 0 counts the CTA on done_ctr, and the CTA that
-// completes the count publishes `epoch` into this rank's slot of every rank's
-// flag array (release) and waits until every slot of its own array has
-// reached `epoch` (acquire; wrap-safe, a peer may already be one launch ahead).
-// The wait gives up after p.wait_ns with ARC_DEV_ERR_TIMEOUT.
-__device__ __forceinline__ void rank_gather_sync(const MvParams& p, uint32_t lane) {
-    __threadfence_system();
-    __syncwarp();
-    if (lane != 0) return;
-    if (atomicAdd(p.done_ctr, 1u) != gridDim.x - 1u) return;
-    __threadfence_system();  // the other CTAs' stores are ordered before their counts
-    *p.done_ctr = 0u;        // re-armed for the next launch in stream order
-#pragma unroll
-    for (uint32_t q = 0; q < kMaxRanks; ++q)
-        if (q < p.n_ranks)
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[q] + p.self_rank), "r"(p.epoch)
-                         : "memory");
-    const uint32_t* mine = p.peer_flags[0];
-#pragma unroll
-    for (uint32_t q = 1; q < kMaxRanks; ++q)
-        if (q == p.self_rank) mine = p.peer_flags[q];
+// End of the rank all-gather, run by every thread of each CTA once the CTA's
+// own rows are stored: CTA b takes an equal slice [i0, i1) of the whole
+// result, reads this rank's words of the slice (up to four per thread in
+// flight) until each carries this launch's epoch and writes the values to
+// gather_out.  The words come from every rank's CTAs, so the launch ends once
+// the last row of the slowest rank has landed -- no fence, counter or flag:
+// each 64-bit word is its own flag.  Gives up after p.wait_ns with
+// ARC_DEV_ERR_TIMEOUT.
+__device__ __forceinline__ void gather_collect(const MvParams& p) {
+    const uint32_t n = p.gather_rows_total, per = (n + gridDim.x - 1u) / gridDim.x;
+    const uint32_t i0 = blockIdx.x * per, i1 = min(n, i0 + per), nt = blockDim.x;
     const unsigned long long t0 = globaltimer();
-    for (uint32_t q = 0; q < p.n_ranks; ++q) {
-        for (;;) {
-            uint32_t v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + q) : "memory");
-            if ((int)(v - p.epoch) >= 0) break;
-            if (globaltimer() - t0 > p.wait_ns) {
-                raise_error(p.err, ARC_DEV_ERR_TIMEOUT);
-                return;
+    for (uint32_t base = i0 + threadIdx.x; base < i1; base += 4u * nt) {
+        unsigned long long v[4];
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j)
+            if (base + j * nt < i1) v[j] = ld_relaxed_sys_u64(p.gather_own + base + j * nt);
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t i = base + j * nt;
+            if (i >= i1) break;
+            while ((uint32_t)(v[j] >> 32) != p.epoch) {
+                if (globaltimer() - t0 > p.wait_ns) {
+                    raise_error(p.err, ARC_DEV_ERR_TIMEOUT);
+                    return;
+                }
+                __nanosleep(32);
+                v[j] = ld_relaxed_sys_u64(p.gather_own + i);
             }
-            __nanosleep(64);
+            p.gather_out[i] = __uint_as_float((uint32_t)v[j]);
         }
     }
 }
@@ -260,44 +259,17 @@ __device__ __forceinline__ void produce_and_finish(const MvParams& p, uint8_t* s
         const uint32_t first = it > S ? it - S : 0;
         for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1u, p.err);
     }
-    // an aborted CTA still counts itself, so the counter re-arms (the error word reports the abort)
-    if (!DUAL && p.n_ranks) rank_gather_sync(p, lane);
 }
 
+// The consumer warps of matvec_imma_kernel.
 template <int FMT, int MT, bool DUAL>
-__global__ void __launch_bounds__(15 * 32, 1) matvec_imma_kernel(const MvParams p, uint32_t nwc) {
+__device__ __forceinline__ void consume(const MvParams& p, const uint8_t* stages, uint64_t* full, uint64_t* empty,
+                                        volatile int* abort_flag, float* red, double* red_d, uint8_t* xscr,
+                                        uint32_t nwc, uint32_t warp, uint32_t lane) {
     constexpr int G = 16 * MT;
     constexpr int NV = DUAL ? 2 * G : G;
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kMaxStages;
-    int* cnt = reinterpret_cast<int*>(empty + kMaxStages);
-    volatile int* abort_flag = cnt + kMaxStages;
-    double* red_d = reinterpret_cast<double*>(smem + kRedD);  // [32]
-    float* red = reinterpret_cast<float*>(red_d + 32);        // [2][stages][nwc][NV]
-    uint8_t* xscr = smem + imma_xscr_off(p.stages, nwc, NV);
-    uint8_t* stages = smem_align_up<128>(smem, imma_stage_off(p.stages, nwc, NV));
-
-    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
-    const uint32_t NT = nwc * 32u;
     const uint32_t S = p.stages;
     const uint32_t mat_off = p.G * p.rb;
-    pdl_trigger();
-
-    if (tid == NT) {
-        for (uint32_t s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], nwc);
-            cnt[s] = 0;
-        }
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
-    if (warp == nwc) {
-        produce_and_finish<G, DUAL>(p, stages, full, empty, abort_flag, mat_off, red, nwc, lane);
-        return;
-    }
 
     // Q4_K: warp w owns super-block w.  Q6_K: half 0 of block w and half 1 of
     // block w^1 (K has an even number of blocks), see q6_tile.
@@ -353,6 +325,49 @@ __global__ void __launch_bounds__(15 * 32, 1) matvec_imma_kernel(const MvParams 
         if (lane == 0) {
             __threadfence_block();
             mbar_arrive(&empty[s]);  // releases the stage and publishes this warp's partials
+        }
+    }
+}
+
+template <int FMT, int MT, bool DUAL>
+__global__ void __launch_bounds__(15 * 32, 1) matvec_imma_kernel(const MvParams p, uint32_t nwc) {
+    constexpr int G = 16 * MT;
+    constexpr int NV = DUAL ? 2 * G : G;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxStages;
+    int* cnt = reinterpret_cast<int*>(empty + kMaxStages);
+    volatile int* abort_flag = cnt + kMaxStages;
+    double* red_d = reinterpret_cast<double*>(smem + kRedD);  // [32]
+    float* red = reinterpret_cast<float*>(red_d + 32);        // [2][stages][nwc][NV]
+    uint8_t* xscr = smem + imma_xscr_off(p.stages, nwc, NV);
+    uint8_t* stages = smem_align_up<128>(smem, imma_stage_off(p.stages, nwc, NV));
+
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const uint32_t NT = nwc * 32u;
+    const uint32_t S = p.stages;
+    const uint32_t mat_off = p.G * p.rb;
+    pdl_trigger();
+
+    if (tid == NT) {
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], nwc);
+            cnt[s] = 0;
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == nwc) {
+        produce_and_finish<G, DUAL>(p, stages, full, empty, abort_flag, mat_off, red, nwc, lane);
+    } else {
+        consume<FMT, MT, DUAL>(p, stages, full, empty, abort_flag, red, red_d, xscr, nwc, warp, lane);
+    }
+    if constexpr (!DUAL) {
+        if (p.n_ranks) {
+            __syncthreads();  // the producer has stored this CTA's rows
+            if (!*abort_flag) gather_collect(p);
         }
     }
 }
@@ -476,19 +491,21 @@ int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint3
     }
     if (gather && gather->n_ranks != 0) {
         if (dual || (rope && rope->mode != 0) || gather->n_ranks > kMaxRanks || gather->self_rank >= gather->n_ranks ||
-            !gather->done_ctr)
+            !gather->out || gather->epoch == 0 || (uint64_t)gather->row0 + rows > gather->rows_total)
             return set_error(ARC_E_INVALID_ARGUMENT, "matvec_imma: bad rank all-gather epilogue");
         p.n_ranks = gather->n_ranks;
         p.self_rank = gather->self_rank;
         p.epoch = gather->epoch;
         p.wait_ns = gather->wait_ns;
         for (uint32_t r = 0; r < gather->n_ranks; ++r) {
-            if (!gather->peer_y[r] || !gather->peer_flags[r])
-                return set_error(ARC_E_INVALID_ARGUMENT, "matvec_imma: null rank buffer");
-            p.peer_y[r] = gather->peer_y[r];
-            p.peer_flags[r] = gather->peer_flags[r];
+            if (!gather->ll[r] || (reinterpret_cast<uintptr_t>(gather->ll[r]) & 7u))
+                return set_error(ARC_E_INVALID_ARGUMENT, "matvec_imma: null or unaligned rank word array");
+            p.gather_ll[r] = gather->ll[r];
         }
-        p.done_ctr = gather->done_ctr;
+        p.gather_own = gather->ll[gather->self_rank];
+        p.gather_out = gather->out;
+        p.gather_row0 = gather->row0;
+        p.gather_rows_total = gather->rows_total;
     }
     static int sm_count[64] = {};  // per device, queried once
     int dev = 0;

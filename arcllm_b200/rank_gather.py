@@ -2,11 +2,12 @@
 (RankGather) and for the vector exchange of the tensor-parallel decode
 (ExchangeBuffers).
 
-One process per GPU.  Each rank allocates one exchange buffer (fp32 logits of
-all rows, then the per-rank flag array and its CTA counter), shares a CUDA IPC
-handle of it with the other ranks and opens theirs, so that
-``arcllm_cuda_matvec_allgather`` can store each rank's rows into every rank's
-buffer with NVLink peer stores and end with a flag handshake.  The handle
+One process per GPU.  Each rank allocates two exchange buffers (one per epoch
+parity: the 64-bit epoch-tagged words of all rows, then the fp32 logits it
+collects from them), shares CUDA IPC handles of them with the other ranks and
+opens theirs, so that ``arcllm_cuda_matvec_allgather`` can store each rank's
+rows into every rank's buffer with NVLink peer stores; each word carries its
+own epoch, so the ranks need no separate flag handshake.  The handle
 exchange itself is a host collective supplied by the caller
 (``torch.distributed.all_gather_object`` in bench.py, a multiprocessing pipe in
 the tests): the data path has no host collective and no NCCL call.
@@ -33,7 +34,7 @@ class RankGather:
     next launch stores into the other buffer, and it cannot get two launches
     ahead, because its launch completes only after this rank's next launch --
     stream-ordered after this rank's reads of the current logits -- has
-    published its flag.
+    stored its rows.
     """
 
     def __init__(self, rows_total, n_ranks, rank, exchange, timeout_us=2000000):
@@ -72,6 +73,9 @@ class RankGather:
                 self._opened.append(p)
                 ptrs.append(p.value)
             self._bufs.append((C.c_void_p * n_ranks)(*ptrs))
+        off = C.c_uint64(0)
+        call("arcllm_cuda_allgather_logits_offset", rows_total, C.byref(off))
+        self._logits_off = off.value
         self.epoch = 0
         self._L = L
 
@@ -79,7 +83,7 @@ class RankGather:
     def logits_ptr(self):
         """Device address of this rank's copy of all rows_total results of the
         last launch."""
-        return self._own[self.epoch & 1].value
+        return self._own[self.epoch & 1].value + self._logits_off
 
     def step(self, w, rows, k, x, row0, stream, ggml_type=GGML_Q6_K):
         """One all-gather matvec of this rank's rows [row0, row0 + rows)."""

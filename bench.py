@@ -342,7 +342,7 @@ def main(argv=None):
     # N=1: the K timed launches as one CUDA graph (no host launch gaps between passes; every pass
     # still streams all weights from HBM).  The epochs of the N>1 all-gather change per launch, so
     # those run as stream launches.
-    graph = None
+    graph = rendezvous = None
     # graph mode: consecutive launches overlap (programmatic dependent launch: a launch streams its weights
     # while its predecessor drains, then waits for it before reading x or writing the logits)
     overlap = args.launch == "graph" and not args.no_overlap
@@ -362,19 +362,23 @@ def main(argv=None):
         # captured with epochs e+K+1 .. e+2K after an untimed graph of epochs e+1 .. e+K, and each graph is
         # replayed exactly once (every rank captures the same sequence).  Host launch gaps, which the flag
         # handshake would otherwise turn into waits of the other ranks, stay out of the timed region.
+        # Between the two sits a one-launch graph replayed untimed right before the timed one: it ends on
+        # every rank within a flag round trip of the others, so the ranks start their timed launches
+        # together instead of at the host skew of the barrier (which the first timed launch would absorb).
         graphs = []
-        for _ in range(2):
+        for n_launch in (args.steps, 1, args.steps):
             g_ = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g_, capture_error_mode="thread_local"):
                 cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-                for _ in range(args.steps):
+                for _ in range(n_launch):
                     rg.step(wp, rows_per, K, xp, r0, cs, TY)
             graphs.append(g_)
         barrier()
         graphs[0].replay()
         torch.cuda.synchronize()
-        del graphs[0]
-        graph = graphs[0]
+        rendezvous = graphs[1]
+        graph = graphs[2]
+        del graphs
     if overlap:
         A.check(L.arcllm_cuda_set_launch_overlap(0), "launch overlap")
     clk = ClockSampler(gpu_smi_id(torch, local_rank))
@@ -384,6 +388,11 @@ def main(argv=None):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(0 if graph is not None else args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if rendezvous is not None:
+        rendezvous.replay()
+        # ~0.5 ms of spinning after the rendezvous, the same on every rank: the host has the timed graph
+        # queued before any rank starts it
+        torch.cuda._sleep(1 << 20)
     t_start.record()
     if graph is not None:
         graph.replay()
@@ -404,7 +413,7 @@ def main(argv=None):
     total_ms = t_start.elapsed_time(t_end)
     # per-launch events in stream mode; in graph mode the mean over the back-to-back replay
     kern_ms = (sum(a.elapsed_time(b) for a, b in ev) if ev else total_ms) / args.steps
-    del graph
+    del graph, rendezvous
     bits = C.c_uint32(0)
     A.check(L.arcllm_cuda_device_error(sp, C.byref(bits)), "device_error")
     if dist is not None:
@@ -595,22 +604,35 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
     ex = ExchangeBuffers(FFN, world, rank, exchange)
     barrier()
 
-    def step1b(i):
+    def step1b(i, stream):
         A.check(L.arcllm_cuda_matvec(A.GGML_Q6_K, C.c_void_p(ws[i % ncop].data_ptr()), hr, FFN,
                                      C.c_void_p(x18.data_ptr()), None, C.c_float(0), None, None,
-                                     C.c_void_p(part.data_ptr() + 4 * h0), sp), "matvec")
-        ex.gather(C.c_void_p(part.data_ptr() + 4 * h0), hr, h0, C.c_void_p(full.data_ptr()), HIDDEN, sp)
+                                     C.c_void_p(part.data_ptr() + 4 * h0), stream), "matvec")
+        ex.gather(C.c_void_p(part.data_ptr() + 4 * h0), hr, h0, C.c_void_p(full.data_ptr()), HIDDEN, stream)
 
     for i in range(10):
-        step1b(i)
+        step1b(i, sp)
     barrier()
+    # the timed steps as one CUDA graph (matvec + exchange per step, consecutive launches overlapping);
+    # the exchange's sequence numbers live on the device, so the graph replays unchanged
     n_it = 200
+    A.check(L.arcllm_cuda_set_launch_overlap(1), "launch overlap")
+    g1 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g1, capture_error_mode="thread_local"):
+        cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for i in range(n_it):
+            step1b(i, cs)
+    A.check(L.arcllm_cuda_set_launch_overlap(0), "launch overlap")
+    g1.replay()  # upload: an untimed pass
+    barrier()
+    step1b(0, sp)  # rendezvous: its exchange ends on every rank within a flag round trip of the others
+    torch.cuda._sleep(1 << 20)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for i in range(n_it):
-        step1b(i)
+    g1.replay()
     b.record()
     barrier()
+    del g1
     ms = max_over_ranks(a.elapsed_time(b) / n_it)
     # check: the last step used copy (n_it - 1) % ncop; the full matrix of that seed on one GPU
     wf = torch.empty(HIDDEN * rb + 16, dtype=torch.uint8, device=dev)
@@ -618,15 +640,26 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
     yf = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
     A.check(L.arcllm_cuda_matvec(A.GGML_Q6_K, C.c_void_p(wf.data_ptr()), HIDDEN, FFN, C.c_void_p(x18.data_ptr()), None,
                                  C.c_float(0), None, None, C.c_void_p(yf.data_ptr()), sp), "matvec")
+    # and every rank's shard rows computed alone on this GPU (the split-K grouping depends on the row
+    # count, so only the same rows are expected to agree bit for bit)
+    ys = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
+    for q in range(world):
+        q0, qr = C.c_uint32(0), C.c_uint32(0)
+        A.call("arcllm_cuda_shard_rows", HIDDEN, 32, world, q, C.byref(q0), C.byref(qr))
+        A.check(L.arcllm_cuda_matvec(A.GGML_Q6_K, C.c_void_p(wf.data_ptr() + q0.value * rb), qr.value, FFN,
+                                     C.c_void_p(x18.data_ptr()), None, C.c_float(0), None, None,
+                                     C.c_void_p(ys.data_ptr() + 4 * q0.value), sp), "matvec")
     torch.cuda.synchronize()
     diff = float((full.double() - yf.double()).norm() / yf.double().norm())
+    same_rows = int(torch.equal(full.view(torch.int32), ys.view(torch.int32)))
     alg = matvec_alg_bytes("q6k", HIDDEN, FFN)
     out["config1b_q6k_3584x18944_rowshard"] = {
         "GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_step": round(ms * 1e3, 2),
         "rows_per_rank": hr, "collective": "exchange kernel (NVLink peer stores + flags)",
+        "timing": "one CUDA graph of %d steps (matvec + exchange each), after a device rendezvous" % n_it,
         "rel_l2_vs_1gpu": float("%.3g" % max_over_ranks(diff)),
-        "bit_exact_vs_1gpu": bool(max_over_ranks(diff) == 0.0)}
-    del ws, wf
+        "bit_exact_vs_1gpu_same_rows": bool(max_over_ranks(-same_rows) == -1)}
+    del ws, wf, ys
     torch.cuda.synchronize()
     barrier()
     ex.close()
@@ -647,20 +680,16 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
     A.call("arcllm_cuda_fill_normal_f32", C.c_void_p(xf.data_ptr()), 0, m * HIDDEN, 0x1C7A, C.c_float(0),
            C.c_float(1), sp)
     xb = xf.to(torch.bfloat16)
-    y = torch.empty(m * fr, dtype=torch.float32, device=dev)
     sizes = [None] * world
     dist.all_gather_object(sizes, fr)
-    equal = len(set(sizes)) == 1
-    yall = torch.empty(world * m * fr, dtype=torch.float32, device=dev) if equal else None
+    fmax = max(sizes)  # shards of unequal size travel padded to the largest, one all-gather of equal parts
+    y = torch.empty(m * fmax, dtype=torch.float32, device=dev)
+    yall = torch.empty(world * m * fmax, dtype=torch.float32, device=dev)
 
     def step4(i):
         A.check(L.arcllm_cuda_gemm_q4k_bf16(C.c_void_p(ws[i % ncop].data_ptr()), fr, HIDDEN,
                                             C.c_void_p(xb.data_ptr()), m, C.c_void_p(y.data_ptr()), sp), "gemm")
-        if equal:
-            dist.all_gather_into_tensor(yall, y)
-        else:
-            ys = [torch.empty(m * s_, dtype=torch.float32, device=dev) for s_ in sizes]
-            dist.all_gather(ys, y)
+        dist.all_gather_into_tensor(yall, y)
 
     for i in range(5):
         step4(i)
@@ -676,7 +705,8 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
     tf = 2.0 * m * FFN * HIDDEN / (ms * 1e-3) / 1e12
     out["config4_prefill_gate_256x18944x3584_rowshard"] = {
         "TFLOP/s": round(tf, 1), "frac_of_bf16_peak_per_gpu": round(tf / world / tflops_peak, 4) if tflops_peak else None,
-        "us_per_step": round(ms * 1e3, 2), "rows_per_rank": fr, "collective": "NCCL all-gather of the Y shards"}
+        "us_per_step": round(ms * 1e3, 2), "rows_per_rank": fr,
+        "collective": "NCCL all-gather of the Y shards (padded to %d rows)" % fmax}
     del ws, xf, xb, y, yall
     torch.cuda.empty_cache()
     barrier()

@@ -118,24 +118,30 @@ ARCLLM_CUDA_API int arcllm_cuda_matvec_hostio(int ggml_type, const void *w, uint
  * Multi-GPU form of the LM head (rows sharded over the ranks: rank r owns rows
  * [row0, row0 + rows) of a rows_total-row matrix; the reference runs the LM
  * head on one device, src/arcllm_v1_runtime.cpp:285-291).  One kernel per
- * rank computes its rows and stores each fp32 result into EVERY rank's
- * exchange buffer (local store for its own, NVLink peer stores for the
- * others), then the ranks meet on per-rank flags: when the launch completes
- * on rank r, rank_bufs[r] holds all rows_total logits.  This replaces
- * matvec + ncclAllGather.
+ * rank computes its rows and stores each result into EVERY rank's exchange
+ * buffer as one 64-bit word (epoch << 32 | fp32 bits; a local store for its
+ * own buffer, NVLink peer stores for the others); each launch then reads its
+ * own buffer's words until all carry its epoch -- every word is its own flag,
+ * so no fence or separate handshake is needed -- and copies the values into
+ * its logits: when the launch completes on rank r, all rows_total logits are
+ * at rank_bufs[r] + arcllm_cuda_allgather_logits_offset(rows_total).  This
+ * replaces matvec + ncclAllGather.
  *   rank_bufs[i]: this process's device address of rank i's exchange buffer
  *                 (its own allocation for i == rank, an IPC mapping otherwise),
  *                 256-byte aligned, arcllm_cuda_allgather_buffer_bytes bytes,
- *                 zero-filled before first use;
+ *                 zero-filled before first use; consecutive launches alternate
+ *                 between two such buffer sets (epoch parity);
  *   epoch: 1, 2, 3 ... -- the same sequence on every rank, one per launch;
- *   timeout_us: bound of the flag wait (0: 2 s); a wait that runs out sets
- *               the device error word (ARC_E_DEVICE_TIMEOUT via
- *               arcllm_cuda_device_error) and the kernel returns.
+ *   timeout_us: bound of the wait for the other ranks' rows (0: 2 s); a wait
+ *               that runs out sets the device error word (ARC_E_DEVICE_TIMEOUT
+ *               via arcllm_cuda_device_error) and the kernel returns.
  * A rank may not rewrite a buffer that peers still store into: launches of
  * one epoch sequence must not overlap a reader of the previous logits.
  * Shapes: the whole-row tensor-core kernel (K/256 <= 14, even for Q6_K),
  * 16-byte aligned x; n_ranks <= 8. */
 ARCLLM_CUDA_API int arcllm_cuda_allgather_buffer_bytes(uint32_t rows_total, uint64_t *out);
+/* Byte offset of the gathered fp32 logits inside an exchange buffer. */
+ARCLLM_CUDA_API int arcllm_cuda_allgather_logits_offset(uint32_t rows_total, uint64_t *out);
 ARCLLM_CUDA_API int arcllm_cuda_matvec_allgather(int ggml_type, const void *w, uint32_t rows, uint32_t k,
                                                  const float *x, uint32_t row0, uint32_t rows_total,
                                                  void *const *rank_bufs, uint32_t n_ranks, uint32_t rank,
@@ -149,20 +155,22 @@ ARCLLM_CUDA_API int arcllm_cuda_ipc_close_handle(void *dev_ptr);
 
 /* ---- rank exchange (all-gather of a vector over NVLink peer stores) ------
  * Not in the reference (it decodes on one device, src/arcllm_v1_runtime.cpp:
- * 371-421); the reassembly step of row-sharded matvecs.  One CTA per rank
- * stores this rank's slice src[0, n_local) (32-bit words) at word `offset`
- * into every rank's exchange buffer (NVLink peer stores; nothing reads another
- * GPU's memory), publishes a sequence number in every rank's flag array and
- * waits (bounded by timeout_us, 0: 2 s) for all ranks' numbers, then copies
- * the assembled vector dst[0, n_total) out of its own buffer.
+ * 371-421); the reassembly step of row-sharded matvecs.  Each rank stores its
+ * slice src[0, n_local) (32-bit words) at word `offset` of every rank's
+ * exchange buffer, each word as one 64-bit word tagged with the exchange's
+ * sequence number (NVLink peer stores; nothing reads another GPU's memory),
+ * then reads the assembled vector dst[0, n_total) out of its own buffer,
+ * waiting (bounded by timeout_us, 0: 2 s) until every word carries the
+ * sequence number -- each word is its own flag, no fence or handshake.
  *   rank_bufs[q]: rank q's buffer as this process maps it (own allocation for
  *   q == rank, an IPC mapping otherwise), arcllm_cuda_exchange_buffer_bytes
  *   (max_words) bytes, 256-byte aligned, zero-filled before first use.
  * Every rank must issue the same sequence of exchanges (the sequence numbers
  * live in the buffers, so a CUDA graph of exchanges replays unchanged).  A
  * wait that runs out sets the device error word's timeout bit (ARC_E_DEVICE_
- * TIMEOUT from arcllm_cuda_device_error); the buffers must then be zeroed on
- * every rank before further use. */
+ * TIMEOUT from arcllm_cuda_device_error) and leaves the words that did not
+ * arrive out of dst; the buffers must then be zeroed on every rank before
+ * further use. */
 ARCLLM_CUDA_API int arcllm_cuda_exchange_buffer_bytes(uint32_t max_words, uint64_t *out);
 ARCLLM_CUDA_API int arcllm_cuda_exchange_gather(void *const *rank_bufs, uint32_t n_ranks, uint32_t rank,
                                                 uint32_t max_words, const void *src, uint32_t n_local,
@@ -427,12 +435,13 @@ ARCLLM_CUDA_API int arcllm_cuda_model_shard_lm_head(arcllm_cuda_model *m, uint32
  * GPU, every rank holding the whole set of weights (the reference decodes on
  * one device, src/arcllm_v1_runtime.cpp:371-421).  Each rank runs the
  * attention half of every layer in full (replicated), its shard of the FFN
- * gate/up rows, its shard of the FFN down rows (+ residual) and its shard of
- * the LM-head rows; after gate/up, after down and after its shard's greedy
- * argmax the ranks exchange the vector over NVLink peer stores
- * (arcllm_cuda_exchange_gather), so every rank holds the full s, the full
- * hidden state and the global greedy token, and all ranks produce the same
- * tokens.  rank_bufs as for arcllm_cuda_exchange_gather with max_words from
+ * gate/up rows, the same K window (its slice of s) of the FFN down projection
+ * and its shard of the LM-head rows; the ranks all-reduce the down
+ * projection's partial sums (+ residual) and exchange their greedy-argmax
+ * records over NVLink peer stores (the exchange kernel of
+ * arcllm_cuda_exchange_gather), so every rank holds the full hidden state and
+ * the global greedy token, and all ranks produce the same tokens.  rank_bufs
+ * as for arcllm_cuda_exchange_gather with max_words from
  * arcllm_cuda_model_tp_exchange_words.  Every rank must call generate() (or
  * the same begin/prefill/step sequence) with the same arguments.  The logits
  * buffer (arcllm_cuda_model_logits) then holds this rank's LM-head rows only.

@@ -72,9 +72,13 @@ def test_allgather_layout_and_argument_validation():
     L = A.lib()
     name = L.arcllm_cuda_status_string
     n = C.c_uint64(0)
-    assert L.arcllm_cuda_allgather_buffer_bytes(6016, C.byref(n)) == 0
-    assert n.value == 24064 + 128  # logits, then flags + counter at a 256-byte boundary
-    assert L.arcllm_cuda_allgather_buffer_bytes(6017, C.byref(n)) == 0 and n.value == 24320 + 128
+    off = C.c_uint64(0)
+    # 64-bit epoch-tagged words of every row, then the fp32 logits at a 256-byte boundary
+    assert L.arcllm_cuda_allgather_buffer_bytes(6016, C.byref(n)) == 0 and n.value == 48128 + 24064
+    assert L.arcllm_cuda_allgather_logits_offset(6016, C.byref(off)) == 0 and off.value == 48128
+    assert L.arcllm_cuda_allgather_buffer_bytes(6017, C.byref(n)) == 0 and n.value == 48384 + 24320
+    assert L.arcllm_cuda_allgather_logits_offset(6017, C.byref(off)) == 0 and off.value == 48384
+    assert name(L.arcllm_cuda_allgather_logits_offset(0, C.byref(off))) == b"ARC_E_INVALID_ARGUMENT"
     ag = L.arcllm_cuda_matvec_allgather
     w, x = C.c_void_p(256), C.c_void_p(256)
     ok = (C.c_void_p * 2)(256, 512)

@@ -43,7 +43,7 @@ class FakeLib:
         return (max_words + 3) & ~3
 
     def arcllm_cuda_exchange_buffer_bytes(self, max_words, out):
-        out._obj.value = ((2 * self._w(max_words) + 16) * 4 + 255) // 256 * 256
+        out._obj.value = (2 * self._w(max_words) * 8 + 16 * 4 + 255) // 256 * 256
         return 0
 
     def arcllm_cuda_malloc(self, nbytes, out):
@@ -83,55 +83,50 @@ class FakeLib:
         shm.unlink()
         return 0
 
+    def _begin(self, bufs, rank, max_words):
+        """sequence number (counter + 1, every per-CTA counter advanced) and the region's word offset"""
+        W = self._w(max_words)
+        ctr = bufs[rank] + 16 * W
+        seq = (struct.unpack("<I", C.string_at(ctr, 4))[0] + 1) & 0xFFFFFFFF
+        C.memmove(ctr, struct.pack("<16I", *([seq] * 16)), 64)
+        return seq, W * (seq & 1)
+
+    @staticmethod
+    def _store(bufs, n_ranks, region, at, words32, seq):
+        tagged = (np.uint64(seq) << np.uint64(32)) | words32.astype(np.uint64)
+        for q in range(n_ranks):  # into every rank's region of this parity
+            C.memmove(bufs[q] + 8 * (region + at), tagged.ctypes.data, tagged.nbytes)
+
+    @staticmethod
+    def _collect(own, n, seq, timeout_us):
+        """the n words at `own` once all carry seq (None on timeout)"""
+        t0 = time.time()
+        while True:
+            w = np.frombuffer(C.string_at(own, 8 * n), np.uint64)
+            if np.all((w >> np.uint64(32)) == np.uint64(seq)):
+                return (w & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+            if time.time() - t0 > timeout_us * 1e-6:
+                return None
+            time.sleep(0.0002)
+
     def arcllm_cuda_exchange_gather(self, bufs, n_ranks, rank, max_words, src, n_local, off, dst, n_total,
                                     timeout_us, stream):
-        W = self._w(max_words)
-        flags = [bufs[q] + 8 * W for q in range(n_ranks)]
-        seq_addr = flags[rank] + 32
-        seq = (struct.unpack("<I", C.string_at(seq_addr, 4))[0] + 1) & 0xFFFFFFFF
-        region = 4 * W * (seq & 1)
-        for q in range(n_ranks):  # the slice into every rank's region of this parity
-            C.memmove(bufs[q] + region + 4 * off, src, 4 * n_local)
-        for q in range(n_ranks):  # this rank's slot of every flag array
-            C.memmove(flags[q] + 4 * rank, struct.pack("<I", seq), 4)
-        t0 = time.time()
-        ok = True
-        while True:  # every slot of the own array reaches seq (wrap-safe)
-            slots = struct.unpack("<%dI" % n_ranks, C.string_at(flags[rank], 4 * n_ranks))
-            if all(((s - seq) & 0xFFFFFFFF) < 0x80000000 for s in slots):
-                break
-            if time.time() - t0 > timeout_us * 1e-6:
-                ok = False
-                break
-            time.sleep(0.0002)
-        C.memmove(seq_addr, struct.pack("<I", seq), 4)
-        if not ok:
+        seq, region = self._begin(bufs, rank, max_words)
+        self._store(bufs, n_ranks, region, off, np.frombuffer(C.string_at(src, 4 * n_local), np.uint32), seq)
+        vals = self._collect(bufs[rank] + 8 * region, n_total, seq, timeout_us)
+        if vals is None:
             return 6
-        C.memmove(dst, bufs[rank] + region, 4 * n_total)
+        C.memmove(dst, vals.ctypes.data, 4 * n_total)
         return 0
 
     def exchange_reduce(self, bufs, n_ranks, rank, max_words, src, n, residual, dst, timeout_us):
         """The reduce form: the whole vector into slot `rank`, then the slots summed in rank order."""
-        W = self._w(max_words)
-        flags = [bufs[q] + 8 * W for q in range(n_ranks)]
-        seq_addr = flags[rank] + 32
-        seq = (struct.unpack("<I", C.string_at(seq_addr, 4))[0] + 1) & 0xFFFFFFFF
-        region = 4 * W * (seq & 1)
-        for q in range(n_ranks):
-            C.memmove(bufs[q] + region + 4 * n * rank, src, 4 * n)
-        for q in range(n_ranks):
-            C.memmove(flags[q] + 4 * rank, struct.pack("<I", seq), 4)
-        t0 = time.time()
-        while True:
-            slots = struct.unpack("<%dI" % n_ranks, C.string_at(flags[rank], 4 * n_ranks))
-            if all(((s - seq) & 0xFFFFFFFF) < 0x80000000 for s in slots):
-                break
-            if time.time() - t0 > timeout_us * 1e-6:
-                C.memmove(seq_addr, struct.pack("<I", seq), 4)
-                return 6
-            time.sleep(0.0002)
-        C.memmove(seq_addr, struct.pack("<I", seq), 4)
-        parts = np.frombuffer(C.string_at(bufs[rank] + region, 4 * n * n_ranks), np.float32).reshape(n_ranks, n)
+        seq, region = self._begin(bufs, rank, max_words)
+        self._store(bufs, n_ranks, region, n * rank, np.frombuffer(C.string_at(src, 4 * n), np.uint32), seq)
+        vals = self._collect(bufs[rank] + 8 * region, n * n_ranks, seq, timeout_us)
+        if vals is None:
+            return 6
+        parts = vals.view(np.float32).reshape(n_ranks, n)
         t = parts[0].copy()
         for q in range(1, n_ranks):
             t = (t + parts[q]).astype(np.float32)

@@ -3,25 +3,25 @@ two and four gloo ranks in spawned processes build RankGather exactly as bench.p
 (handles swapped with all_gather_object), with the CUDA library replaced by a
 stand-in whose "device memory" is POSIX shared memory, whose IPC handles name
 those segments, and whose all-gather matvec follows the kernel's protocol
-(store this rank's rows into every rank's buffer of the launch's parity, write
-the epoch into this rank's flag slot everywhere, wait for all slots).
+(store this rank's rows as 64-bit (epoch << 32 | fp32 bits) words into every
+rank's buffer of the launch's parity, then read its own buffer's words until
+all carry the epoch and copy their values into the logits).
 
-Checked: the handle exchange and peer mapping, the buffer layout (flags after
-the logits at a 256-byte boundary), the epoch parity that alternates the two
-buffers, logits_ptr, and close().  The device kernel itself is covered by
+Checked: the handle exchange and peer mapping, the buffer layout (the logits
+after the words at a 256-byte boundary), the epoch parity that alternates the
+two buffers, logits_ptr, and close().  The device kernel itself is covered by
 tests/test_allgather_gpu.py.
 """
 import ctypes as C
 import datetime
 import multiprocessing as mp
 import socket
-import struct
 import time
 
 import numpy as np
 import pytest
 
-ROWS_TOTAL = 1000  # 2 x 500 or 4 x 250 rows; flags at align256(4000) = 4096
+ROWS_TOTAL = 1000  # 2 x 500 or 4 x 250 rows; logits at align256(8000) = 8192
 
 
 class FakeLib:
@@ -35,11 +35,15 @@ class FakeLib:
     def _addr(self, shm):
         return C.addressof(C.c_char.from_buffer(shm.buf))
 
-    def _flags_off(self, rows_total):
-        return (4 * rows_total + 255) // 256 * 256
+    def _logits_off(self, rows_total):
+        return (8 * rows_total + 255) // 256 * 256
 
     def arcllm_cuda_allgather_buffer_bytes(self, rows_total, out):
-        out._obj.value = self._flags_off(rows_total) + 128
+        out._obj.value = self._logits_off(rows_total) + (4 * rows_total + 255) // 256 * 256
+        return 0
+
+    def arcllm_cuda_allgather_logits_offset(self, rows_total, out):
+        out._obj.value = self._logits_off(rows_total)
         return 0
 
     def arcllm_cuda_malloc(self, nbytes, out):
@@ -81,16 +85,16 @@ class FakeLib:
 
     def arcllm_cuda_matvec_allgather(self, ggml_type, w, rows, k, x, row0, rows_total, bufs, n_ranks, rank, epoch,
                                      timeout_us, stream):
-        fo = self._flags_off(rows_total)
         y = (np.arange(row0, row0 + rows, dtype=np.float32) + np.float32(1000 * epoch))
-        for r in range(n_ranks):  # rows into every rank's buffer of this parity
-            C.memmove(bufs[r] + 4 * row0, y.ctypes.data, 4 * rows)
-        for r in range(n_ranks):  # this rank's slot of every flag array
-            C.memmove(bufs[r] + fo + 4 * rank, struct.pack("<I", epoch), 4)
+        words = (np.uint64(epoch) << np.uint64(32)) | y.view(np.uint32).astype(np.uint64)
+        for r in range(n_ranks):  # tagged rows into every rank's buffer of this parity
+            C.memmove(bufs[r] + 8 * row0, words.ctypes.data, 8 * rows)
         t0 = time.time()
-        while True:  # every slot of our own array reaches the epoch (wrap-safe compare)
-            slots = struct.unpack("<%dI" % n_ranks, C.string_at(bufs[rank] + fo, 4 * n_ranks))
-            if all(((s - epoch) & 0xFFFFFFFF) < 0x80000000 for s in slots):
+        while True:  # every word of our own buffer carries the epoch
+            got = np.frombuffer(C.string_at(bufs[rank], 8 * rows_total), np.uint64)
+            if np.all((got >> np.uint64(32)) == np.uint64(epoch)):
+                vals = (got & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+                C.memmove(bufs[rank] + self._logits_off(rows_total), vals.ctypes.data, 4 * rows_total)
                 return 0
             if time.time() - t0 > timeout_us * 1e-6:
                 return 6
@@ -126,7 +130,8 @@ def _worker(rank, world, port, q):
             rg.step(None, rows, 256, None, rank * rows, None)
             got = np.frombuffer(C.string_at(rg.logits_ptr, 4 * ROWS_TOTAL), np.float32)
             want = np.arange(ROWS_TOTAL, dtype=np.float32) + np.float32(1000 * e)
-            seen.append((rg.epoch, bool(np.array_equal(got, want)), rg.logits_ptr == rg._own[e & 1].value))
+            seen.append((rg.epoch, bool(np.array_equal(got, want)),
+                         rg.logits_ptr == rg._own[e & 1].value + fake._logits_off(ROWS_TOTAL)))
             dist.barrier()  # nobody runs the next epoch while another still reads these logits
         dist.barrier()
         rg.close()

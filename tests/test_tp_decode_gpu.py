@@ -58,8 +58,10 @@ def test_exchange_single_rank_is_a_copy_over_both_parities():
 
 def test_exchange_wait_times_out_when_a_rank_never_arrives():
     """Rank 0 of two whose rank-1 buffer is a local allocation nothing ever
-    signals: the wait gives up after 50 ms, sets the timeout bit, skips the
-    copy, and the next call (one rank) works."""
+    fills: rank 0's slice lands in both buffers as words tagged with sequence
+    number 1, the wait for rank 1's words gives up after 50 ms and sets the
+    timeout bit, rank 1's half of dst stays untouched, and the next call (one
+    rank) works."""
     n = C.c_uint64(0)
     A.call("arcllm_cuda_exchange_buffer_bytes", 3584, C.byref(n))
     bufs = [torch.zeros(n.value // 4 + 64, dtype=torch.int32, device=G.dev()) for _ in range(2)]
@@ -69,8 +71,13 @@ def test_exchange_wait_times_out_when_a_rank_never_arrives():
     assert _error_bits() == 0
     A.call("arcllm_cuda_exchange_gather", ptrs, 2, 0, 3584, G.ptr(src), 1792, 0, G.ptr(dst), 3584, 50000, G.stream())
     torch.cuda.synchronize()
-    assert _error_bits() & 1, "the flag wait should have timed out"
-    assert np.isnan(G.host(dst)).all()  # no copy after a timeout
+    assert _error_bits() & 1, "the wait should have timed out"
+    assert np.isnan(G.host(dst)[1792:]).all()  # rank 1's words never arrived
+    want = (np.uint64(1) << np.uint64(32)) | G.host(src).view(np.uint32).astype(np.uint64)
+    for b, p in zip(bufs, ptrs):  # sequence 1 -> data region 1, after region 0's 3584 words
+        words = b.cpu().numpy().view(np.uint8)[p - b.data_ptr():][:16 * 3584].view(np.uint64)
+        assert np.array_equal(words[3584:3584 + 1792], want)
+        assert not words[3584 + 1792:].any()
     one = (C.c_void_p * 1)(ptrs[0])
     A.call("arcllm_cuda_exchange_gather", one, 1, 0, 3584, G.ptr(src), 1792, 0, G.ptr(dst), 1792, 50000, G.stream())
     assert np.array_equal(G.host(dst)[:1792].view(np.uint32), G.host(src).view(np.uint32))
