@@ -655,7 +655,7 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
     alg = matvec_alg_bytes("q6k", HIDDEN, FFN)
     out["config1b_q6k_3584x18944_rowshard"] = {
         "GB/s": round(alg / (ms * 1e-3) / 1e9, 1), "us_per_step": round(ms * 1e3, 2),
-        "rows_per_rank": hr, "collective": "exchange kernel (NVLink peer stores + flags)",
+        "rows_per_rank": hr, "collective": "exchange kernel (NVLink peer stores of epoch-tagged 64-bit words)",
         "timing": "one CUDA graph of %d steps (matvec + exchange each), after a device rendezvous" % n_it,
         "rel_l2_vs_1gpu": float("%.3g" % max_over_ranks(diff)),
         "bit_exact_vs_1gpu_same_rows": bool(max_over_ranks(-same_rows) == -1)}
@@ -760,16 +760,23 @@ def run_extra(A, L, torch, dev, sp, hbm_peak, which="all"):
 
     def timed(launch, n_iter=200, warm=10):
         """Device time per launch: the n_iter launches are captured into one
-        CUDA graph (so host launch overhead does not gap the stream) and the
-        graph replay is timed with CUDA events on its stream."""
+        CUDA graph (so host launch overhead does not gap the stream), with
+        consecutive launches overlapping as in the headline (programmatic
+        dependent launch: a launch streams its weights while its predecessor
+        drains, then waits for it before reading inputs or writing outputs),
+        and the graph replay is timed with CUDA events on its stream."""
         for i in range(warm):
             launch(i, sp)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, capture_error_mode="thread_local"):
-            cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-            for i in range(n_iter):
-                launch(i, cs)
+        A.check(L.arcllm_cuda_set_launch_overlap(1), "launch overlap")
+        try:
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                cs = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+                for i in range(n_iter):
+                    launch(i, cs)
+        finally:
+            A.check(L.arcllm_cuda_set_launch_overlap(0), "launch overlap")
         g.replay()  # warm replay
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
