@@ -327,7 +327,7 @@ def main(argv=None):
         barrier()
 
     def step():
-        if rg is not None:  # one kernel: rows + NVLink peer stores + flag handshake
+        if rg is not None:  # one kernel: rows + NVLink peer stores of epoch-tagged words
             rg.step(wp, rows_per, K, xp, r0, sp, TY)
             return
         st = L.arcllm_cuda_matvec(TY, wp, rows_per, K, xp, None, C.c_float(0.0), None, None, yp, sp)
@@ -516,7 +516,7 @@ def main(argv=None):
                 "workload": ("config1: Q6_K LM-head matvec 152064x3584 (447.07 MB packed weights), fp32 x ~ N(0,1)"
                              if headline else "profiling case: %s matvec %dx%d" % (fmt, ROWS, K))
                             + (("; rows sharded over %d GPUs, fp32 logits all-gathered by the matvec kernel itself "
-                                "(NVLink peer stores + flag handshake)" % world if rg is not None else
+                                "(NVLink peer stores of epoch-tagged 64-bit words)" % world if rg is not None else
                                 "; rows sharded over %d GPUs + NCCL all-gather of fp32 logits" % world)
                                if world > 1 else ""),
                 "l2": "weights larger than L2 (%.0f MB vs 126 MB): no flush needed between steps"
@@ -528,7 +528,7 @@ def main(argv=None):
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                 "kernel": "matvec_imma_kernel (%s)" % fmt + (" with the NVLink all-gather epilogue; kernel_ms "
-                                                             "includes the peer stores and the rank handshake"
+                                                             "includes the peer stores and the wait for every rank's rows"
                                                              if rg is not None else ""),
                 "kernel_ms": round(kern_ms, 5), "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
                 "timing": ("mean launch time over one CUDA-graph replay of the %d timed launches%s" %
