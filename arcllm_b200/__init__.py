@@ -41,6 +41,7 @@ SIGNATURES = {
     "arcllm_cuda_matvec_q4k": [_vp, _u32, _u32, _vp, _vp, _vp, _vp],
     "arcllm_cuda_matvec_q6k": [_vp, _u32, _u32, _vp, _vp, _vp, _vp],
     "arcllm_cuda_gateup_silu_q4k": [_vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp],
+    "arcllm_cuda_ffn_block": [_i32, _vp, _vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp, _vp, _vp],
     "arcllm_cuda_gemm_q4k_bf16": [_vp, _u32, _u32, _vp, _u32, _vp, _vp],
     "arcllm_cuda_gemm_bf16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],
     "arcllm_cuda_gemm_f16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],

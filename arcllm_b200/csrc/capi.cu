@@ -292,6 +292,18 @@ int arcllm_cuda_gateup_silu_q4k(const void* w_gate, const void* w_up, uint32_t r
     ARC_GUARD_END
 }
 
+int arcllm_cuda_ffn_block(int down_type, const void* w_gate, const void* w_up, const void* w_down, uint32_t hidden,
+                          uint32_t ffn, const float* x, const float* gamma, float eps, float* s,
+                          const float* residual, float* y, void* stream) {
+    ARC_GUARD_BEGIN
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc = arc::matvec_any(ARC_GGML_Q4_K, true, w_gate, w_up, ffn, hidden, x, gamma, eps, nullptr, nullptr, s, st);
+    if (rc == ARC_OK)
+        rc = arc::matvec_any(down_type, false, w_down, nullptr, hidden, ffn, s, nullptr, 0.f, nullptr, residual, y, st);
+    return rc;
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_exec148_materialize(const void* q4k, uint64_t n_blocks, void* exec, void* stream) {
     ARC_GUARD_BEGIN
     return arc::exec148_materialize(q4k, n_blocks, exec, static_cast<cudaStream_t>(stream));

@@ -188,6 +188,16 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
+// Relaxed GPU-scope 64-bit accesses, for tagged words exchanged between CTAs of one device.
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Relaxed system-scope 64-bit accesses: single-copy atomic, so a word that
 // carries its own epoch tag next to its value needs no fence on either side.
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {

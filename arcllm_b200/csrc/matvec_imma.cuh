@@ -512,5 +512,44 @@ __device__ __forceinline__ void q6_tile_lowreg(const uint8_t* st, uint32_t row0,
     y1 += out[1];
 }
 
+// Whole-row kernels: the warp's x slice (windows 0..3 from block bA, 4..7 from block bB):
+// load, fuse the RMSNorm (sum of squares over all warps, in double), quantise
+// into the warp's scratch, gather this lane's fragments.
+template <int FMT>
+__device__ __forceinline__ void build_xfrag(const float* x, const float* gamma, float eps, uint32_t k, double* red_d,
+                                            uint32_t nwc, uint32_t warp, uint32_t bA, uint32_t bB, uint32_t lane,
+                                            uint8_t* xs, XFrag& f) {
+    const uint32_t jw = lane >> 2, qd = lane & 3u;
+    const uint32_t e0 = 256u * (jw < 4 ? bA : bB) + 32u * jw + 8u * qd;
+    float v[8];
+    {
+        const float4 a0 = *reinterpret_cast<const float4*>(x + e0);
+        const float4 a1 = *reinterpret_cast<const float4*>(x + e0 + 4);
+        v[0] = a0.x, v[1] = a0.y, v[2] = a0.z, v[3] = a0.w, v[4] = a1.x, v[5] = a1.y, v[6] = a1.z, v[7] = a1.w;
+    }
+    if (gamma) {
+        const float4 g0 = *reinterpret_cast<const float4*>(gamma + e0);
+        const float4 g1 = *reinterpret_cast<const float4*>(gamma + e0 + 4);
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        // fused RMSNorm: 1/sqrt(mean(x^2) + eps), sum of squares in double.
+        // The warps' 256-element slices cover x exactly once.
+        double ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += (double)v[i] * (double)v[i];
+        ss = warp_sum_d(ss);
+        if (lane == 0) red_d[warp] = ss;
+        named_bar_sync(1, nwc * 32u);
+        double tot = 0.0;
+        for (uint32_t w = 0; w < nwc; ++w) tot += red_d[w];
+        const float inv = 1.0f / sqrtf((float)(tot / (double)k) + eps);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = (v[i] * inv) * gv[i];
+    }
+    float* kc = reinterpret_cast<float*>(xs + 768);
+    quantize8<FMT>(v, lane, xs, kc);
+    __syncwarp();
+    gather_xfrag<FMT>(xs, kc, xs, kc, lane, f);
+}
+
 }  // namespace
 }  // namespace arc

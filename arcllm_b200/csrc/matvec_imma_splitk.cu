@@ -55,12 +55,12 @@ constexpr uint32_t kMaxMaps = 4;
 constexpr uint32_t kNW = 14;                         // consumer warps = widest slice
 constexpr uint32_t kG = 32;                          // rows per stage (two 16-row MMA tiles)
 constexpr uint32_t kXScratch = 1024;                 // per consumer warp: 3 limb planes + window constants
-constexpr uint32_t kHead = 2 * kMaxStages * 8 + 16;  // full/empty barriers, abort flag (+pad)
+constexpr uint32_t kHead = 2 * kMaxStages * 8 + 16;  // full/empty barriers, abort flag, launch tag (+pad)
 constexpr uint32_t kBoxMax = 2048;                   // bytes: 256 u64 elements per box row
 
 struct KSlice {
-    float* part;    // [P][rows] slice partials
-    uint32_t* cnt;  // [n_groups] arrival counters (zero between launches)
+    unsigned long long* part;  // [P][rows] slice partials, (tag << 32 | fp32 bits)
+    uint32_t* ctl;             // [0] launch counter (tag = ctl[0] + 1), [1] CTAs counted out (zero between launches)
     uint32_t P, tx_max;
     uint16_t kb0[kMaxSlices], W[kMaxSlices], cta0[kMaxSlices + 1];
     // per slice: columns (1 or 2) = (first block in the slice, box bytes, map, smem region offset)
@@ -122,55 +122,70 @@ __device__ __forceinline__ void tma_box_2d(void* dst, const CUtensorMap* map, in
 
 // Round `itr` of this CTA (row group grp) is complete: add the consumer
 // warps' partials in warp order and store the CTA's slice partial of the
-// group's rows (plain stores; ks_close publishes them).  Run by the producer.
+// group's rows as words tagged with this launch's tag.  Run by the producer.
 __device__ __forceinline__ void ks_partial(const MvParams& p, const KSlice& q, const float* red, uint32_t W,
-                                           uint32_t sl, uint32_t itr, uint32_t grp, uint32_t lane) {
+                                           uint32_t sl, uint32_t itr, uint32_t grp, uint32_t lane, uint32_t tag) {
     const uint32_t S = p.stages, s = itr % S, par = (itr / S) & 1u;
     const uint32_t rows_g = min(kG, p.rows - grp * kG);
     const float* rs = red + (par * S + s) * kNW * kG;
     if (lane < rows_g) {
         float a = 0.f;
         for (uint32_t w = 0; w < W; ++w) a += rs[w * kG + lane];
-        q.part[(size_t)sl * p.rows + grp * kG + lane] = a;
+        st_relaxed_gpu_u64(q.part + (size_t)sl * p.rows + grp * kG + lane,
+                           ((unsigned long long)tag << 32) | __float_as_uint(a));
     }
 }
 
-// After the CTA's last round: publish its slice partials (one fence), count
-// this slice in for each of its row groups, and for every group whose last
-// slice this CTA delivered add the P slice partials in slice order
-// (deterministic whichever CTA comes last), apply bias / residual, write y
-// and re-arm the group's counter for the next launch.  The cross-CTA
-// round trips are paid once per CTA, off the streaming loop.
-__device__ __forceinline__ void ks_close(const MvParams& p, const KSlice& q, uint32_t g0, uint32_t n, uint32_t lane) {
-    __threadfence();
-    __syncwarp();
-    for (uint32_t base = 0; base < n; base += 32u) {
-        const uint32_t gi = base + lane;
-        bool last = false;
-        if (gi < n) last = atomicAdd(&q.cnt[g0 + gi], 1u) == q.P - 1u;
-        uint32_t m = __ballot_sync(0xffffffffu, last);
-        if (m) __threadfence();  // the other slices' partials of those groups are visible in L2
-        while (m) {
-            const uint32_t grp = g0 + base + (uint32_t)(__ffs(m) - 1);
-            m &= m - 1u;
-            const uint32_t rows_g = min(kG, p.rows - grp * kG);
-            const uint32_t row = grp * kG + lane;
-            if (lane < rows_g) {
-                float v[kMaxSlices];
+// Closing a row group: the CTA of slice (group % P) that owns the group,
+// once its own rounds are consumed, has consumer warp w take its groups w,
+// w + W, ... among those; for each row (one per lane) the warp reads the P
+// slice partials until every word carries this launch's tag, adds them in
+// slice order (deterministic: the same order whichever slice came last),
+// applies bias / residual and writes y.  No fence and no counter: each word is
+// its own flag, and the close work is spread over the slices and the warps.
+// Gives up after kWaitLimitNs.
+__device__ __forceinline__ void ks_close(const MvParams& p, const KSlice& q, uint32_t sl, uint32_t g0, uint32_t n,
+                                         uint32_t warp, uint32_t W, uint32_t lane, uint32_t tag) {
+    const unsigned long long t0 = globaltimer();
+    uint32_t k = 0;  // index among this CTA's groups that it closes
+    for (uint32_t gi = 0; gi < n; ++gi) {
+        const uint32_t grp = g0 + gi;
+        if (grp % q.P != sl) continue;
+        if (k++ % W != warp) continue;
+        const uint32_t rows_g = min(kG, p.rows - grp * kG);
+        const uint32_t row = grp * kG + lane;
+        if (lane >= rows_g) continue;
+        unsigned long long v[kMaxSlices];
 #pragma unroll
-                for (uint32_t j = 0; j < kMaxSlices; ++j)
-                    v[j] = j < q.P ? __ldcg(q.part + (size_t)j * p.rows + row) : 0.f;
-                float t = 0.f;
+        for (uint32_t j = 0; j < kMaxSlices; ++j)  // every slice's word in flight before the first wait
+            if (j < q.P) v[j] = ld_relaxed_gpu_u64(q.part + (size_t)j * p.rows + row);
+        float t = 0.f;
 #pragma unroll
-                for (uint32_t j = 0; j < kMaxSlices; ++j)
-                    if (j < q.P) t += v[j];
-                if (p.bias) t += p.bias[row];
-                if (p.residual) t = p.residual[row] + t;
-                p.y[row] = t;
+        for (uint32_t j = 0; j < kMaxSlices; ++j) {
+            if (j >= q.P) break;
+            while ((uint32_t)(v[j] >> 32) != tag) {
+                if (globaltimer() - t0 > kWaitLimitNs) {
+                    raise_error(p.err, ARC_DEV_ERR_TIMEOUT);
+                    return;
+                }
+                __nanosleep(32);
+                v[j] = ld_relaxed_gpu_u64(q.part + (size_t)j * p.rows + row);
             }
-            __syncwarp();
-            if (lane == 0) atomicExch(&q.cnt[grp], 0u);
+            t += __uint_as_float((uint32_t)v[j]);
         }
+        if (p.bias) t += p.bias[row];
+        if (p.residual) t = p.residual[row] + t;
+        p.y[row] = t;
+    }
+}
+
+// Producer lane 0 at the very end of every CTA: count the CTA out; the last
+// one advances the launch counter (the next launch's tag) and re-arms the count.
+// Every CTA of this launch read the counter before it counted out.
+__device__ __forceinline__ void ks_count_out(const KSlice& q) {
+    if (atomicAdd(q.ctl + 1, 1u) == gridDim.x - 1u) {
+        q.ctl[1] = 0u;
+        atomicAdd(q.ctl, 1u);
     }
 }
 
@@ -180,133 +195,56 @@ __device__ __forceinline__ void ks_close(const MvParams& p, const KSlice& q, uin
 __host__ __device__ constexpr uint32_t ks_bsz(int fmt) { return fmt == 12 ? 144u : fmt == 14 ? 210u : 148u; }
 __host__ __device__ constexpr uint32_t ks_rs(int fmt) { return fmt == 12 ? 1u : fmt == 14 ? 4u : 2u; }
 
+// Lane 0 of a producer warp: the TMA boxes of row group grp of this CTA's
+// slice into stage stg, completing on bar.
 template <int FMT>
-__global__ void __launch_bounds__((kNW + 1) * 32, 1)
-    matvec_imma_kslice_kernel(const MvParams p, const __grid_constant__ KSlice q, const __grid_constant__ KMaps maps) {
+__device__ __forceinline__ void ks_issue(const MvParams& p, const SliceView& sv, const KMaps& maps, uint8_t* stg,
+                                         uint64_t* bar, uint32_t grp, uint64_t pol) {
     constexpr uint32_t bsz = ks_bsz(FMT);
     constexpr uint32_t Rs = ks_rs(FMT);  // rows per tensor-map super-row
-    constexpr uint32_t J = kG / Rs;               // box rows
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kMaxStages;
-    volatile int* abort_flag = reinterpret_cast<int*>(empty + kMaxStages);
-    double* red_d = reinterpret_cast<double*>(smem + kHead);     // [32]
-    float* red = reinterpret_cast<float*>(smem + ks_red_off());  // [2][S][kNW][kG]
-    uint8_t* xscr = smem + ks_xscr_off(p.stages);
-    uint8_t* stages = smem_align_up<128>(smem, ks_stage_off(p.stages));
-
-    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
-    const uint32_t S = p.stages;
-    // this CTA's slice and its contiguous range of row groups
-    const SliceView sv = slice_of(q, blockIdx.x);
-    const uint32_t sl = sv.sl, W = sv.W, kb0 = sv.kb0;
-    const uint32_t g0 = (uint32_t)((uint64_t)p.n_groups * sv.ci / sv.C);
-    const uint32_t n = (uint32_t)((uint64_t)p.n_groups * (sv.ci + 1) / sv.C) - g0;
-    pdl_trigger();
-
-    if (tid == kNW * 32) {
-        for (uint32_t s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], W);
-        }
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    if (warp == kNW) {
-        // ---------------- producer ----------------
-        const uint64_t pol = l2_evict_first_policy();
-        if (!p.early) pdl_wait();
-        uint32_t it = 0;
-        bool ok = true;
-        auto released = [&](uint32_t j) {  // wait until the consumers released round j of its slot
-            bool w = true;
-            if (lane == 0) w = mbar_wait(&empty[j % S], (j / S) & 1u, p.err);
-            w = __shfl_sync(0xffffffffu, w, 0);
-            if (!w || *abort_flag) {
-                if (lane == 0) *abort_flag = 1;
-                return false;
-            }
-            return true;
-        };
-        for (; it < n; ++it) {
-            const uint32_t s = it % S;
-            if (it >= S && !released(it - S)) {
-                ok = false;
-                break;
-            }
-            const uint32_t grp = g0 + it;
-            if (lane == 0) {
-                uint8_t* stg = stages + s * p.stage_smem;
-                mbar_arrive_expect_tx(&full[s], sv.tx);  // whole boxes, zero-filled rows included
+    constexpr uint32_t J = kG / Rs;      // box rows
+    mbar_arrive_expect_tx(bar, sv.tx);   // whole boxes, zero-filled rows included
 #pragma unroll
-                for (uint32_t c = 0; c < 2; ++c) {
-                    if (c < sv.ncol) {
-                        const uint32_t mi = sv.cmap[c];
-                        const CUtensorMap* mp = mi == 0 ? &maps.m[0] : mi == 1 ? &maps.m[1] : mi == 2 ? &maps.m[2] : &maps.m[3];
-                        const uint32_t bw = sv.cbw[c];
+    for (uint32_t c = 0; c < 2; ++c) {
+        if (c < sv.ncol) {
+            const uint32_t mi = sv.cmap[c];
+            const CUtensorMap* mp = mi == 0 ? &maps.m[0] : mi == 1 ? &maps.m[1] : mi == 2 ? &maps.m[2] : &maps.m[3];
+            const uint32_t bw = sv.cbw[c];
 #pragma unroll
-                        for (uint32_t i = 0; i < Rs; ++i) {
-                            const uint32_t xb = (uint32_t)(((uint64_t)i * p.rb +
-                                                            (uint64_t)(p.kb_base + kb0 + sv.cst[c]) * bsz) &
-                                                           ~(uint64_t)15);
-                            tma_box_2d(stg + sv.coff[c] + i * J * bw, mp, (int)(xb / 8u), (int)(grp * J), &full[s],
-                                       pol);
-                        }
-                    }
-                }
-            }
-            __syncwarp();
-            if (it >= S) ks_partial(p, q, red, W, sl, it - S, g0 + it - S, lane);
-        }
-        if (ok) {
-            for (uint32_t j = it > S ? it - S : 0; j < it; ++j) {
-                if (!released(j)) {
-                    ok = false;
-                    break;
-                }
-                ks_partial(p, q, red, W, sl, j, g0 + j, lane);
+            for (uint32_t i = 0; i < Rs; ++i) {
+                const uint32_t xb = (uint32_t)(((uint64_t)i * p.rb + (uint64_t)(p.kb_base + sv.kb0 + sv.cst[c]) * bsz) &
+                                               ~(uint64_t)15);
+                tma_box_2d(stg + sv.coff[c] + i * J * bw, mp, (int)(xb / 8u), (int)(grp * J), bar, pol);
             }
         }
-        if (ok) {
-            ks_close(p, q, g0, n, lane);
-        } else if (lane == 0) {  // no box may still be landing in this CTA's smem at exit
-            const uint32_t first = it > S ? it - S : 0;
-            for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1u, p.err);
-        }
-        return;
     }
+}
 
-    // ---------------- consumers ----------------
-    pdl_wait();  // x, gamma, bias and residual come from the preceding kernels
+// Consumer warp `warp` (< the slice width) of a K-slice CTA: builds its routed
+// x fragments (x indexed by the full K, times `inv` and gamma when the RMSNorm
+// is fused), then consumes rounds [it0, it0 + n) of the stage ring -- this
+// CTA's row groups of its slice -- leaving per-row partials in `red` and
+// releasing each stage.  LDCG: read x through L2 (x written by other CTAs of
+// the same launch).
+template <int FMT, bool LDCG>
+__device__ __forceinline__ void ks_consume(const MvParams& p, const SliceView& sv, const uint8_t* stages,
+                                           uint64_t* full, uint64_t* empty, volatile int* abort_flag, float* red,
+                                           uint8_t* xscr, float inv, uint32_t it0, uint32_t n, uint32_t warp,
+                                           uint32_t lane) {
+    constexpr uint32_t bsz = ks_bsz(FMT);
+    constexpr uint32_t Rs = ks_rs(FMT);
+    constexpr uint32_t J = kG / Rs;
+    const uint32_t S = p.stages, kb0 = sv.kb0;
     const uint32_t jw = lane >> 2, qd = lane & 3u;
-    float inv = 1.0f;
-    if (p.gamma) {  // fused RMSNorm over all of K (every consumer warp takes part)
-        double ss = 0.0;
-        for (uint32_t sb = warp; sb < p.nb; sb += kNW) {
-            const uint32_t e0 = 256u * sb + 32u * jw + 8u * qd;
-            const float4 a0 = *reinterpret_cast<const float4*>(p.x + e0);
-            const float4 a1 = *reinterpret_cast<const float4*>(p.x + e0 + 4);
-            ss += (double)a0.x * a0.x + (double)a0.y * a0.y + (double)a0.z * a0.z + (double)a0.w * a0.w;
-            ss += (double)a1.x * a1.x + (double)a1.y * a1.y + (double)a1.z * a1.z + (double)a1.w * a1.w;
-        }
-        ss = warp_sum_d(ss);
-        if (lane == 0) red_d[warp] = ss;
-        named_bar_sync(1, kNW * 32u);
-        double tot = 0.0;
-        for (uint32_t w = 0; w < kNW; ++w) tot += red_d[w];
-        inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
-    }
-    if (warp >= W) return;  // narrower slice: this warp has no super-block
-
     // this warp's super-block(s) of the slice: x slice, quantised, routed fragments
     const uint32_t bA = p.kb_base + kb0 + warp, bB = FMT == 14 ? p.kb_base + kb0 + (warp ^ 1u) : bA;
     XFrag f;
     {
         const uint32_t e0 = 256u * (jw < 4 ? bA : bB) + 32u * jw + 8u * qd;
-        const float4 a0 = *reinterpret_cast<const float4*>(p.x + e0);
-        const float4 a1 = *reinterpret_cast<const float4*>(p.x + e0 + 4);
+        const float4 a0 = LDCG ? __ldcg(reinterpret_cast<const float4*>(p.x + e0))
+                               : *reinterpret_cast<const float4*>(p.x + e0);
+        const float4 a1 = LDCG ? __ldcg(reinterpret_cast<const float4*>(p.x + e0 + 4))
+                               : *reinterpret_cast<const float4*>(p.x + e0 + 4);
         float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         if (p.gamma) {
             const float4 g0v = *reinterpret_cast<const float4*>(p.gamma + e0);
@@ -350,7 +288,7 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1)
     const uint32_t offA = (warp - cs) * bsz, offB = (FMT == 14 ? ((warp ^ 1u) - cs) : (warp - cs)) * bsz;
     const bool oddA = FMT == 14 && (warp & 1u) != 0u;
 
-    for (uint32_t it = 0; it < n; ++it) {
+    for (uint32_t it = it0; it < it0 + n; ++it) {
         const uint32_t s = it % S;
         if (!mbar_wait(&full[s], (it / S) & 1u, p.err)) *abort_flag = 1;
         if (*abort_flag) break;
@@ -390,10 +328,114 @@ __global__ void __launch_bounds__((kNW + 1) * 32, 1)
     }
 }
 
+template <int FMT>
+__global__ void __launch_bounds__((kNW + 1) * 32, 1)
+    matvec_imma_kslice_kernel(const MvParams p, const __grid_constant__ KSlice q, const __grid_constant__ KMaps maps) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxStages;
+    volatile int* abort_flag = reinterpret_cast<int*>(empty + kMaxStages);
+    double* red_d = reinterpret_cast<double*>(smem + kHead);     // [32]
+    float* red = reinterpret_cast<float*>(smem + ks_red_off());  // [2][S][kNW][kG]
+    uint8_t* xscr = smem + ks_xscr_off(p.stages);
+    uint8_t* stages = smem_align_up<128>(smem, ks_stage_off(p.stages));
+    // this launch's tag (the header word after the abort flag), stored by consumer warp 0 after
+    // griddepcontrol.wait
+    volatile uint32_t* tagp = reinterpret_cast<volatile uint32_t*>(empty + kMaxStages) + 1;
+
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const uint32_t S = p.stages;
+    // this CTA's slice and its contiguous range of row groups
+    const SliceView sv = slice_of(q, blockIdx.x);
+    const uint32_t sl = sv.sl, W = sv.W;
+    const uint32_t g0 = (uint32_t)((uint64_t)p.n_groups * sv.ci / sv.C);
+    const uint32_t n = (uint32_t)((uint64_t)p.n_groups * (sv.ci + 1) / sv.C) - g0;
+    pdl_trigger();
+
+    if (tid == kNW * 32) {
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], W);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kNW) {
+        // ---------------- producer ----------------
+        const uint64_t pol = l2_evict_first_policy();
+        if (!p.early) pdl_wait();
+        uint32_t it = 0;
+        bool ok = true;
+        auto released = [&](uint32_t j) {  // wait until the consumers released round j of its slot
+            bool w = true;
+            if (lane == 0) w = mbar_wait(&empty[j % S], (j / S) & 1u, p.err);
+            w = __shfl_sync(0xffffffffu, w, 0);
+            if (!w || *abort_flag) {
+                if (lane == 0) *abort_flag = 1;
+                return false;
+            }
+            return true;
+        };
+        for (; it < n; ++it) {
+            const uint32_t s = it % S;
+            if (it >= S && !released(it - S)) {
+                ok = false;
+                break;
+            }
+            if (lane == 0) ks_issue<FMT>(p, sv, maps, stages + s * p.stage_smem, &full[s], g0 + it, pol);
+            __syncwarp();
+            // (a released round implies consumer warp 0 has stored the tag)
+            if (it >= S) ks_partial(p, q, red, W, sl, it - S, g0 + it - S, lane, *tagp);
+        }
+        if (ok) {
+            for (uint32_t j = it > S ? it - S : 0; j < it; ++j) {
+                if (!released(j)) {
+                    ok = false;
+                    break;
+                }
+                ks_partial(p, q, red, W, sl, j, g0 + j, lane, *tagp);
+            }
+        }
+        if (!ok && lane == 0) {  // no box may still be landing in this CTA's smem at exit
+            const uint32_t first = it > S ? it - S : 0;
+            for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1u, p.err);
+        }
+        if (lane == 0) ks_count_out(q);
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    pdl_wait();  // x, gamma, bias and residual come from the preceding kernels
+    if (tid == 0) *tagp = *reinterpret_cast<volatile uint32_t*>(q.ctl) + 1u;  // before warp 0's first release
+    float inv = 1.0f;
+    if (p.gamma) {  // fused RMSNorm over all of K (every consumer warp takes part)
+        const uint32_t jw = lane >> 2, qd = lane & 3u;
+        double ss = 0.0;
+        for (uint32_t sb = warp; sb < p.nb; sb += kNW) {
+            const uint32_t e0 = 256u * sb + 32u * jw + 8u * qd;
+            const float4 a0 = *reinterpret_cast<const float4*>(p.x + e0);
+            const float4 a1 = *reinterpret_cast<const float4*>(p.x + e0 + 4);
+            ss += (double)a0.x * a0.x + (double)a0.y * a0.y + (double)a0.z * a0.z + (double)a0.w * a0.w;
+            ss += (double)a1.x * a1.x + (double)a1.y * a1.y + (double)a1.z * a1.z + (double)a1.w * a1.w;
+        }
+        ss = warp_sum_d(ss);
+        if (lane == 0) red_d[warp] = ss;
+        named_bar_sync(1, kNW * 32u);
+        double tot = 0.0;
+        for (uint32_t w = 0; w < kNW; ++w) tot += red_d[w];
+        inv = 1.0f / sqrtf((float)(tot / (double)p.k) + p.eps);
+    }
+    if (warp >= W) return;  // narrower slice: this warp has no super-block
+    ks_consume<FMT, false>(p, sv, stages, full, empty, abort_flag, red, xscr, inv, 0u, n, warp, lane);
+    if (!*abort_flag) ks_close(p, q, sl, g0, n, warp, W, lane, *tagp);
+}
+
 struct KsScratch {
-    float* part = nullptr;
-    uint32_t* cnt = nullptr;
-    size_t part_floats = 0, cnt_n = 0;
+    unsigned long long* part = nullptr;  // tagged slice partials
+    uint32_t* ctl = nullptr;             // launch counter + CTA count-out
+    size_t part_words = 0;
 };
 std::mutex g_ks_mutex;
 KsScratch g_ks[64];
@@ -551,6 +593,26 @@ cudaError_t set_attr_ks() {
                                 227 * 1024);
 }
 
+// The rows x k matrix as u64 words in super-rows of Rs rows (Rs * row bytes is a multiple of 16),
+// one tensor map per box width of the plan.
+int ks_encode_maps(int fmt, const void* w, uint32_t rows, uint32_t k, const KsPlan& pl, KMaps* maps) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return set_error(ARC_E_CUDA, "matvec split-K: cuTensorMapEncodeTiled unavailable");
+    const uint32_t nb = k / 256u, rb = nb * ks_bsz(fmt), Rs = ks_rs(fmt);
+    std::memset(maps, 0, sizeof *maps);
+    for (uint32_t i = 0; i < pl.nmaps; ++i) {
+        const cuuint64_t dims[2] = {(cuuint64_t)Rs * rb / 8u, (cuuint64_t)(rows / Rs)};
+        const cuuint64_t strides[1] = {(cuuint64_t)Rs * rb};
+        const cuuint32_t box[2] = {pl.map_bw[i] / 8u, kG / Rs};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUresult r = enc(&maps->m[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides,
+                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return set_error(ARC_E_INVALID_ARGUMENT, "matvec split-K: tensor map rejected");
+    }
+    return ARC_OK;
+}
+
 }  // namespace
 
 int ks_reserve(int fmt, uint32_t rows, uint32_t k);
@@ -566,30 +628,39 @@ int matvec_kwindow_reserve(int fmt, uint32_t rows, uint32_t nb_win) { return ks_
 int ks_reserve(int fmt, uint32_t rows, uint32_t k) {
     const KsPlan pl = ks_plan_cached(fmt, rows, k, (uint32_t)ks_sm_count());
     if (!pl.ok) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec split-K: no plan fits shared memory");
-    const size_t need_part = (size_t)pl.q.P * rows, need_cnt = pl.n_groups;
+    const size_t need_part = (size_t)pl.q.P * rows;
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(g_ks_mutex);
     KsScratch& sc = g_ks[dev & 63];
-    if (sc.part_floats >= need_part && sc.cnt_n >= need_cnt) return ARC_OK;
-    const size_t np = std::max(need_part, sc.part_floats), nc = std::max(need_cnt, sc.cnt_n);
-    float* part = nullptr;
-    uint32_t* cnt = nullptr;
-    cudaError_t e = cudaMalloc(&part, np * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&cnt, nc * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMemset(cnt, 0, nc * sizeof(uint32_t));
+    if (sc.part_words >= need_part && sc.ctl) return ARC_OK;
+    const size_t np = std::max(need_part, sc.part_words);
+    unsigned long long* part = nullptr;
+    uint32_t* ctl = nullptr;
+    cudaError_t e = cudaMalloc(&part, np * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMalloc(&ctl, 4 * sizeof(uint32_t));
+    // zeroed words carry tag 0, which no launch uses (tags start at 1)
+    if (e == cudaSuccess) e = cudaMemset(part, 0, np * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(ctl, 0, 4 * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(part);
-        cudaFree(cnt);
+        cudaFree(ctl);
         return set_cuda_error(e, "matvec split-K scratch");
     }
+    if (sc.ctl) {  // keep the launch counter running: words of earlier launches carry earlier tags
+        e = cudaMemcpy(ctl, sc.ctl, sizeof(uint32_t), cudaMemcpyDeviceToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(part);
+            cudaFree(ctl);
+            return set_cuda_error(e, "matvec split-K scratch");
+        }
+    }
     cudaFree(sc.part);  // grown only outside concurrent use (documented)
-    cudaFree(sc.cnt);
+    cudaFree(sc.ctl);
     sc.part = part;
-    sc.cnt = cnt;
-    sc.part_floats = np;
-    sc.cnt_n = nc;
+    sc.ctl = ctl;
+    sc.part_words = np;
     return ARC_OK;
 }
 
@@ -646,28 +717,16 @@ int matvec_kwindow_launch(int fmt, const void* w, uint32_t rows, uint32_t k, uin
     if (st != ARC_OK) return st;
     KsPlan pl = ks_plan_cached(fmt, rows, kw, (uint32_t)ks_sm_count());
     if (!pl.ok) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec split-K: no plan fits shared memory");
-    EncodeTiledFn enc = encode_tiled_fn();
-    if (!enc) return set_error(ARC_E_CUDA, "matvec split-K: cuTensorMapEncodeTiled unavailable");
-    // the matrix as u64 words in super-rows of Rs rows (Rs * row bytes is a multiple of 16)
-    const uint32_t nb = k / 256u, rb = nb * ks_bsz(fmt), Rs = ks_rs(fmt);
+    const uint32_t rb = (k / 256u) * ks_bsz(fmt);
     KMaps maps;
-    std::memset(&maps, 0, sizeof maps);
-    for (uint32_t i = 0; i < pl.nmaps; ++i) {
-        const cuuint64_t dims[2] = {(cuuint64_t)Rs * rb / 8u, (cuuint64_t)(rows / Rs)};
-        const cuuint64_t strides[1] = {(cuuint64_t)Rs * rb};
-        const cuuint32_t box[2] = {pl.map_bw[i] / 8u, kG / Rs};
-        const cuuint32_t estr[2] = {1, 1};
-        const CUresult r = enc(&maps.m[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) return set_error(ARC_E_INVALID_ARGUMENT, "matvec split-K: tensor map rejected");
-    }
+    st = ks_encode_maps(fmt, w, rows, k, pl, &maps);
+    if (st != ARC_OK) return st;
     int dev = 0;
     cudaGetDevice(&dev);
     {
         std::lock_guard<std::mutex> lock(g_ks_mutex);
         pl.q.part = g_ks[dev & 63].part;
-        pl.q.cnt = g_ks[dev & 63].cnt;
+        pl.q.ctl = g_ks[dev & 63].ctl;
     }
     MvParams p{};
     p.w0 = static_cast<const uint8_t*>(w);

@@ -864,20 +864,18 @@ def run_extra(A, L, torch, dev, sp, hbm_peak, which="all"):
     s = torch.empty(FFN, dtype=torch.float32, device=dev)
     h = torch.empty(HIDDEN, dtype=torch.float32, device=dev)
 
-    def ffn(i, stream):
+    def ffn(i, stream):  # RMSNorm + gate/up + SiLU*up, then down + residual (two launches)
         c = i % n
-        A.check(L.arcllm_cuda_gateup_silu_q4k(C.c_void_p(wg[c].data_ptr()), C.c_void_p(wu[c].data_ptr()), FFN, HIDDEN,
-                                              C.c_void_p(x35.data_ptr()), C.c_void_p(gamma.data_ptr()),
-                                              C.c_float(1e-6), C.c_void_p(s.data_ptr()), stream), "gateup")
-        A.check(L.arcllm_cuda_matvec(A.GGML_Q4_K, C.c_void_p(wd[c].data_ptr()), HIDDEN, FFN, C.c_void_p(s.data_ptr()),
-                                     None, C.c_float(0), None, C.c_void_p(x35.data_ptr()), C.c_void_p(h.data_ptr()),
-                                     stream), "down")
+        A.check(L.arcllm_cuda_ffn_block(A.GGML_Q4_K, C.c_void_p(wg[c].data_ptr()), C.c_void_p(wu[c].data_ptr()),
+                                        C.c_void_p(wd[c].data_ptr()), HIDDEN, FFN, C.c_void_p(x35.data_ptr()),
+                                        C.c_void_p(gamma.data_ptr()), C.c_float(1e-6), C.c_void_p(s.data_ptr()),
+                                        C.c_void_p(x35.data_ptr()), C.c_void_p(h.data_ptr()), stream), "ffn block")
 
     ms = timed(ffn, n_iter=100)
     alg = 3 * q_bytes("q4k", FFN, HIDDEN) + 4 * (HIDDEN * 3 + FFN * 2)
     out["config2_ffn_block_q4k"] = {"GB/s": round(alg / (ms * 1e-3) / 1e9, 1),
                                     "frac_of_hbm": round(alg / (ms * 1e-3) / 1e9 / hbm_peak, 4),
-                                    "us": round(ms * 1e3, 2), "launches": 2}
+                                    "us": round(ms * 1e3, 2), "launches": 2, "api": "arcllm_cuda_ffn_block"}
     del wg, wu, wd
     torch.cuda.empty_cache()
     out.update(run_prefill_gemm(A, L, torch, dev, sp, timed, copies, make_w))

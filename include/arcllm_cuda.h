@@ -190,6 +190,17 @@ ARCLLM_CUDA_API int arcllm_cuda_shard_rows(uint32_t n, uint32_t align, uint32_t 
 ARCLLM_CUDA_API int arcllm_cuda_gateup_silu_q4k(const void *w_gate, const void *w_up, uint32_t rows, uint32_t k,
                                 const float *x, const float *gamma, float eps, float *s, void *stream);
 
+/* The decode FFN block (src/arcllm_v1_runtime.cpp:389-415: ffn_norm RMSNorm,
+ * the gate/up pair, SwiGLU, the down projection, the residual add):
+ *   s = silu(W_gate . xn) * (W_up . xn),  y = residual + W_down . s
+ * with xn = RMSNorm(x) * gamma; gate/up Q4_K (ffn x hidden), down Q4_K or
+ * Q6_K (hidden x ffn); residual may be null; s (ffn floats) is written too.
+ * Two launches on the stream: arcllm_cuda_gateup_silu_q4k, then
+ * arcllm_cuda_matvec of the down projection. */
+ARCLLM_CUDA_API int arcllm_cuda_ffn_block(int down_type, const void *w_gate, const void *w_up, const void *w_down,
+                                          uint32_t hidden, uint32_t ffn, const float *x, const float *gamma,
+                                          float eps, float *s, const float *residual, float *y, void *stream);
+
 /* EXEC148 image of n_blocks Q4_K super-blocks (src/q4_down_exec148_materializer.h:14,
  * shaders/b1_2_exec148_gpu_materialize.comp: acquisition path P1 on the GPU).
  * q4k 16-byte aligned, exec 4-byte aligned, exec holds 148 * n_blocks bytes. */
