@@ -29,12 +29,15 @@
 // zero-filled by the TMA unit and never stored.
 //
 // Reduction: the producer warp adds the consumer warps' row partials in warp
-// order and stores the CTA's slice partial to a per-device scratch; once its
-// rounds are done the CTA fences once and bumps a per-group arrival counter
-// for each of its row groups, and the CTA that delivers a group's last slice
-// adds the P slice partials in slice order -- deterministic whichever CTA
-// comes last -- applies bias / residual, writes y and re-arms the counter for
-// the next launch.
+// order and stores the CTA's slice partial to a per-device scratch as 64-bit
+// words tagged with the launch's tag (a device counter read after
+// griddepcontrol.wait and advanced by the launch's last CTA out).  Row group g
+// is closed by the CTA of slice g % P that owns it: its idle consumer warps
+// read the P slice words of each row until all carry the tag, add them in
+// slice order -- deterministic whichever slice came last -- apply bias /
+// residual and write y.  Every word is its own flag: no fence and no arrival
+// counter on the critical path (measured on B200, the fence + counter close
+// it replaces cost Q6_K 3584 x 18944 18.2 against 16.9 us).
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
