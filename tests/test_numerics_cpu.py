@@ -37,3 +37,25 @@ def test_prefill_attention_score_split_precision():
     # a single fp16 operand would be ~2^-11 off: the split is what keeps softmax sharp
     single = (q.astype(np.float16).astype(np.float64) @ k.astype(np.float64).T)
     assert np.abs(single - exact).max() > 2.0 ** -14 * mag.max()
+
+
+def test_prefill_attention_score_split_range_edges():
+    """Where the hi + lo split holds: up to the fp16 maximum (65504) the scores
+    keep the 2^-19 relative bound; past it hi overflows to inf, which the kernel
+    reports through the device error word's range bit instead of returning NaN
+    rows; for tiny |q * scale| the halves go subnormal and the error is bounded
+    by the fp16 subnormal spacing (2^-24) times sum |k| rather than relatively."""
+    rng = np.random.default_rng(11)
+    d = 128
+    k = (rng.standard_normal((32, d)) * 4.0).astype(np.float16)
+    big = (rng.uniform(-1, 1, (4, d)) * 6.0e4).astype(np.float32)  # just inside the fp16 range
+    exact = big.astype(np.float64) @ k.astype(np.float64).T
+    mag = np.abs(big.astype(np.float64)) @ np.abs(k.astype(np.float64)).T
+    assert np.abs(split_scores(big, k).astype(np.float64) - exact).max() <= 2.0 ** -19 * mag.max()
+    over = np.full((1, d), 7.0e4, np.float32)  # past 65504: hi is inf -- the condition the kernel flags
+    with np.errstate(over="ignore"):
+        assert np.isinf(over.astype(np.float16)).all()
+    tiny = (rng.standard_normal((4, d)) * 1e-6).astype(np.float32)
+    exact = tiny.astype(np.float64) @ k.astype(np.float64).T
+    err = np.abs(split_scores(tiny, k).astype(np.float64) - exact).max()
+    assert err <= 2.0 ** -24 * np.abs(k.astype(np.float64)).sum(axis=1).max()
