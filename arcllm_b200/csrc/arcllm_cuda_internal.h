@@ -90,6 +90,21 @@ struct RankGather {
     unsigned long long* ll[8];
     float* out;
 };
+// One job of matvec_imma_multi_launch: y = W . RMSNorm(x) (+ bias, RoPE / KV-store epilogue).
+struct ImmaJob {
+    int fmt;
+    const void* w;
+    uint32_t rows;
+    const float* bias;
+    float* y;
+    const RopeEpilogue* rope;
+};
+// The decode step's Q, K and V projections (same x, gamma and K) as ONE launch, each job on its
+// own CTAs; supported when every job takes the whole-row kernel with 32-row groups and all the
+// groups fit on the SMs at once.
+bool matvec_imma_multi_supported(const ImmaJob (&jobs)[3], uint32_t k);
+int matvec_imma_multi_launch(const ImmaJob (&jobs)[3], uint32_t k, const float* x, const float* gamma, float eps,
+                             cudaStream_t stream);
 int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
                        const float* gamma, float eps, const float* bias, const float* residual, float* y,
                        cudaStream_t stream, const RopeEpilogue* rope = nullptr, const RankGather* gather = nullptr);

@@ -54,7 +54,14 @@ struct MvParams {
     // K-slice kernel only: the first super-block of the K window this launch covers
     // (the matrix rows keep their full length rb; nb counts the window's blocks)
     uint32_t kb_base;
+    // several jobs in one launch (matvec_imma_multi_kernel): this job's CTAs are
+    // [cta0, cta0 + ncta) of the grid; ncta 0 = the whole grid
+    uint32_t cta0, ncta;
 };
+
+// This CTA's index within its job and the job's CTA count.
+__device__ __forceinline__ uint32_t job_cta(const MvParams& p) { return p.ncta ? blockIdx.x - p.cta0 : blockIdx.x; }
+__device__ __forceinline__ uint32_t job_ctas(const MvParams& p) { return p.ncta ? p.ncta : gridDim.x; }
 
 // Fold N per-row partial sums over the warp: afterwards lane L holds the full
 // sum of value index (L >> (5 - log2 N)).  One shuffle per value per step.

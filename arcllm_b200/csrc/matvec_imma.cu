@@ -64,7 +64,7 @@ __device__ __forceinline__ void finish_rows(const MvParams& p, const float* red,
                                             uint32_t lane) {
     constexpr int NV = DUAL ? 2 * G : G;
     const uint32_t S = p.stages, s = itr % S, par = (itr / S) & 1u;
-    const uint32_t grp = blockIdx.x + itr * gridDim.x;
+    const uint32_t grp = job_cta(p) + itr * job_ctas(p);
     const uint32_t rows_g = min(p.G, p.rows - grp * p.G);
     const float* rs = red + (par * S + s) * nwc * NV;
     for (uint32_t r = lane; (DUAL || p.rope_mode == 0) && r < rows_g; r += 32u) {
@@ -176,7 +176,7 @@ __device__ __forceinline__ void produce_and_finish(const MvParams& p, uint8_t* s
         }
         return true;
     };
-    for (uint32_t grp = blockIdx.x; grp < p.n_groups; grp += gridDim.x, ++it) {
+    for (uint32_t grp = job_cta(p); grp < p.n_groups; grp += job_ctas(p), ++it) {
         const uint32_t s = it % S;
         if (it >= S && !released(it - S)) {
             ok = false;
@@ -244,7 +244,7 @@ __device__ __forceinline__ void consume(const MvParams& p, const uint8_t* stages
     const bool oddA = FMT == 14 && (offA & 3u) != 0u;
 
     uint32_t it = 0;
-    for (uint32_t grp = blockIdx.x; grp < p.n_groups; grp += gridDim.x, ++it) {
+    for (uint32_t grp = job_cta(p); grp < p.n_groups; grp += job_ctas(p), ++it) {
         const uint32_t s = it % S;
         if (!mbar_wait(&full[s], (it / S) & 1u, p.err)) *abort_flag = 1;
         if (*abort_flag) break;
@@ -290,8 +290,10 @@ __device__ __forceinline__ void consume(const MvParams& p, const uint8_t* stages
     }
 }
 
+// One CTA of a whole-row matvec: barriers, then the producer warp and the
+// consumer warps (and, with n_ranks, the all-gather collect).
 template <int FMT, int MT, bool DUAL>
-__global__ void __launch_bounds__(15 * 32, 1) matvec_imma_kernel(const MvParams p, uint32_t nwc) {
+__device__ __forceinline__ void imma_cta(const MvParams& p, uint32_t nwc) {
     constexpr int G = 16 * MT;
     constexpr int NV = DUAL ? 2 * G : G;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -331,6 +333,34 @@ __global__ void __launch_bounds__(15 * 32, 1) matvec_imma_kernel(const MvParams 
             if (!*abort_flag) gather_collect(p);
         }
     }
+}
+
+template <int FMT, int MT, bool DUAL>
+__global__ void __launch_bounds__(15 * 32, 1) matvec_imma_kernel(const MvParams p, uint32_t nwc) {
+    imma_cta<FMT, MT, DUAL>(p, nwc);
+}
+
+// Up to three independent single-matrix jobs with the same K in one launch
+// (the decode step's Q, K and V projections: they read the same x, and one
+// grid lets the next kernel follow with programmatic dependent launch instead
+// of after a join of streams).  Job j owns CTAs [pj.cta0, pj.cta0 + pj.ncta);
+// fj is its format (12 Q4_K, 14 Q6_K).
+__device__ __forceinline__ void imma_job(const MvParams& p, int f, uint32_t nwc) {
+    if (f == 12)
+        imma_cta<12, 2, false>(p, nwc);
+    else
+        imma_cta<14, 2, false>(p, nwc);
+}
+
+__global__ void __launch_bounds__(15 * 32, 1)
+    matvec_imma_multi_kernel(const MvParams p0, const MvParams p1, const MvParams p2, int f0, int f1, int f2,
+                             uint32_t nwc) {
+    if (blockIdx.x < p1.cta0)
+        imma_job(p0, f0, nwc);
+    else if (blockIdx.x < p2.cta0)
+        imma_job(p1, f1, nwc);
+    else
+        imma_job(p2, f2, nwc);
 }
 
 template <int FMT, int MT, bool DUAL>
@@ -390,6 +420,8 @@ int matvec_imma_prepare() {
     if (e == cudaSuccess) e = set_attr_imma<12, 2, true>();
     if (e == cudaSuccess) e = set_attr_imma<14, 1, false>();
     if (e == cudaSuccess) e = set_attr_imma<14, 2, false>();
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(matvec_imma_multi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return set_cuda_error(e, "matvec_imma prepare");
     done[dev & 63] = true;
     return ARC_OK;
@@ -407,19 +439,17 @@ bool matvec_imma_supported(int fmt, bool dual, uint32_t rows, uint32_t k) {
     return imma_config(fmt, dual, k).smem <= 227u * 1024u;
 }
 
-int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
-                       const float* gamma, float eps, const float* bias, const float* residual, float* y,
-                       cudaStream_t stream, const RopeEpilogue* rope, const RankGather* gather) {
-    if (!matvec_imma_supported(fmt, dual, rows, k))
-        return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec_imma: shape outside K/256 <= 14 (even for Q6_K)");
+namespace {
+// Parameters of one whole-row launch (matvec_imma_supported already checked).
+int imma_params(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
+                const float* gamma, float eps, const float* bias, const float* residual, float* y,
+                const RopeEpilogue* rope, const RankGather* gather, MvParams& p, ImmaConfig& c) {
     if (!w0 || !x || !y || (dual && !w1)) return set_error(ARC_E_INVALID_ARGUMENT, "matvec: null pointer");
     if ((reinterpret_cast<uintptr_t>(w0) & 15u) || (w1 && (reinterpret_cast<uintptr_t>(w1) & 15u)))
         return set_error(ARC_E_ALIGNMENT, "matvec: weight pointers must be 16-byte aligned");
-    int st = matvec_imma_prepare();
-    if (st != ARC_OK) return st;
-    const ImmaConfig c = imma_config(fmt, dual, k);
+    c = imma_config(fmt, dual, k);
     const uint32_t nb = k / 256u;
-    MvParams p{};
+    p = MvParams{};
     p.w0 = static_cast<const uint8_t*>(w0);
     p.w1 = static_cast<const uint8_t*>(w1);
     p.x = x;
@@ -468,12 +498,32 @@ int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint3
         p.gather_row0 = gather->row0;
         p.gather_rows_total = gather->rows_total;
     }
+    return ARC_OK;
+}
+
+uint32_t imma_sm_count() {
     static int sm_count[64] = {};  // per device, queried once
     int dev = 0;
     cudaGetDevice(&dev);
     int& sms = sm_count[dev & 63];
     if (sms <= 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
-    const uint32_t grid = std::min(p.n_groups, (uint32_t)sms);
+    return (uint32_t)sms;
+}
+}  // namespace
+
+int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint32_t rows, uint32_t k, const float* x,
+                       const float* gamma, float eps, const float* bias, const float* residual, float* y,
+                       cudaStream_t stream, const RopeEpilogue* rope, const RankGather* gather) {
+    if (!matvec_imma_supported(fmt, dual, rows, k))
+        return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec_imma: shape outside K/256 <= 14 (even for Q6_K)");
+    int st = matvec_imma_prepare();
+    if (st != ARC_OK) return st;
+    MvParams p;
+    ImmaConfig c;
+    st = imma_params(fmt, dual, w0, w1, rows, k, x, gamma, eps, bias, residual, y, rope, gather, p, c);
+    if (st != ARC_OK) return st;
+    const uint32_t nb = k / 256u;
+    const uint32_t grid = std::min(p.n_groups, imma_sm_count());
     cudaError_t e;
     if (fmt == 12) {
         if (dual)
@@ -487,6 +537,46 @@ int matvec_imma_launch(int fmt, bool dual, const void* w0, const void* w1, uint3
                       : launch_imma_t<14, 1, false>(p, nb, c.smem, grid, stream);
     }
     if (e != cudaSuccess) return set_cuda_error(e, "matvec_imma launch");
+    return ARC_OK;
+}
+
+// Three whole-row jobs sharing x, gamma and K in one grid (matvec_imma_multi_kernel): each
+// job gets one CTA per row group, so all groups of all jobs must fit on the SMs at once and
+// every job must use 32-row groups.
+bool matvec_imma_multi_supported(const ImmaJob (&jobs)[3], uint32_t k) {
+    uint32_t ctas = 0;
+    for (const ImmaJob& j : jobs) {
+        if (!matvec_imma_supported(j.fmt, false, j.rows, k)) return false;
+        const ImmaConfig c = imma_config(j.fmt, false, k);
+        if (c.MT != 2) return false;
+        ctas += (j.rows + c.G - 1u) / c.G;
+    }
+    return ctas <= imma_sm_count();
+}
+
+int matvec_imma_multi_launch(const ImmaJob (&jobs)[3], uint32_t k, const float* x, const float* gamma, float eps,
+                             cudaStream_t stream) {
+    if (!matvec_imma_multi_supported(jobs, k))
+        return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec_imma multi: jobs do not fit one grid");
+    int st = matvec_imma_prepare();
+    if (st != ARC_OK) return st;
+    MvParams p[3];
+    uint32_t cta = 0, smem = 0;
+    for (int i = 0; i < 3; ++i) {
+        const ImmaJob& j = jobs[i];
+        ImmaConfig c;
+        st = imma_params(j.fmt, false, j.w, nullptr, j.rows, k, x, gamma, eps, j.bias, nullptr, j.y, j.rope, nullptr,
+                         p[i], c);
+        if (st != ARC_OK) return st;
+        p[i].cta0 = cta;
+        p[i].ncta = p[i].n_groups;
+        cta += p[i].ncta;
+        smem = std::max(smem, c.smem);
+    }
+    const uint32_t nwc = k / 256u;  // one consumer warp per super-block, plus the producer warp
+    const cudaError_t e = launch_kernel(matvec_imma_multi_kernel, dim3(cta), dim3((nwc + 1) * 32), smem, stream, p[0],
+                                        p[1], p[2], jobs[0].fmt, jobs[1].fmt, jobs[2].fmt, nwc);
+    if (e != cudaSuccess) return set_cuda_error(e, "matvec_imma multi launch");
     return ARC_OK;
 }
 

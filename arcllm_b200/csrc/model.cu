@@ -135,6 +135,16 @@ bool fuse_rope_ok(const arcllm_cuda_model* m, const arcllm_cuda_layer& L) {
            matvec_imma_supported(L.type_v, false, KV, H);
 }
 
+// Q, K and V as one launch (matvec_imma_multi_launch) where it applies; ARCLLM_QKV_ONE_LAUNCH=0
+// keeps three launches, K and V on side streams.
+bool qkv_one_launch() {
+    static const bool on = [] {
+        const char* e = std::getenv("ARCLLM_QKV_ONE_LAUNCH");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 // Enqueue one token step; `with_head` adds output norm + LM head + argmax.
 int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t* n_launch) {
     const arcllm_cuda_model_config& c = m->cfg;
@@ -146,10 +156,6 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
     float* hm = m->h1;
     for (uint32_t l = 0; l < c.n_layers; ++l) {
         const arcllm_cuda_layer& L = m->layers[l];
-        // Q, K and V read the same input: K and V go to side streams so the three
-        // matvecs (112 + 16 + 16 CTAs at the Qwen2.5-7B shape) share the GPU
-        ARC_TRY(launch_checked(cudaEventRecord(m->ev_fork, st), "fork"));
-        for (int i = 0; i < 2; ++i) ARC_TRY(launch_checked(cudaStreamWaitEvent(m->side[i], m->ev_fork, 0), "fork"));
         // RoPE and the fp16 KV store ride in the Q/K/V matvec epilogues when the whole-row
         // integer-MMA kernel takes all three (ARCLLM_FUSE_ROPE=0 keeps the separate kernel)
         const bool fuse = fuse_rope_ok(m, L);
@@ -158,37 +164,54 @@ int enqueue_step(arcllm_cuda_model* m, bool with_head, cudaStream_t st, uint32_t
         const RopeEpilogue rq{1u, half, c.max_ctx, m->rope, &m->state->pos, nullptr};
         const RopeEpilogue rk{2u, half, c.max_ctx, m->rope, &m->state->pos, m->kc + lcache};
         const RopeEpilogue rv{3u, half, c.max_ctx, m->rope, &m->state->pos, m->vc + lcache};
-        if (fuse)
-            ARC_TRY(matvec_imma_launch(L.type_q, false, L.wq, nullptr, H, H, hc, L.attn_norm, c.rms_eps, L.bq, nullptr,
-                                       m->q, st, &rq));
-        else
-            ARC_TRY(mv(L.type_q, L.wq, H, H, hc, L.attn_norm, c.rms_eps, L.bq, nullptr, m->q, st));
-        {
-            PdlScope plain(false);  // a side stream's predecessor is an event, not a kernel
-            if (fuse) {
-                ARC_TRY(matvec_imma_launch(L.type_k, false, L.wk, nullptr, KV, H, hc, L.attn_norm, c.rms_eps, L.bk,
-                                           nullptr, m->k, m->side[0], &rk));
-                ARC_TRY(matvec_imma_launch(L.type_v, false, L.wv, nullptr, KV, H, hc, L.attn_norm, c.rms_eps, L.bv,
-                                           nullptr, m->v, m->side[1], &rv));
-            } else {
-                ARC_TRY(mv(L.type_k, L.wk, KV, H, hc, L.attn_norm, c.rms_eps, L.bk, nullptr, m->k, m->side[0]));
-                ARC_TRY(mv(L.type_v, L.wv, KV, H, hc, L.attn_norm, c.rms_eps, L.bv, nullptr, m->v, m->side[1]));
+        const ImmaJob qkv[3] = {{L.type_q, L.wq, H, L.bq, m->q, &rq},
+                                {L.type_k, L.wk, KV, L.bk, m->k, &rk},
+                                {L.type_v, L.wv, KV, L.bv, m->v, &rv}};
+        if (fuse && qkv_one_launch() && matvec_imma_multi_supported(qkv, H)) {
+            // Q, K and V read the same input: one grid (112 + 16 + 16 CTAs at the Qwen2.5-7B
+            // shape), so the attention follows it with programmatic dependent launch
+            ARC_TRY(matvec_imma_multi_launch(qkv, H, hc, L.attn_norm, c.rms_eps, st));
+            n += 1;
+        } else {
+            // otherwise K and V go to side streams so the three matvecs share the GPU
+            ARC_TRY(launch_checked(cudaEventRecord(m->ev_fork, st), "fork"));
+            for (int i = 0; i < 2; ++i)
+                ARC_TRY(launch_checked(cudaStreamWaitEvent(m->side[i], m->ev_fork, 0), "fork"));
+            if (fuse)
+                ARC_TRY(matvec_imma_launch(L.type_q, false, L.wq, nullptr, H, H, hc, L.attn_norm, c.rms_eps, L.bq,
+                                           nullptr, m->q, st, &rq));
+            else
+                ARC_TRY(mv(L.type_q, L.wq, H, H, hc, L.attn_norm, c.rms_eps, L.bq, nullptr, m->q, st));
+            {
+                PdlScope plain(false);  // a side stream's predecessor is an event, not a kernel
+                if (fuse) {
+                    ARC_TRY(matvec_imma_launch(L.type_k, false, L.wk, nullptr, KV, H, hc, L.attn_norm, c.rms_eps,
+                                               L.bk, nullptr, m->k, m->side[0], &rk));
+                    ARC_TRY(matvec_imma_launch(L.type_v, false, L.wv, nullptr, KV, H, hc, L.attn_norm, c.rms_eps,
+                                               L.bv, nullptr, m->v, m->side[1], &rv));
+                } else {
+                    ARC_TRY(mv(L.type_k, L.wk, KV, H, hc, L.attn_norm, c.rms_eps, L.bk, nullptr, m->k,
+                               m->side[0]));
+                    ARC_TRY(mv(L.type_v, L.wv, KV, H, hc, L.attn_norm, c.rms_eps, L.bv, nullptr, m->v,
+                               m->side[1]));
+                }
             }
-        }
-        for (int i = 0; i < 2; ++i) {
-            ARC_TRY(launch_checked(cudaEventRecord(m->ev_join[i], m->side[i]), "join"));
-            ARC_TRY(launch_checked(cudaStreamWaitEvent(st, m->ev_join[i], 0), "join"));
-        }
-        if (!fuse) {
-            RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
-            ARC_TRY(launch_rope_kv_store(m->q, m->k, m->v, m->rope, &m->state->pos, m->kc, m->vc, rs, st));
-            ++n;
+            for (int i = 0; i < 2; ++i) {
+                ARC_TRY(launch_checked(cudaEventRecord(m->ev_join[i], m->side[i]), "join"));
+                ARC_TRY(launch_checked(cudaStreamWaitEvent(st, m->ev_join[i], 0), "join"));
+            }
+            if (!fuse) {
+                RopeKvShape rs{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l};
+                ARC_TRY(launch_rope_kv_store(m->q, m->k, m->v, m->rope, &m->state->pos, m->kc, m->vc, rs, st));
+                ++n;
+            }
+            n += 3;
         }
         AttnShape as{c.n_heads, c.n_kv_heads, c.head_dim, c.max_ctx, l, m->attn_splits,
                      1.0f / std::sqrt((float)c.head_dim)};
         ARC_TRY(launch_attention(m->q, m->kc, m->vc, &m->state->pos, as, m->part, m->attn, st));
         ARC_TRY(mv(L.type_o, L.wo, H, H, m->attn, nullptr, 0.f, nullptr, hc, hm, st));
-        n += 4 + (uint32_t)attention_launches(m->attn_splits, c.n_heads, c.n_kv_heads);  // Q K V (attn) O
+        n += 1 + (uint32_t)attention_launches(m->attn_splits, c.n_heads, c.n_kv_heads);  // (attn) O
         if (m->tp.n_ranks > 1) {
             // this rank's gate/up rows -> its slice of s; the FFN down over the same K window
             // (every output row, this slice's super-blocks) -> partial sums; the ranks' partials
