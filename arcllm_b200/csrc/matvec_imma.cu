@@ -345,22 +345,26 @@ __global__ void __launch_bounds__(15 * 32, 1) matvec_imma_kernel(const MvParams 
 // grid lets the next kernel follow with programmatic dependent launch instead
 // of after a join of streams).  Job j owns CTAs [pj.cta0, pj.cta0 + pj.ncta);
 // fj is its format (12 Q4_K, 14 Q6_K).
-__device__ __forceinline__ void imma_job(const MvParams& p, int f, uint32_t nwc) {
-    if (f == 12)
-        imma_cta<12, 2, false>(p, nwc);
-    else
-        imma_cta<14, 2, false>(p, nwc);
-}
+// Dynamic shared memory of the multi-job kernel: 227 KB less room for its static copy of a job's parameters.
+constexpr uint32_t kMultiMaxDynSmem = 227u * 1024u - 1024u;
 
+// The CTA copies its job's parameters into shared memory first, so the kernel
+// holds one body per format instead of one per (job, format): each CTA runs
+// its code once, and a smaller kernel means fewer cold instruction fetches.
 __global__ void __launch_bounds__(15 * 32, 1)
-    matvec_imma_multi_kernel(const MvParams p0, const MvParams p1, const MvParams p2, int f0, int f1, int f2,
-                             uint32_t nwc) {
-    if (blockIdx.x < p1.cta0)
-        imma_job(p0, f0, nwc);
-    else if (blockIdx.x < p2.cta0)
-        imma_job(p1, f1, nwc);
+    matvec_imma_multi_kernel(const __grid_constant__ MvParams p0, const __grid_constant__ MvParams p1,
+                             const __grid_constant__ MvParams p2, int f0, int f1, int f2, uint32_t nwc) {
+    __shared__ __align__(16) MvParams sp;
+    static_assert(sizeof(MvParams) % 4 == 0, "copied as words");
+    const uint32_t job = blockIdx.x < p1.cta0 ? 0u : blockIdx.x < p2.cta0 ? 1u : 2u;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(job == 0 ? &p0 : job == 1 ? &p1 : &p2);
+    for (uint32_t i = threadIdx.x; i < sizeof(MvParams) / 4; i += blockDim.x)
+        reinterpret_cast<uint32_t*>(&sp)[i] = src[i];
+    __syncthreads();
+    if ((job == 0 ? f0 : job == 1 ? f1 : f2) == 12)
+        imma_cta<12, 2, false>(sp, nwc);
     else
-        imma_job(p2, f2, nwc);
+        imma_cta<14, 2, false>(sp, nwc);
 }
 
 template <int FMT, int MT, bool DUAL>
@@ -421,7 +425,8 @@ int matvec_imma_prepare() {
     if (e == cudaSuccess) e = set_attr_imma<14, 1, false>();
     if (e == cudaSuccess) e = set_attr_imma<14, 2, false>();
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(matvec_imma_multi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        e = cudaFuncSetAttribute(matvec_imma_multi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kMultiMaxDynSmem);
     if (e != cudaSuccess) return set_cuda_error(e, "matvec_imma prepare");
     done[dev & 63] = true;
     return ARC_OK;
@@ -548,7 +553,8 @@ bool matvec_imma_multi_supported(const ImmaJob (&jobs)[3], uint32_t k) {
     for (const ImmaJob& j : jobs) {
         if (!matvec_imma_supported(j.fmt, false, j.rows, k)) return false;
         const ImmaConfig c = imma_config(j.fmt, false, k);
-        if (c.MT != 2) return false;
+        // 32-row groups; the job's shared memory plus the kernel's copy of its parameters fits
+        if (c.MT != 2 || c.smem > kMultiMaxDynSmem) return false;
         ctas += (j.rows + c.G - 1u) / c.G;
     }
     return ctas <= imma_sm_count();
