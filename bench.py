@@ -89,11 +89,26 @@ class ClockSampler:
             self.proc = subprocess.Popen(cmd, stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        # nvidia-smi can take a while to start on a many-GPU box: wait (bounded) for its first sample,
+        # so the samples bracket the timed region however short it is
+        t0 = time.time()
+        while self._lines() == 0 and self.proc.poll() is None and time.time() - t0 < 5.0:
+            time.sleep(0.02)
+
+    def _lines(self):
+        try:
+            with open(self.f.name) as g:
+                return sum(1 for ln in g if ln.strip())
+        except OSError:
+            return 0
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        time.sleep(0.06)
+        n0, t0 = self._lines(), time.time()  # one more sample after the timed region (bounded)
+        while self._lines() <= n0 and self.proc.poll() is None and time.time() - t0 < 1.0:
+            time.sleep(0.02)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
