@@ -43,6 +43,9 @@ SIGNATURES = {
     "arcllm_cuda_gateup_silu_q4k": [_vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp],
     "arcllm_cuda_ffn_block": [_i32, _vp, _vp, _vp, _u32, _u32, _vp, _vp, _f32, _vp, _vp, _vp, _vp],
     "arcllm_cuda_gemm_q4k_bf16": [_vp, _u32, _u32, _vp, _u32, _vp, _vp],
+    "arcllm_cuda_gemm_allgather_buffer_bytes": [_u32, _u32, C.POINTER(_u64)],
+    "arcllm_cuda_gemm_bf16_allgather": [_i32, _vp, _u32, _u32, _vp, _u32, _u32, _u32, C.POINTER(_vp), _u32, _u32,
+                                        _u32, _u32, _vp],
     "arcllm_cuda_gemm_bf16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],
     "arcllm_cuda_gemm_f16": [_i32, _vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp],
     "arcllm_cuda_gemm_f16x3": [_i32, _vp, _u32, _u32, _vp, _vp, _u32, _vp, _vp, _vp],

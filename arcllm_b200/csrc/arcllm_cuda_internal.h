@@ -172,6 +172,13 @@ int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint
 // 2: fp16 hi + lo of both, y = (x + x_lo)(W_hi + W_lo)^T without the lo*lo term.
 int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
                  const float* residual, float* y, cudaStream_t stream, int mode = 0, const uint16_t* x_lo = nullptr);
+// Output-row-sharded GEMM with the result all-gathered by its reduce kernel over NVLink peer stores:
+// this rank's columns [c0, c0 + n) of an m x n_total result into every rank's buffer (rank_bufs,
+// gemm_gather_flags_offset(m, n_total) + 128 bytes each, zeroed before first use), then a flag handshake.
+uint64_t gemm_gather_flags_offset(uint32_t m, uint32_t n_total);
+int gemm_kq_allgather(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, uint32_t c0,
+                      uint32_t n_total, void* const* rank_bufs, uint32_t n_ranks, uint32_t rank, uint32_t epoch,
+                      uint32_t timeout_us, cudaStream_t stream);
 
 std::vector<float> rope_table(uint32_t max_ctx, uint32_t head_dim, float theta);
 int model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out);

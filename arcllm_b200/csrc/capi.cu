@@ -324,6 +324,25 @@ int arcllm_cuda_gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint1
     ARC_GUARD_END
 }
 
+int arcllm_cuda_gemm_allgather_buffer_bytes(uint32_t m, uint32_t n_total, uint64_t* out) {
+    ARC_GUARD_BEGIN
+    if (!out || m == 0 || n_total == 0)
+        return set_error(ARC_E_INVALID_ARGUMENT, "gemm_allgather_buffer_bytes: bad argument");
+    *out = arc::gemm_gather_flags_offset(m, n_total) + 128u;
+    return ARC_OK;
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_gemm_bf16_allgather(int type, const void* w, uint32_t n, uint32_t k, const uint16_t* x_bf16,
+                                    uint32_t m, uint32_t c0, uint32_t n_total, void* const* rank_bufs,
+                                    uint32_t n_ranks, uint32_t rank, uint32_t epoch, uint32_t timeout_us,
+                                    void* stream) {
+    ARC_GUARD_BEGIN
+    return arc::gemm_kq_allgather(type, w, n, k, x_bf16, m, c0, n_total, rank_bufs, n_ranks, rank, epoch, timeout_us,
+                                  static_cast<cudaStream_t>(stream));
+    ARC_GUARD_END
+}
+
 int arcllm_cuda_gemm_bf16(int type, const void* w, uint32_t n, uint32_t k, const uint16_t* x_bf16, uint32_t m,
                           const float* residual, float* y, void* stream) {
     ARC_GUARD_BEGIN

@@ -646,6 +646,49 @@ __global__ void __launch_bounds__(256) gemm_splitk_reduce_kernel(const float4* _
     }
 }
 
+// The same reduce, the output rows of this rank's shard (columns [c0, c0 + n) of an
+// m x n_total result) stored into EVERY rank's result -- local stores for its own,
+// NVLink peer stores for the others, float4 by float4, nothing read from a peer --
+// then the ranks' flag handshake (rank_flag_handshake) run by the warp of the CTA
+// that completes the counter: when the launch ends on rank r, y[r] holds all
+// n_total columns.  The fused form of GEMM + all-gather for output-row-sharded
+// prefill projections.
+struct GemmGather {
+    float* y[8];           // rank q's m x n_total result, as this process maps it
+    uint32_t* flags[8];    // rank q's flag array
+    uint32_t* ctr;         // this rank's CTA counter (zero between launches)
+    uint32_t n_ranks, rank, epoch, c0, n_total;
+    unsigned long long wait_ns;
+};
+
+__global__ void __launch_bounds__(256) gemm_reduce_gather_kernel(const float4* __restrict__ ws, uint32_t ks,
+                                                                 uint32_t n4_row, uint64_t n4,
+                                                                 const GemmGather g, unsigned int* err) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (uint32_t sp = 0; sp < ks; ++sp) {
+            const float4 v = ws[(uint64_t)sp * n4 + i];
+            t.x += v.x, t.y += v.y, t.z += v.z, t.w += v.w;
+        }
+        const uint64_t row = i / n4_row, c4 = i - row * n4_row;
+        const uint64_t off = (row * g.n_total + g.c0) / 4u + c4;  // float4 index in every rank's result
+#pragma unroll
+        for (uint32_t q = 0; q < 8; ++q)
+            if (q < g.n_ranks) reinterpret_cast<float4*>(g.y[q])[off] = t;
+    }
+    __threadfence_system();  // this thread's (peer) stores before the CTA's count
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        uint32_t last = 0;
+        if (threadIdx.x == 0) last = atomicAdd(g.ctr, 1u) == gridDim.x - 1u ? 1u : 0u;
+        if (__shfl_sync(0xffffffffu, last, 0)) {
+            if (threadIdx.x == 0) *g.ctr = 0u;  // re-armed for the next launch in stream order
+            rank_flag_handshake(g.flags, g.n_ranks, g.rank, g.epoch, g.wait_ns, err);
+        }
+    }
+}
+
 struct GemmScratch {
     float* ws = nullptr;
     size_t ws_floats = 0;
@@ -717,11 +760,14 @@ int encode_x_map(EncodeTiledFn enc, const uint16_t* x, uint32_t k, uint32_t m, b
 }
 }  // namespace
 
-int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
-                 const float* residual, float* y, cudaStream_t stream, int mode, const uint16_t* x_lo) {
+namespace {
+int gemm_kq_impl(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
+                 const float* residual, float* y, cudaStream_t stream, int mode, const uint16_t* x_lo,
+                 const GemmGather* gather) {
     if (fmt != 12 && fmt != 14) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: weights must be Q4_K or Q6_K");
     if (mode < 0 || mode > 2) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: operand mode 0 (bf16), 1 or 2 (fp16)");
-    if (!w || !x || !y || (mode == 2 && !x_lo)) return set_error(ARC_E_INVALID_ARGUMENT, "gemm: null pointer");
+    if (!w || !x || (!y && !gather) || (mode == 2 && !x_lo))
+        return set_error(ARC_E_INVALID_ARGUMENT, "gemm: null pointer");
     if (m == 0 || m > 256 || n == 0 || n % kBN || k == 0 || k % 256u)
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "gemm: needs 1 <= M <= 256, N % 128 == 0, K % 256 == 0");
     if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
@@ -748,9 +794,10 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
         if (f >= 1u && f <= k / 256u) ks = f;
     }
     SplitKWs sk{nullptr, ks};
-    if (ks > 1) {
+    if (ks > 1 || gather) {  // the gather form always reduces out of the scratch (one split: a copy)
         st = gemm_splitk_reserve((size_t)ks * m * n, &sk.ws);
         if (st != ARC_OK) return st;
+        if (ks == 1) y = sk.ws;  // the single split's tile lands in the scratch
     }
     const uint8_t* wb = static_cast<const uint8_t*>(w);
     const dim3 grid(tiles, ks), block(kThreads);
@@ -764,7 +811,12 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
     else
         e = mode == 0 ? ARC_GEMM_LAUNCH(14, 0) : mode == 1 ? ARC_GEMM_LAUNCH(14, 1) : ARC_GEMM_LAUNCH(14, 2);
 #undef ARC_GEMM_LAUNCH
-    if (e == cudaSuccess && ks > 1) {
+    if (e == cudaSuccess && gather) {
+        const uint64_t n4 = (uint64_t)m * n / 4u;
+        const uint32_t blocks = (uint32_t)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)sms * 8u);
+        e = launch_kernel(gemm_reduce_gather_kernel, dim3(blocks), dim3(256), 0, stream,
+                          reinterpret_cast<const float4*>(sk.ws), ks, n / 4u, n4, *gather, err);
+    } else if (e == cudaSuccess && ks > 1) {
         const uint64_t n4 = (uint64_t)m * n / 4u;
         const uint32_t blocks = (uint32_t)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)sms * 8u);
         e = launch_kernel(gemm_splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream,
@@ -772,6 +824,43 @@ int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t*
                           reinterpret_cast<float4*>(y));
     }
     return e == cudaSuccess ? ARC_OK : set_cuda_error(e, "gemm launch");
+}
+}  // namespace
+
+int gemm_kq_bf16(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m,
+                 const float* residual, float* y, cudaStream_t stream, int mode, const uint16_t* x_lo) {
+    return gemm_kq_impl(fmt, w, n, k, x, m, residual, y, stream, mode, x_lo, nullptr);
+}
+
+// Exchange buffer of one rank for the gathered GEMM: the m x n_total fp32 result at 0, then at a
+// 256-byte boundary the flag array (8 u32) and, 64 bytes further, the CTA counter.
+uint64_t gemm_gather_flags_offset(uint32_t m, uint32_t n_total) {
+    return ((uint64_t)m * n_total * 4u + 255u) & ~uint64_t(255);
+}
+
+int gemm_kq_allgather(int fmt, const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, uint32_t c0,
+                      uint32_t n_total, void* const* rank_bufs, uint32_t n_ranks, uint32_t rank, uint32_t epoch,
+                      uint32_t timeout_us, cudaStream_t stream) {
+    if (!rank_bufs || n_ranks == 0 || n_ranks > 8 || rank >= n_ranks || epoch == 0 || (uint64_t)c0 + n > n_total ||
+        c0 % 4u || n_total % 4u)
+        return set_error(ARC_E_INVALID_ARGUMENT, "gemm all-gather: bad rank layout, columns or epoch");
+    GemmGather g{};
+    const uint64_t fo = gemm_gather_flags_offset(m, n_total);
+    for (uint32_t q = 0; q < n_ranks; ++q) {
+        if (!rank_bufs[q] || (reinterpret_cast<uintptr_t>(rank_bufs[q]) & 255u))
+            return set_error(ARC_E_ALIGNMENT, "gemm all-gather: rank buffers must be 256-byte aligned");
+        uint8_t* b = static_cast<uint8_t*>(rank_bufs[q]);
+        g.y[q] = reinterpret_cast<float*>(b);
+        g.flags[q] = reinterpret_cast<uint32_t*>(b + fo);
+    }
+    g.ctr = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(rank_bufs[rank]) + fo + 64u);
+    g.n_ranks = n_ranks;
+    g.rank = rank;
+    g.epoch = epoch;
+    g.c0 = c0;
+    g.n_total = n_total;
+    g.wait_ns = 1000ull * (timeout_us ? timeout_us : 2000000u);
+    return gemm_kq_impl(fmt, w, n, k, x, m, nullptr, nullptr, stream, 0, nullptr, &g);
 }
 
 int gemm_q4k_bf16(const void* w, uint32_t n, uint32_t k, const uint16_t* x, uint32_t m, float* y,

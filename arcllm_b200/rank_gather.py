@@ -23,28 +23,16 @@ from . import GGML_Q6_K, call, lib
 HANDLE_BYTES = 64  # cudaIpcMemHandle_t
 
 
-class RankGather:
-    """Exchange buffers of `n_ranks` ranks for a `rows_total`-row result.
+class _ParityBuffers:
+    """Two exchange buffers of `nbytes` per rank (one per epoch parity),
+    zero-filled, shared with the other ranks through CUDA IPC handles
+    (`exchange`: the caller's host all-gather of bytes) and mapped in this
+    process; `_bufs[b]` is the rank-ordered array of device addresses of set b."""
 
-    exchange(handle_bytes) -> list of every rank's handle bytes, in rank order
-    (the caller's host all-gather).  After construction, `step()` launches one
-    all-gather matvec and `logits_ptr` holds all rows once it completes.
-
-    Two buffers alternate by epoch parity: a peer that is already running the
-    next launch stores into the other buffer, and it cannot get two launches
-    ahead, because its launch completes only after this rank's next launch --
-    stream-ordered after this rank's reads of the current logits -- has
-    stored its rows.
-    """
-
-    def __init__(self, rows_total, n_ranks, rank, exchange, timeout_us=2000000):
+    def _setup_buffers(self, nbytes, n_ranks, rank, exchange, what):
         if not (1 <= n_ranks <= 8 and 0 <= rank < n_ranks):
-            raise ValueError("RankGather: 1 <= n_ranks <= 8 and 0 <= rank < n_ranks")
-        L = lib()
-        self.rows_total, self.n_ranks, self.rank, self.timeout_us = rows_total, n_ranks, rank, timeout_us
-        n = C.c_uint64(0)
-        call("arcllm_cuda_allgather_buffer_bytes", rows_total, C.byref(n))
-        self.nbytes = n.value
+            raise ValueError("%s: 1 <= n_ranks <= 8 and 0 <= rank < n_ranks" % what)
+        self.nbytes, self.n_ranks, self.rank = nbytes, n_ranks, rank
         self._own, self._opened, self._bufs = [], [], []
         zeros = (C.c_uint8 * self.nbytes)()
         handles = []
@@ -59,7 +47,7 @@ class RankGather:
         call("arcllm_cuda_stream_synchronize", None)
         everyone = exchange(handles[0] + handles[1])
         if len(everyone) != n_ranks:
-            raise RuntimeError("RankGather: exchange returned %d entries for %d ranks" % (len(everyone), n_ranks))
+            raise RuntimeError("%s: exchange returned %d entries for %d ranks" % (what, len(everyone), n_ranks))
         for b in range(2):
             ptrs = []
             for r, hb in enumerate(everyone):
@@ -73,6 +61,40 @@ class RankGather:
                 self._opened.append(p)
                 ptrs.append(p.value)
             self._bufs.append((C.c_void_p * n_ranks)(*ptrs))
+        self.epoch = 0
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's.  Call only after every
+        rank has finished its last step (a host barrier), so no peer still
+        stores into this buffer."""
+        for p in self._opened:
+            call("arcllm_cuda_ipc_close_handle", p)
+        self._opened = []
+        for own in self._own:
+            call("arcllm_cuda_free", own)
+        self._own = []
+
+
+class RankGather(_ParityBuffers):
+    """Exchange buffers of `n_ranks` ranks for a `rows_total`-row result.
+
+    exchange(handle_bytes) -> list of every rank's handle bytes, in rank order
+    (the caller's host all-gather).  After construction, `step()` launches one
+    all-gather matvec and `logits_ptr` holds all rows once it completes.
+
+    Two buffers alternate by epoch parity: a peer that is already running the
+    next launch stores into the other buffer, and it cannot get two launches
+    ahead, because its launch completes only after this rank's next launch --
+    stream-ordered after this rank's reads of the current logits -- has
+    stored its rows.
+    """
+
+    def __init__(self, rows_total, n_ranks, rank, exchange, timeout_us=2000000):
+        L = lib()
+        self.rows_total, self.timeout_us = rows_total, timeout_us
+        n = C.c_uint64(0)
+        call("arcllm_cuda_allgather_buffer_bytes", rows_total, C.byref(n))
+        self._setup_buffers(n.value, n_ranks, rank, exchange, "RankGather")
         off = C.c_uint64(0)
         call("arcllm_cuda_allgather_logits_offset", rows_total, C.byref(off))
         self._logits_off = off.value
@@ -95,16 +117,31 @@ class RankGather:
             from . import check
             check(st, "matvec_allgather")
 
-    def close(self):
-        """Unmap the peers' buffers and free this rank's.  Call only after every
-        rank has finished its last step (a host barrier), so no peer still
-        stores into this buffer."""
-        for p in self._opened:
-            call("arcllm_cuda_ipc_close_handle", p)
-        self._opened = []
-        for own in self._own:
-            call("arcllm_cuda_free", own)
-        self._own = []
+
+class GemmGather(_ParityBuffers):
+    """Buffers of the output-row-sharded prefill GEMM whose split-K reduce
+    kernel all-gathers the result over NVLink (arcllm_cuda_gemm_bf16_allgather):
+    after `step()`, `y_ptr` holds the whole m x n_total fp32 result on this
+    rank.  Two buffer sets alternate by epoch parity, as in RankGather."""
+
+    def __init__(self, m, n_total, n_ranks, rank, exchange, timeout_us=2000000):
+        lib()
+        self.m, self.n_total, self.timeout_us = m, n_total, timeout_us
+        n = C.c_uint64(0)
+        call("arcllm_cuda_gemm_allgather_buffer_bytes", m, n_total, C.byref(n))
+        self._setup_buffers(n.value, n_ranks, rank, exchange, "GemmGather")
+
+    @property
+    def y_ptr(self):
+        """Device address of this rank's copy of the last launch's m x n_total result."""
+        return self._own[self.epoch & 1].value
+
+    def step(self, ggml_type, w, n, k, x, c0, stream):
+        """One GEMM of this rank's weight rows [c0, c0 + n) (w points at row c0)
+        against x (m x k bf16), gathered into every rank's result."""
+        self.epoch += 1
+        call("arcllm_cuda_gemm_bf16_allgather", ggml_type, w, n, k, x, self.m, c0, self.n_total,
+             self._bufs[self.epoch & 1], self.n_ranks, self.rank, self.epoch, self.timeout_us, stream)
 
 
 class ExchangeBuffers:

@@ -689,7 +689,9 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
     ex.close()
     torch.cuda.empty_cache()
 
-    # ---- config 4: prefill gate GEMM, output rows sharded + NCCL all-gather ----
+    # ---- config 4: prefill gate GEMM, output rows sharded; the result all-gathered by the GEMM's
+    # split-K reduce kernel over NVLink peer stores (NCCL all-gather timed beside it) ----
+    from arcllm_b200.rank_gather import GemmGather
     _, tflops_peak, _ = measured_peaks()
     m = 256
     f0, fr = shard(FFN, 128)
@@ -705,33 +707,66 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
            C.c_float(1), sp)
     xb = xf.to(torch.bfloat16)
     sizes = [None] * world
-    dist.all_gather_object(sizes, fr)
-    fmax = max(sizes)  # shards of unequal size travel padded to the largest, one all-gather of equal parts
+    dist.all_gather_object(sizes, (f0, fr))
+    fmax = max(r_ for _, r_ in sizes)  # NCCL form: shards padded to the largest, one all-gather of equal parts
     y = torch.empty(m * fmax, dtype=torch.float32, device=dev)
     yall = torch.empty(world * m * fmax, dtype=torch.float32, device=dev)
+    gg = GemmGather(m, FFN, world, rank, exchange)
 
     def step4(i):
+        gg.step(A.GGML_Q4_K, C.c_void_p(ws[i % ncop].data_ptr()), fr, HIDDEN, C.c_void_p(xb.data_ptr()), f0, sp)
+
+    def step4_nccl(i):
         A.check(L.arcllm_cuda_gemm_q4k_bf16(C.c_void_p(ws[i % ncop].data_ptr()), fr, HIDDEN,
                                             C.c_void_p(xb.data_ptr()), m, C.c_void_p(y.data_ptr()), sp), "gemm")
         dist.all_gather_into_tensor(yall, y)
 
-    for i in range(5):
-        step4(i)
-    barrier()
-    n_it = 50
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for i in range(n_it):
-        step4(i)
-    b.record()
-    barrier()
-    ms = max_over_ranks(a.elapsed_time(b) / n_it)
+    def timed4(step, n_it=50):
+        for i in range(5):
+            step(i)
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(n_it):
+            step(i)
+        b.record()
+        barrier()
+        return max_over_ranks(a.elapsed_time(b) / n_it), n_it
+
+    ms, n_it = timed4(step4)
+    # check: every rank's gathered result against plain single-GPU GEMMs of each rank's shard (same
+    # split-K as the shard's own launch, so bit for bit), weights of the last step's copy
+    last = (n_it - 1) % ncop
+    got_h = torch.empty(m * FFN, dtype=torch.float32).pin_memory()
+    A.check(L.arcllm_cuda_memcpy_d2h(C.c_void_p(got_h.data_ptr()), C.c_void_p(gg.y_ptr), 4 * m * FFN, sp), "d2h")
+    A.check(L.arcllm_cuda_stream_synchronize(sp), "sync")
+    got = got_h.to(dev).view(m, FFN)
+    same = 1
+    for q0, qr in sizes:
+        wq = torch.empty(q_bytes("q4k", qr, HIDDEN) + 16, dtype=torch.uint8, device=dev)
+        A.call("arcllm_cuda_fill_q4k", C.c_void_p(wq.data_ptr()), q0 * (HIDDEN // 256), qr * (HIDDEN // 256),
+               0x1C00 + last, sp)
+        yq = torch.empty(m * qr, dtype=torch.float32, device=dev)
+        A.check(L.arcllm_cuda_gemm_q4k_bf16(C.c_void_p(wq.data_ptr()), qr, HIDDEN, C.c_void_p(xb.data_ptr()), m,
+                                            C.c_void_p(yq.data_ptr()), sp), "gemm")
+        torch.cuda.synchronize()
+        same &= int(torch.equal(got[:, q0:q0 + qr].contiguous().view(torch.int32), yq.view(m, qr).view(torch.int32)))
+        del wq, yq
+    bits = C.c_uint32(0)
+    dev_err = L.arcllm_cuda_device_error(sp, C.byref(bits))
+    ms_nccl, _ = timed4(step4_nccl)
     tf = 2.0 * m * FFN * HIDDEN / (ms * 1e-3) / 1e12
     out["config4_prefill_gate_256x18944x3584_rowshard"] = {
         "TFLOP/s": round(tf, 1), "frac_of_bf16_peak_per_gpu": round(tf / world / tflops_peak, 4) if tflops_peak else None,
         "us_per_step": round(ms * 1e3, 2), "rows_per_rank": fr,
-        "collective": "NCCL all-gather of the Y shards (padded to %d rows)" % fmax}
-    del ws, xf, xb, y, yall
+        "collective": "fused: the GEMM's split-K reduce kernel stores the shard into every rank's m x 18944 result "
+                      "(NVLink peer stores) + flag handshake",
+        "bit_exact_vs_1gpu_shards": bool(max_over_ranks(-same) == -1) and dev_err == 0,
+        "us_per_step_gemm_plus_nccl_allgather": round(ms_nccl * 1e3, 2)}
+    del ws, xf, xb, y, yall, got, got_h
+    torch.cuda.synchronize()
+    barrier()
+    gg.close()
     torch.cuda.empty_cache()
     barrier()
 

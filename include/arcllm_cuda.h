@@ -228,6 +228,29 @@ ARCLLM_CUDA_API int arcllm_cuda_gemm_q4k_bf16(const void *w, uint32_t n, uint32_
  * fused into the epilogue).  Q6_K rows need only be 2-byte aligned. */
 ARCLLM_CUDA_API int arcllm_cuda_gemm_bf16(int type, const void *w, uint32_t n, uint32_t k, const uint16_t *x_bf16,
                                           uint32_t m, const float *residual, float *y, void *stream);
+/* Output-row-sharded form of the same GEMM (config 4 over N GPUs; the
+ * reference runs it on one device, src/arcllm_v1_runtime.cpp:343-366): rank
+ * `rank` holds rows [c0, c0 + n) of the full n_total x k weight matrix (w
+ * points at row c0) and computes those columns of y; the kernel that adds the
+ * split-K partials stores every float4 of them into EVERY rank's m x n_total
+ * result (its own with local stores, the others with NVLink peer stores --
+ * stores only), then the ranks meet on per-rank flags: when the launch
+ * completes on rank r, rank_bufs[r] holds all n_total columns.  This replaces
+ * GEMM + ncclAllGather.
+ *   rank_bufs[q]: rank q's buffer as this process maps it (IPC mapping for
+ *   q != rank), arcllm_cuda_gemm_allgather_buffer_bytes(m, n_total) bytes,
+ *   256-byte aligned, zero-filled before first use; consecutive launches
+ *   alternate between two buffer sets (epoch parity), as for
+ *   arcllm_cuda_matvec_allgather;
+ *   epoch: 1, 2, 3 ... the same sequence on every rank; timeout_us bounds the
+ *   flag wait (0: 2 s; a wait that runs out sets the device error word).
+ * c0 and n_total multiples of 4, n % 128 == 0; bf16 operands (mode 0). */
+ARCLLM_CUDA_API int arcllm_cuda_gemm_allgather_buffer_bytes(uint32_t m, uint32_t n_total, uint64_t *out);
+ARCLLM_CUDA_API int arcllm_cuda_gemm_bf16_allgather(int type, const void *w, uint32_t n, uint32_t k,
+                                                    const uint16_t *x_bf16, uint32_t m, uint32_t c0,
+                                                    uint32_t n_total, void *const *rank_bufs, uint32_t n_ranks,
+                                                    uint32_t rank, uint32_t epoch, uint32_t timeout_us,
+                                                    void *stream);
 /* The same GEMM with fp16 operands: x_f16 is fp16 and the weights are
  * dequantised to fp16 (scale and offset of each sub-block and q*f - o rounded
  * to 11 significant bits instead of bf16's 8), at the same tensor-core rate.
