@@ -75,6 +75,7 @@ SIGNATURES = {
     "arcllm_cuda_stream_create": [C.POINTER(_vp)],
     "arcllm_cuda_stream_destroy": [_vp],
     "arcllm_cuda_stream_synchronize": [_vp],
+    "arcllm_cuda_stream_delay_us": [_u32, _vp],
     "arcllm_cuda_model_create": [_vp, C.POINTER(_vp)],
     "arcllm_cuda_model_destroy": [_vp],
     "arcllm_cuda_model_set_layer": [_vp, _u32, _vp],

@@ -560,6 +560,22 @@ int arcllm_cuda_stream_synchronize(void* stream) {
     return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "stream_synchronize");
 }
 
+namespace {
+// One thread polls %globaltimer until `ns` nanoseconds have passed: the same wall-clock delay on every
+// GPU whatever its SM clock (a cycle-count spin ends up to ~10 % apart between GPUs at different clocks).
+__global__ void stream_delay_kernel(unsigned long long ns) {
+    const unsigned long long t0 = arc::globaltimer();
+    while (arc::globaltimer() - t0 < ns) __nanosleep(1000);
+}
+}  // namespace
+
+int arcllm_cuda_stream_delay_us(uint32_t us, void* stream) {
+    if (us > 1000000u) return set_error(ARC_E_INVALID_ARGUMENT, "stream_delay_us: at most 1 s");
+    stream_delay_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(1000ull * us);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? ARC_OK : arc::set_cuda_error(e, "stream_delay_us");
+}
+
 int arcllm_cuda_model_create(const arcllm_cuda_model_config* cfg, arcllm_cuda_model** out) {
     ARC_GUARD_BEGIN
     return arc::model_create(cfg, out);

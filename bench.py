@@ -414,9 +414,9 @@ def main(argv=None):
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if rendezvous is not None:
         rendezvous.replay()
-        # ~2 ms of spinning after the rendezvous, the same on every rank: the host has the timed graph
-        # queued before any rank starts it
-        torch.cuda._sleep(1 << 22)
+        # 2 ms of device wall-clock time after the rendezvous, the same on every rank whatever its SM
+        # clock: the host has the timed graph queued before any rank starts it
+        A.check(L.arcllm_cuda_stream_delay_us(2000, sp), "stream_delay")
     t_start.record()
     if graph is not None:
         graph.replay()
@@ -650,7 +650,7 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
     g1.replay()  # upload: an untimed pass
     barrier()
     step1b(0, sp)  # rendezvous: its exchange ends on every rank within a flag round trip of the others
-    torch.cuda._sleep(1 << 22)
+    A.check(L.arcllm_cuda_stream_delay_us(2000, sp), "stream_delay")
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     g1.replay()

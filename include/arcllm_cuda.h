@@ -385,6 +385,10 @@ ARCLLM_CUDA_API int arcllm_cuda_memcpy_d2h(void *dst_host, const void *src, uint
 ARCLLM_CUDA_API int arcllm_cuda_stream_create(void **out);
 ARCLLM_CUDA_API int arcllm_cuda_stream_destroy(void *stream);
 ARCLLM_CUDA_API int arcllm_cuda_stream_synchronize(void *stream);
+/* Enqueues a one-thread kernel on `stream` that waits `us` microseconds of
+ * device wall-clock time (%globaltimer), at most 1 s; used to start several
+ * GPUs' timed work together after a device rendezvous. */
+ARCLLM_CUDA_API int arcllm_cuda_stream_delay_us(uint32_t us, void *stream);
 
 /* ---- greedy decode of one Qwen2-family model -----------------------------
  * The device half of arcllm::v1::runtime::generate() (src/arcllm_v1_runtime.cpp:

@@ -181,3 +181,17 @@ def test_allgather_ranks_on_separate_gpus(world):
         assert msg == "", "rank %d: %s" % (rank, msg)
         assert bits == 0, "rank %d device error %#x" % (rank, bits)
         assert ok, "rank %d logits differ from the single-GPU matvec" % rank
+
+
+def test_stream_delay_waits_its_wall_clock_time():
+    """The rendezvous delay of the multi-GPU bench: a 2 ms arcllm_cuda_stream_delay_us lasts at least
+    2 ms by CUDA events on its stream and ends well within 10 ms."""
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    A.call("arcllm_cuda_stream_delay_us", 10, C.c_void_p(s.cuda_stream))  # first launch loads the module
+    a.record(s)
+    A.call("arcllm_cuda_stream_delay_us", 2000, C.c_void_p(s.cuda_stream))
+    b.record(s)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    assert 1.99 <= ms < 10.0, ms

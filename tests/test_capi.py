@@ -64,6 +64,8 @@ def test_host_side_argument_validation():
     assert L.arcllm_cuda_status_string(st) == b"ARC_E_UNSUPPORTED_SHAPE"
     st = L.arcllm_cuda_dequant_q4k(None, 4, None, None)
     assert L.arcllm_cuda_status_string(st) == b"ARC_E_INVALID_ARGUMENT"
+    st = L.arcllm_cuda_stream_delay_us(1000001, None)
+    assert L.arcllm_cuda_status_string(st) == b"ARC_E_INVALID_ARGUMENT"
 
 
 def test_allgather_layout_and_argument_validation():
