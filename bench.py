@@ -725,6 +725,10 @@ def run_extra_multi(A, L, torch, dist, dev, sp, world, rank, hbm_peak, barrier):
         for i in range(5):
             step(i)
         barrier()
+        # rendezvous (one untimed step: its gather ends on every rank together) and 2 ms of wall-clock
+        # delay, for both forms, so the first timed step does not absorb the host skew of the barrier
+        step(5)
+        A.check(L.arcllm_cuda_stream_delay_us(2000, sp), "stream_delay")
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for i in range(n_it):
