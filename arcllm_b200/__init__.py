@@ -35,6 +35,8 @@ SIGNATURES = {
     "arcllm_cuda_allgather_logits_offset": [_u32, C.POINTER(_u64)],
     "arcllm_cuda_matvec_allgather": [_i32, _vp, _u32, _u32, _vp, _u32, _u32, C.POINTER(_vp), _u32, _u32, _u32, _u32,
                                      _vp],
+    "arcllm_cuda_matvec_allgather_hostio": [_i32, _vp, _u32, _u32, _vp, _vp, _u32, _u32, C.POINTER(_vp), _u32, _u32,
+                                            _u32, _u32, _vp, _vp],
     "arcllm_cuda_ipc_get_handle": [_vp, _vp],
     "arcllm_cuda_ipc_open_handle": [_vp, C.POINTER(_vp)],
     "arcllm_cuda_ipc_close_handle": [_vp],

@@ -182,10 +182,11 @@ int arcllm_cuda_allgather_logits_offset(uint32_t rows_total, uint64_t* out) {
     ARC_GUARD_END
 }
 
-int arcllm_cuda_matvec_allgather(int ggml_type, const void* w, uint32_t rows, uint32_t k, const float* x,
-                                 uint32_t row0, uint32_t rows_total, void* const* rank_bufs, uint32_t n_ranks,
-                                 uint32_t rank, uint32_t epoch, uint32_t timeout_us, void* stream) {
-    ARC_GUARD_BEGIN
+// Checks the arguments of one all-gather matvec and fills its RankGather (g.out = this rank's logits
+// in its own exchange buffer).  Shared by the device-resident and the host-IO entry points.
+static int allgather_setup(int ggml_type, uint32_t rows, uint32_t k, const float* x, uint32_t row0,
+                           uint32_t rows_total, void* const* rank_bufs, uint32_t n_ranks, uint32_t rank,
+                           uint32_t epoch, uint32_t timeout_us, arc::RankGather& g) {
     if (ggml_type != ARC_GGML_Q4_K && ggml_type != ARC_GGML_Q6_K)
         return set_error(ARC_E_INVALID_ARGUMENT, "matvec_allgather: Q4_K or Q6_K weights");
     if (!rank_bufs || n_ranks == 0 || n_ranks > 8 || rank >= n_ranks || epoch == 0 || rows == 0 ||
@@ -194,7 +195,7 @@ int arcllm_cuda_matvec_allgather(int ggml_type, const void* w, uint32_t rows, ui
     if (!arc::matvec_imma_supported(ggml_type, false, rows, k) || (reinterpret_cast<uintptr_t>(x) & 15u))
         return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec_allgather: needs the whole-row tensor-core kernel "
                                                   "(K/256 <= 14, 16-byte aligned x)");
-    arc::RankGather g{};
+    g = arc::RankGather{};
     g.n_ranks = n_ranks;
     g.self_rank = rank;
     g.epoch = epoch;
@@ -207,8 +208,54 @@ int arcllm_cuda_matvec_allgather(int ggml_type, const void* w, uint32_t rows, ui
         g.ll[r] = static_cast<unsigned long long*>(rank_bufs[r]);
     }
     g.out = reinterpret_cast<float*>(static_cast<uint8_t*>(rank_bufs[rank]) + gather_logits_offset(rows_total));
+    return ARC_OK;
+}
+
+int arcllm_cuda_matvec_allgather(int ggml_type, const void* w, uint32_t rows, uint32_t k, const float* x,
+                                 uint32_t row0, uint32_t rows_total, void* const* rank_bufs, uint32_t n_ranks,
+                                 uint32_t rank, uint32_t epoch, uint32_t timeout_us, void* stream) {
+    ARC_GUARD_BEGIN
+    arc::RankGather g;
+    const int st = allgather_setup(ggml_type, rows, k, x, row0, rows_total, rank_bufs, n_ranks, rank, epoch,
+                                   timeout_us, g);
+    if (st != ARC_OK) return st;
     return arc::matvec_imma_launch(ggml_type, false, w, nullptr, rows, k, x, nullptr, 0.f, nullptr, nullptr,
                                    g.out + row0, static_cast<cudaStream_t>(stream), nullptr, &g);
+    ARC_GUARD_END
+}
+
+int arcllm_cuda_matvec_allgather_hostio(int ggml_type, const void* w, uint32_t rows, uint32_t k,
+                                        const float* x_host, float* x_dev, uint32_t row0, uint32_t rows_total,
+                                        void* const* rank_bufs, uint32_t n_ranks, uint32_t rank, uint32_t epoch,
+                                        uint32_t timeout_us, float* y_host, void* stream) {
+    ARC_GUARD_BEGIN
+    if (!x_host || !y_host || !x_dev) return set_error(ARC_E_INVALID_ARGUMENT, "matvec_allgather_hostio: null pointer");
+    arc::RankGather g;
+    int st = allgather_setup(ggml_type, rows, k, x_dev, row0, rows_total, rank_bufs, n_ranks, rank, epoch,
+                             timeout_us, g);
+    if (st != ARC_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(x_dev, x_host, sizeof(float) * k, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_allgather_hostio h2d");
+    // Pinned, device-mapped y_host: the collect phase stores every rank's rows straight into it, so
+    // each logit crosses the host link once and no copy follows the kernel (this rank's own rows still
+    // go to its device buffer, which nothing reads).  Pageable y_host: the device logits, then one copy.
+    cudaPointerAttributes at{};
+    const bool mapped = cudaPointerGetAttributes(&at, y_host) == cudaSuccess && at.type == cudaMemoryTypeHost &&
+                        at.devicePointer != nullptr;
+    if (!mapped) cudaGetLastError();  // clear a lookup failure of an unregistered pointer
+    float* const own = g.out;
+    if (mapped) g.out = static_cast<float*>(at.devicePointer);
+    st = arc::matvec_imma_launch(ggml_type, false, w, nullptr, rows, k, x_dev, nullptr, 0.f, nullptr, nullptr,
+                                 own + row0, s, nullptr, &g);
+    if (st != ARC_OK) return st;
+    if (!mapped) {
+        e = cudaMemcpyAsync(y_host, own, sizeof(float) * rows_total, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_allgather_hostio d2h");
+    }
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return arc::set_cuda_error(e, "matvec_allgather_hostio sync");
+    return ARC_OK;
     ARC_GUARD_END
 }
 

@@ -117,6 +117,18 @@ class RankGather(_ParityBuffers):
             from . import check
             check(st, "matvec_allgather")
 
+    def step_hostio(self, w, rows, k, x_host, x_dev, row0, y_host, stream, ggml_type=GGML_Q6_K):
+        """One all-gather matvec with host buffers: x_host (k floats) in, all
+        rows_total logits in y_host (pinned and device-mapped: stored by the
+        kernel itself) when it returns."""
+        self.epoch += 1
+        st = self._L.arcllm_cuda_matvec_allgather_hostio(ggml_type, w, rows, k, x_host, x_dev, row0, self.rows_total,
+                                                         self._bufs[self.epoch & 1], self.n_ranks, self.rank,
+                                                         self.epoch, self.timeout_us, y_host, stream)
+        if st:
+            from . import check
+            check(st, "matvec_allgather_hostio")
+
 
 class GemmGather(_ParityBuffers):
     """Buffers of the output-row-sharded prefill GEMM whose split-K reduce

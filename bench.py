@@ -3,8 +3,10 @@
 Headline workload (N=1 and every N): the Q6_K LM-head matvec, 152064 x 3584
 (447,068,160 weight bytes), fp32 x ~ N(0,1).  One step = one pass of the LM
 head over one activation vector.  At N>1 the rows are sharded over the ranks
-(152064/N contiguous rows each) and the fp32 logits are all-gathered with
-NCCL, so every rank ends the step with the full logits (strong scaling).
+(152064/N contiguous rows each) and the fp32 logits are all-gathered by the
+matvec kernel itself over NVLink peer stores (`--collective nccl`: matvec +
+ncclAllGather), so every rank ends the step with the full logits (strong
+scaling).
 
 Timing: W untimed warm-up steps, then K steps between barrier +
 cuda.synchronize on both sides, CUDA events on the launching stream, max
@@ -15,9 +17,10 @@ enough weight copies to exceed 3x L2.
 Printed (rank 0, one JSON line): the contract keys plus `roofline` (dominant
 kernel = the matvec; achieved = algorithmic bytes / mean kernel time vs the
 measured HBM copy bandwidth), `cpu_baseline` (the reference's own CPU
-matmul_q6_cpu timed on this host), `e2e` (the C-ABI host-IO call:
-x host->device, matvec, logits device->host, every step), `clocks`, and
-`extra` (configs 0, 1b, 2 at N=1).
+matmul_q6_cpu timed on this host), `e2e` (the C-ABI host-IO call every
+step: pinned host x copied in, the matvec -- with the all-gather at N>1 --
+storing all logits into pinned mapped host memory, stream sync), `clocks`,
+and `extra` (configs 0, 1b, 2, 3, 4 at N=1; the sharded forms at N>1).
 
 `--impl reference` times the reference's CPU implementation of the same
 workload (oracle/_ref, compiled from the reference sources; the restated
@@ -461,12 +464,9 @@ def main(argv=None):
     e2e_steps = 0 if args.no_e2e else max(10, min(args.steps, 500))
 
     def e2e_step():
-        if rg is not None:  # host x in, the fused all-gather matvec, every row's logit out
-            A.check(L.arcllm_cuda_memcpy_h2d(C.c_void_p(xd.data_ptr()), C.c_void_p(xh.data_ptr()), 4 * K, sp))
-            rg.step(wp, rows_per, K, C.c_void_p(xd.data_ptr()), r0, sp, TY)
-            A.check(L.arcllm_cuda_memcpy_d2h(C.c_void_p(lh.data_ptr()), C.c_void_p(rg.logits_ptr),
-                                             4 * rows_per * world, sp))
-            A.check(L.arcllm_cuda_stream_synchronize(sp))
+        if rg is not None:  # host x in, the fused all-gather matvec, every row's logit into pinned host memory
+            rg.step_hostio(wp, rows_per, K, C.c_void_p(xh.data_ptr()), C.c_void_p(xd.data_ptr()), r0,
+                           C.c_void_p(lh.data_ptr()), sp, TY)
             return
         A.check(L.arcllm_cuda_matvec_hostio(TY, wp, rows_per, K, C.c_void_p(xh.data_ptr()),
                                             C.c_void_p(xd.data_ptr()), yp, C.c_void_p(yh.data_ptr()), sp),
@@ -564,8 +564,9 @@ def main(argv=None):
             "e2e": {"value": None if e2e_val is None else round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": 4 * K,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
-                    "api": ("arcllm_cuda_memcpy_h2d + arcllm_cuda_matvec_allgather + arcllm_cuda_memcpy_d2h of all "
-                            "logits + stream sync" if rg is not None else
+                    "api": ("arcllm_cuda_matvec_allgather_hostio (pinned host x copied in, every rank's logits "
+                            "stored by the kernel's collect phase into pinned mapped host memory, stream sync)"
+                            if rg is not None else
                             "arcllm_cuda_matvec_hostio (pinned host x copied in, logits stored by the kernel into "
                             "pinned mapped host memory, stream sync)")},
             "gpu_launches": args.steps,

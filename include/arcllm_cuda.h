@@ -146,6 +146,18 @@ ARCLLM_CUDA_API int arcllm_cuda_matvec_allgather(int ggml_type, const void *w, u
                                                  const float *x, uint32_t row0, uint32_t rows_total,
                                                  void *const *rank_bufs, uint32_t n_ranks, uint32_t rank,
                                                  uint32_t epoch, uint32_t timeout_us, void *stream);
+/* The same launch with host buffers (the multi-GPU form of
+ * arcllm_cuda_matvec_hostio): copies x_host (k floats) into x_dev, runs the
+ * all-gather matvec and returns once all rows_total logits are in y_host.
+ * Pinned, device-mapped y_host: the kernel's collect phase stores every
+ * logit straight into it over the host link (no copy after the kernel);
+ * pageable y_host: one device-to-host copy of the gathered logits.
+ * Synchronises `stream`. */
+ARCLLM_CUDA_API int arcllm_cuda_matvec_allgather_hostio(int ggml_type, const void *w, uint32_t rows, uint32_t k,
+                                                        const float *x_host, float *x_dev, uint32_t row0,
+                                                        uint32_t rows_total, void *const *rank_bufs,
+                                                        uint32_t n_ranks, uint32_t rank, uint32_t epoch,
+                                                        uint32_t timeout_us, float *y_host, void *stream);
 /* CUDA IPC of exchange buffers between the ranks' processes: a 64-byte
  * handle of a buffer allocated with arcllm_cuda_malloc, opened in a peer
  * process (peer access enabled lazily), closed before the owner frees it. */

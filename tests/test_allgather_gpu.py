@@ -1,6 +1,6 @@
 """The row-sharded LM head with its logits all-gathered over NVLink peer stores
-(arcllm_cuda_matvec_allgather): every rank's copy of the logits equals the
-single-GPU matvec of the whole matrix bit for bit, the epoch-tagged words tell
+(arcllm_cuda_matvec_allgather, and its host-IO form): every rank's copy of the
+logits equals the single-GPU matvec of the whole matrix bit for bit, the epoch-tagged words tell
 consecutive launches apart, and a rank that never arrives ends the wait with
 the device timeout flag (no hang, context still usable).
 
@@ -69,6 +69,37 @@ def test_allgather_single_rank_equals_matvec():
             torch.cuda.synchronize()
             got = _d2h(rg.logits_ptr, rows)
             assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        assert _device_error_bits() == 0
+    finally:
+        rg.close()
+
+
+def test_allgather_hostio_single_rank_equals_matvec():
+    """arcllm_cuda_matvec_allgather_hostio: host x in, all logits in host memory.  A pinned y_host is
+    written by the kernel's collect phase itself; a pageable one gets the gathered logits copied.  Both
+    equal the plain matvec bit for bit, over consecutive epochs with a changing x."""
+    from arcllm_b200.rank_gather import RankGather
+    rows, seed = 5000, 774
+    sp = G.stream()
+    w = G.empty_u8(rows * RB + 16)
+    A.call("arcllm_cuda_fill_q6k", G.ptr(w), 0, rows * NB, seed, sp)
+    xd = G.empty_f32(K)
+    xs = torch.empty(K, dtype=torch.float32).pin_memory()
+    y_pinned = torch.full((rows,), float("nan"), dtype=torch.float32).pin_memory()
+    y_pageable = np.full(rows, np.nan, np.float32)
+    rg = RankGather(rows, 1, 0, lambda h: [h])
+    try:
+        for it in range(4):
+            x = torch.from_numpy(np.random.default_rng(seed + it).standard_normal(K).astype(np.float32))
+            xs.copy_(x)
+            xref = G.empty_f32(K)
+            xref.copy_(x.to(G.dev()))
+            ref = _plain(G.ptr(w), rows, G.ptr(xref), sp)
+            pinned = it % 2 == 0
+            yh = C.c_void_p(y_pinned.data_ptr()) if pinned else y_pageable.ctypes.data_as(C.c_void_p)
+            rg.step_hostio(G.ptr(w), rows, K, C.c_void_p(xs.data_ptr()), G.ptr(xd), 0, yh, sp)
+            got = y_pinned.numpy() if pinned else y_pageable
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), "pinned" if pinned else "pageable"
         assert _device_error_bits() == 0
     finally:
         rg.close()
@@ -149,6 +180,16 @@ def _rank_worker(rank, world, port, rows_total, seed, q):
             got = _d2h(rg.logits_ptr, rows_total)
             ok = ok and np.array_equal(got.view(np.uint32), ref.view(np.uint32))
             dist.barrier()  # no rank starts the next epoch while another still reads these logits
+        # the host-IO form: host x in, every rank's rows stored into this rank's pinned host logits
+        xh = torch.empty(K, dtype=torch.float32).pin_memory()
+        xh.copy_(x.cpu())
+        yh = torch.full((rows_total,), float("nan"), dtype=torch.float32).pin_memory()
+        xd = torch.empty(K, dtype=torch.float32, device=dev)
+        for _ in range(2):
+            rg.step_hostio(C.c_void_p(w.data_ptr()), rows, K, C.c_void_p(xh.data_ptr()), C.c_void_p(xd.data_ptr()),
+                           row0, C.c_void_p(yh.data_ptr()), sp)
+            ok = ok and np.array_equal(yh.numpy().view(np.uint32), ref.view(np.uint32))
+            dist.barrier()
         bits = C.c_uint32(0)
         A.lib().arcllm_cuda_device_error(sp, C.byref(bits))
         dist.barrier()
