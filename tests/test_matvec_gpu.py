@@ -309,20 +309,25 @@ def test_matvec_nonfinite_x_propagates(fmt, bad):
 
 
 @pytest.mark.parametrize("pinned", [True, False])
-def test_matvec_hostio_pinned_and_pageable(pinned):
+@pytest.mark.parametrize("fmt,rows,k", [("q6k", 152064 // 8, 3584), ("q4k", 3584, 18944)])
+def test_matvec_hostio_pinned_and_pageable(pinned, fmt, rows, k):
     """arcllm_cuda_matvec_hostio: a pinned y_host is written by the kernel
-    itself (mapped host memory), a pageable one by a copy afterwards; both
-    hold the device matvec's rows bit for bit."""
-    rows, k, seed = 152064 // 8, 3584, 3131
-    w = gpu_fill("q6k", rows, k, seed)
-    x = O.normal_f32(k, seed + 1)
-    y_ref = run_matvec("q6k", w, rows, k, x)
-    xh = torch.from_numpy(x.copy())
+    itself (mapped host memory), a pageable one by a copy afterwards.  Whole-row
+    (LM-head shard) and K-slice (FFN down) kernels; three calls with a different
+    x each hold the device matvec's rows bit for bit."""
+    seed = 3131
+    w = gpu_fill(fmt, rows, k, seed)
+    xd, yd = G.empty_f32(k), G.empty_f32(rows)
+    xh = torch.empty(k, dtype=torch.float32)
     yh = torch.full((rows,), float("nan"), dtype=torch.float32)
     if pinned:
         xh, yh = xh.pin_memory(), yh.pin_memory()
-    xd, yd = G.empty_f32(k), G.empty_f32(rows)
-    A.call("arcllm_cuda_matvec_hostio", A.GGML_Q6_K, G.ptr(w), rows, k, C.c_void_p(xh.data_ptr()), G.ptr(xd),
-           G.ptr(yd), C.c_void_p(yh.data_ptr()), G.stream())
-    assert np.array_equal(yh.numpy().view(np.uint32), y_ref.view(np.uint32))
+    ty = A.GGML_Q6_K if fmt == "q6k" else A.GGML_Q4_K
+    for it in range(3):
+        x = O.normal_f32(k, seed + 1 + it)
+        y_ref = run_matvec(fmt, w, rows, k, x)
+        xh.copy_(torch.from_numpy(x))
+        A.call("arcllm_cuda_matvec_hostio", ty, G.ptr(w), rows, k, C.c_void_p(xh.data_ptr()), G.ptr(xd),
+               G.ptr(yd), C.c_void_p(yh.data_ptr()), G.stream())
+        assert np.array_equal(yh.numpy().view(np.uint32), y_ref.view(np.uint32)), it
     G.check_device_error()
