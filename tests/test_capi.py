@@ -96,6 +96,17 @@ def test_allgather_layout_and_argument_validation():
     ]
     for args, want in cases:
         assert name(ag(*args)) == want, args
+    # the host-IO form runs the same checks (x_dev in place of x), plus its host pointers, before any device work
+    agh = L.arcllm_cuda_matvec_allgather_hostio
+    xh, yh = C.c_void_p(4096), C.c_void_p(8192)
+    for args, want in cases:
+        t, w_, rows, k, xd, row0, total, bufs, n_r, rank, ep, tmo, st = args
+        assert name(agh(t, w_, rows, k, xh, xd, row0, total, bufs, n_r, rank, ep, tmo, yh, st)) == want, args
+    good = (A.GGML_Q6_K, w, 3008, 3584, xh, x, 0, 6016, ok, 2, 0, 1, 0, yh, None)
+    for i in (4, 5, 13):  # null x_host, x_dev, y_host
+        bad = list(good)
+        bad[i] = None
+        assert name(agh(*bad)) == b"ARC_E_INVALID_ARGUMENT", i
 
 
 def test_shard_rows_cover_and_align():
