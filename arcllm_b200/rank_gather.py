@@ -104,7 +104,8 @@ class RankGather(_ParityBuffers):
     @property
     def logits_ptr(self):
         """Device address of this rank's copy of all rows_total results of the
-        last launch."""
+        last `step()` (after `step_hostio()` with a pinned y_host it holds only
+        this rank's own rows: the others went straight to y_host)."""
         return self._own[self.epoch & 1].value + self._logits_off
 
     def step(self, w, rows, k, x, row0, stream, ggml_type=GGML_Q6_K):

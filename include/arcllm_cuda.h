@@ -151,7 +151,8 @@ ARCLLM_CUDA_API int arcllm_cuda_matvec_allgather(int ggml_type, const void *w, u
  * all-gather matvec and returns once all rows_total logits are in y_host.
  * Pinned, device-mapped y_host: the kernel's collect phase stores every
  * logit straight into it over the host link (no copy after the kernel);
- * pageable y_host: one device-to-host copy of the gathered logits.
+ * pageable y_host: one device-to-host copy of the gathered logits.  With a
+ * pinned y_host the rank's own logits area holds only its own rows.
  * Synchronises `stream`. */
 ARCLLM_CUDA_API int arcllm_cuda_matvec_allgather_hostio(int ggml_type, const void *w, uint32_t rows, uint32_t k,
                                                         const float *x_host, float *x_dev, uint32_t row0,
