@@ -153,6 +153,18 @@ def gpu_smi_id(torch, local_rank):
 
 
 # --------------------------------------------------------------- cpu baseline
+def host_cpu_model():
+    """The host CPU's model name (first /proc/cpuinfo entry), or None."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def cpu_baseline(seconds=10.0):
     """The reference's own matmul_q6_cpu (oracle/_ref) on a bounded sample of
     the LM head, 1 thread (the reference's form); the restated oracle is used
@@ -176,7 +188,7 @@ def cpu_baseline(seconds=10.0):
         if el >= seconds or done >= 400:
             break
     gbs = done * matvec_alg_bytes("q6k", rows, HIDDEN) / el / 1e9
-    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "cpu_model": host_cpu_model(),
             "sample": "%d passes over an 8192-row slice (%.1f MB) of the 152064x3584 Q6_K LM head, "
                       "x fp32, 1 thread, %.1f s" % (done, q_bytes("q6k", rows, HIDDEN) / 1e6, el)}
 
@@ -232,6 +244,7 @@ def run_reference(args):
         "config": {"workload": "config1: Q6_K LM-head matvec 152064x3584, fp32 x; reference CPU path on a "
                                "19008-row (1/8) sample per step", "parallelism": "%d host threads" % cores},
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "cpu_model": host_cpu_model(),
                          "sample": "19008 rows x 3584 (55.9 MB) of the LM head per step, rows split over "
                                    "%d threads, reference matmul_q6_cpu per row" % cores},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
