@@ -385,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint8_t* __restrict__ w, uint32_t n_total, uint32_t k, uint32_t m,
                         const float* __restrict__ residual, float* __restrict__ y, unsigned int* err,
                         const SplitKWs sk) {
+    pdl_wait();  // X and the residual may come from the preceding kernels (a no-op for a plain launch)
     constexpr bool F16 = MODE >= 1;
     constexpr uint32_t kStages = GemmStage<MODE>::kStages, kStageBytes = GemmStage<MODE>::kBytes;
     constexpr uint32_t kBOff = GemmStage<MODE>::kBOff;
@@ -631,6 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void __launch_bounds__(256) gemm_splitk_reduce_kernel(const float4* __restrict__ ws, uint32_t ks,
                                                                  uint64_t n4, const float4* __restrict__ residual,
                                                                  float4* __restrict__ y) {
+    pdl_wait();  // the partials come from the GEMM launch before
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
@@ -664,6 +666,7 @@ struct GemmGather {
 __global__ void __launch_bounds__(256) gemm_reduce_gather_kernel(const float4* __restrict__ ws, uint32_t ks,
                                                                  uint32_t n4_row, uint64_t n4,
                                                                  const GemmGather g, unsigned int* err) {
+    pdl_wait();  // the partials come from the GEMM launch before
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4

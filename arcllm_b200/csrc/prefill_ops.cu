@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_bf16_kernel(const float* __r
                                                                 const float* __restrict__ gamma, float eps, uint32_t h,
                                                                 uint16_t* __restrict__ out,
                                                                 uint16_t* __restrict__ out_lo, unsigned int* err) {
+    pdl_wait();  // inputs come from the preceding kernels (a no-op for a plain launch)
     __shared__ double red[8];
     const float* xr = x + (uint64_t)blockIdx.x * h;
     double ss = 0.0;
@@ -77,6 +78,7 @@ __global__ void rope_kv_rows_kernel(float* __restrict__ q, float* __restrict__ k
                                     const float* __restrict__ bq, const float* __restrict__ bk,
                                     const float* __restrict__ bv, const float2* __restrict__ table, uint32_t pos0,
                                     uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, RopeKvShape s) {
+    pdl_wait();  // inputs come from the preceding kernels
     const uint32_t t = blockIdx.y, pos = pos0 + t;
     const uint32_t half = s.head_dim / 2u;
     const uint32_t nq = s.q_heads * half, nk = s.kv_heads * half;
@@ -166,6 +168,7 @@ __global__ void __launch_bounds__(64) attention_prefill_kernel(const float* __re
                                                                const uint16_t* __restrict__ vc, uint32_t pos0,
                                                                uint32_t T, AttnShape s, uint16_t* __restrict__ out,
                                                                unsigned int* err) {
+    pdl_wait();  // inputs come from the preceding kernels
     constexpr int D = 128, GP = GQ == 7 ? 8 : GQ, RQ = 16 / GP, NWARP = 2, PT = 16;
     constexpr uint32_t ROWB = D * 2 + 16;  // bytes per cached row in smem (padding: conflict-free ldmatrix)
     __shared__ __align__(128) uint8_t sm[NWARP][2][2][PT * ROWB];  // [warp][buffer][K, V][position row]
@@ -316,6 +319,7 @@ __device__ __forceinline__ uint16_t silu_mul_bf16(float a, float u) { return f2b
 // and the pointers allow it; otherwise one element at a time.  Same expression per element.
 __global__ void silu_mul_rows_bf16_kernel(const float* __restrict__ g, const float* __restrict__ u, uint64_t n,
                                           uint16_t* __restrict__ out) {
+    pdl_wait();  // inputs come from the preceding kernels
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (uint64_t)gridDim.x * blockDim.x;
     const bool vec = (n % 4u) == 0u && ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u)) & 15u) == 0u &&
                      (reinterpret_cast<uintptr_t>(out) & 7u) == 0u;
@@ -336,6 +340,7 @@ __global__ void silu_mul_rows_bf16_kernel(const float* __restrict__ g, const flo
 // After a batched prefill of positions 0 .. n_prompt-2: the decode graph
 // continues with the last prompt token at its position.
 __global__ void prefill_done_kernel(GreedyState* st, const uint32_t* __restrict__ prompt, uint32_t n_prompt) {
+    pdl_wait();  // the prefill's last kernels may still be writing the cache
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     st->pos = n_prompt - 1u;
     st->token = prompt[n_prompt - 1u];

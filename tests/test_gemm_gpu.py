@@ -234,3 +234,46 @@ def test_gemm_f16x3_near_fp32(fmt, m, n, k, res):
     print("f16x3 gemm %s %dx%dx%d res=%d: rel-L2 %.2e vs fp32 x and W" % (fmt, m, n, k, res, rel))
     assert np.isfinite(yv).all()
     assert rel <= 5e-6
+
+
+def test_prefill_chain_with_launch_overlap_equals_plain():
+    """With launch overlap on (programmatic dependent launch), a kernel may start while the one before
+    it runs; the matvec releases its dependents as it starts.  A chain matvec -> batched RMSNorm to
+    bf16 -> split-K GEMM (+ its reduce) must still read each input only once it is complete: the
+    results equal the plainly launched chain bit for bit, over repeated runs."""
+    m, h, n = 64, 1024, 512
+    sp = G.stream()
+    wm = G.empty_u8(m * h * (h // 256) * 144 + 16)  # matvec weights: m*h rows of k = h
+    A.call("arcllm_cuda_fill_q4k", G.ptr(wm), 0, m * h * (h // 256), 0x5A1, sp)
+    wg = G.empty_u8(n * (h // 256) * 144 + 16)
+    A.call("arcllm_cuda_fill_q4k", G.ptr(wg), 0, n * (h // 256), 0x5A2, sp)
+    gamma = G.empty_f32(h)
+    A.call("arcllm_cuda_fill_normal_f32", G.ptr(gamma), 0, h, 0x5A3, C.c_float(1.0), C.c_float(0.1), sp)
+    xs = [G.empty_f32(h) for _ in range(3)]
+    for i, x in enumerate(xs):
+        A.call("arcllm_cuda_fill_normal_f32", G.ptr(x), 0, h, 0x5B0 + i, C.c_float(0.0), C.c_float(1.0), sp)
+    rows = G.empty_f32(m * h)
+    xb = torch.empty(m * h, dtype=torch.bfloat16, device=G.dev())
+    y = G.empty_f32(m * n)
+
+    def chain(x):
+        A.call("arcllm_cuda_matvec", A.GGML_Q4_K, G.ptr(wm), m * h, h, G.ptr(x), None, C.c_float(0.0), None, None,
+               G.ptr(rows), sp)
+        A.call("arcllm_cuda_rmsnorm_rows", G.ptr(rows), G.ptr(gamma), C.c_float(1e-6), m, h, 0,
+               C.c_void_p(xb.data_ptr()), None, sp)
+        A.call("arcllm_cuda_gemm_bf16", A.GGML_Q4_K, G.ptr(wg), n, h, C.c_void_p(xb.data_ptr()), m, None, G.ptr(y), sp)
+
+    plain = []
+    for x in xs:
+        chain(x)
+        plain.append(G.host(y).copy())
+    A.call("arcllm_cuda_set_launch_overlap", 1)
+    try:
+        for _ in range(3):
+            for x, want in zip(xs, plain):
+                y.fill_(float("nan"))
+                chain(x)
+                assert np.array_equal(G.host(y).view(np.uint32), want.view(np.uint32))
+    finally:
+        A.call("arcllm_cuda_set_launch_overlap", 0)
+    G.check_device_error()
