@@ -15,6 +15,14 @@ namespace arc {
 int set_error(int status, const char* msg);
 int set_cuda_error(cudaError_t e, const char* where);
 
+// Index of the current device in the library's per-device tables (64 slots); -1 when there is no
+// current device or its index is 64 or more (such devices are not supported).
+inline int device_slot() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    return dev;
+}
+
 // Device address of this library's device error word on the current device
 // (nullptr if it cannot be resolved).
 unsigned int* dev_error_word();

@@ -1,6 +1,7 @@
 // extern "C" entry points of libarcllm_cuda.so (declared in include/arcllm_cuda.h).
 // Each one validates its arguments, maps failures to a status code and never
 // lets a C++ exception or a CUDA error escape the ABI.
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -24,14 +25,18 @@ __device__ unsigned int g_dev_error = 0;
 }
 
 unsigned int* dev_error_word() {
-    static unsigned int* cache[64] = {};
+    static std::atomic<unsigned int*> cache[64] = {};  // per device; concurrent first calls store the same value
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-    unsigned int*& slot = cache[dev & 63];
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        void* p = nullptr;  // outside the cache: resolve every time
+        return cudaGetSymbolAddress(&p, g_dev_error) == cudaSuccess ? static_cast<unsigned int*>(p) : nullptr;
+    }
+    unsigned int* slot = cache[dev].load(std::memory_order_acquire);
     if (!slot) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_dev_error) != cudaSuccess) return nullptr;
         slot = static_cast<unsigned int*>(p);
+        cache[dev].store(slot, std::memory_order_release);
     }
     return slot;
 }

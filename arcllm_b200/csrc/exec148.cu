@@ -12,6 +12,7 @@
 //   matvec       shaders/q4_down_exec148_serial.comp:6 (y = W x with the same
 //                w = d*sc*q - dmin*mn per element)
 #include <algorithm>
+#include <atomic>
 
 #include "arcllm_cuda_internal.h"
 #include "common.cuh"
@@ -216,14 +217,16 @@ int exec148_matvec(const void* w, uint32_t rows, uint32_t k, const float* x, con
         return set_error(ARC_E_ALIGNMENT, "matvec EXEC148: image 4-byte, x 16-byte aligned");
     const size_t smem = (size_t)k * 4u + (size_t)(k / 32u) * 4u;
     if (smem > 227u * 1024u) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec EXEC148: K too large");
-    static bool attr_done[64] = {};
+    static std::atomic<bool> attr_done[64] = {};  // concurrent first calls set the same (idempotent) attribute
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
-    if (!attr_done[dev & 63]) {
+    const int slot = device_slot();
+    if (slot < 0) return set_error(ARC_E_CUDA, "matvec EXEC148: no current device below index 64");
+    if (!attr_done[slot].load(std::memory_order_acquire)) {
         const cudaError_t a = cudaFuncSetAttribute(exec148_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    227 * 1024);
         if (a != cudaSuccess) return set_cuda_error(a, "matvec EXEC148 attribute");
-        attr_done[dev & 63] = true;
+        attr_done[slot].store(true, std::memory_order_release);
     }
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const uint32_t per_sm = smem <= 113u * 1024u ? 2u : 1u;

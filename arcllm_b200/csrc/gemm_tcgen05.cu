@@ -702,10 +702,10 @@ GemmScratch g_gemm_scratch[64];
 // Per-device split-K scratch, grown on demand (not while a graph is being
 // captured; split-K launches on one device must not overlap in time).
 int gemm_splitk_reserve(size_t ws_floats, float** ws) {
-    int dev = 0;
-    cudaGetDevice(&dev);
+    const int slot = device_slot();
+    if (slot < 0) return set_error(ARC_E_CUDA, "gemm split-K scratch: no current device below index 64");
     std::lock_guard<std::mutex> lock(g_gemm_mutex);
-    GemmScratch& g = g_gemm_scratch[dev & 63];
+    GemmScratch& g = g_gemm_scratch[slot];
     if (g.ws_floats < ws_floats) {
         float* nws = nullptr;
         cudaError_t e = cudaMalloc(&nws, ws_floats * sizeof(float));

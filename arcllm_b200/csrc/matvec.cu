@@ -33,9 +33,11 @@
 //     order -- results are deterministic -- and runs the epilogue (bias,
 //     residual, or silu(g)*u).
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "arcllm_cuda_internal.h"
@@ -386,13 +388,23 @@ struct DevInfo {
 };
 
 DevInfo dev_info() {
-    static DevInfo cache[64];
+    static DevInfo cache[64];  // per device, queried once (under the mutex)
+    static std::mutex mu;
     int dev = 0;
     cudaGetDevice(&dev);
-    DevInfo& d = cache[dev & 63];
+    const int slot = device_slot();
+    DevInfo d;
+    if (slot >= 0) {
+        std::lock_guard<std::mutex> lock(mu);
+        d = cache[slot];
+    }
     if (d.sms == 0) {
         cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
         cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (slot >= 0) {
+            std::lock_guard<std::mutex> lock(mu);
+            cache[slot] = d;
+        }
     }
     return d;
 }
@@ -415,10 +427,10 @@ cudaError_t set_attr_g() {
 // current device (once).  Also forces the kernels to load, so launches can be
 // captured into CUDA graphs afterwards.
 cudaError_t prepare_all() {
-    static bool done[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (done[dev & 63]) return cudaSuccess;
+    static std::atomic<bool> done[64] = {};  // concurrent first calls set the same (idempotent) attributes
+    const int slot = device_slot();
+    if (slot < 0) return cudaErrorInvalidDevice;
+    if (done[slot].load(std::memory_order_acquire)) return cudaSuccess;
     cudaError_t e = set_attr_g<12, 4, false>();
     if (e == cudaSuccess) e = set_attr_g<12, 8, false>();
     if (e == cudaSuccess) e = set_attr_g<12, 16, false>();
@@ -427,7 +439,7 @@ cudaError_t prepare_all() {
     if (e == cudaSuccess) e = set_attr_g<14, 4, false>();
     if (e == cudaSuccess) e = set_attr_g<14, 8, false>();
     if (e == cudaSuccess) e = set_attr_g<14, 16, false>();
-    if (e == cudaSuccess) done[dev & 63] = true;
+    if (e == cudaSuccess) done[slot].store(true, std::memory_order_release);
     return e;
 }
 

@@ -34,6 +34,7 @@
 // partials in shared memory; the producer warp adds them in a fixed warp
 // order (deterministic) after refilling the stage.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -414,10 +415,10 @@ ImmaConfig imma_config(int fmt, bool dual, uint32_t k) {
 }  // namespace
 
 int matvec_imma_prepare() {
-    static bool done[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (done[dev & 63]) return ARC_OK;
+    static std::atomic<bool> done[64] = {};  // concurrent first calls set the same (idempotent) attributes
+    const int slot = device_slot();
+    if (slot < 0) return set_error(ARC_E_CUDA, "matvec_imma prepare: no current device below index 64");
+    if (done[slot].load(std::memory_order_acquire)) return ARC_OK;
     cudaError_t e = set_attr_imma<12, 1, false>();
     if (e == cudaSuccess) e = set_attr_imma<12, 2, false>();
     if (e == cudaSuccess) e = set_attr_imma<12, 1, true>();
@@ -428,7 +429,7 @@ int matvec_imma_prepare() {
         e = cudaFuncSetAttribute(matvec_imma_multi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kMultiMaxDynSmem);
     if (e != cudaSuccess) return set_cuda_error(e, "matvec_imma prepare");
-    done[dev & 63] = true;
+    done[slot].store(true, std::memory_order_release);
     return ARC_OK;
 }
 
@@ -507,11 +508,15 @@ int imma_params(int fmt, bool dual, const void* w0, const void* w1, uint32_t row
 }
 
 uint32_t imma_sm_count() {
-    static int sm_count[64] = {};  // per device, queried once
+    static std::atomic<int> sm_count[64] = {};  // per device, queried once
+    const int slot = device_slot();
+    int sms = slot >= 0 ? sm_count[slot].load(std::memory_order_relaxed) : 0;
+    if (sms > 0) return (uint32_t)sms;
     int dev = 0;
-    cudaGetDevice(&dev);
-    int& sms = sm_count[dev & 63];
-    if (sms <= 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        sms = 148;
+    if (slot >= 0) sm_count[slot].store(sms, std::memory_order_relaxed);
     return (uint32_t)sms;
 }
 }  // namespace

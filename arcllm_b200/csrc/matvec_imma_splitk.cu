@@ -39,6 +39,7 @@
 // counter on the critical path (measured on B200, the fence + counter close
 // it replaces cost Q6_K 3584 x 18944 18.2 against 16.9 us).
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -582,11 +583,15 @@ KsPlan ks_plan_cached(int fmt, uint32_t rows, uint32_t k, uint32_t sms) {
 }
 
 int ks_sm_count() {
-    static int sm_count[64] = {};
+    static std::atomic<int> sm_count[64] = {};  // per device, queried once
+    const int slot = device_slot();
+    int sms = slot >= 0 ? sm_count[slot].load(std::memory_order_relaxed) : 0;
+    if (sms > 0) return sms;
     int dev = 0;
-    cudaGetDevice(&dev);
-    int& sms = sm_count[dev & 63];
-    if (sms <= 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+        sms = 148;
+    if (slot >= 0) sm_count[slot].store(sms, std::memory_order_relaxed);
     return sms;
 }
 
@@ -632,10 +637,10 @@ int ks_reserve(int fmt, uint32_t rows, uint32_t k) {
     const KsPlan pl = ks_plan_cached(fmt, rows, k, (uint32_t)ks_sm_count());
     if (!pl.ok) return set_error(ARC_E_UNSUPPORTED_SHAPE, "matvec split-K: no plan fits shared memory");
     const size_t need_part = (size_t)pl.q.P * rows;
-    int dev = 0;
-    cudaGetDevice(&dev);
+    const int slot = device_slot();
+    if (slot < 0) return set_error(ARC_E_CUDA, "matvec split-K: no current device below index 64");
     std::lock_guard<std::mutex> lock(g_ks_mutex);
-    KsScratch& sc = g_ks[dev & 63];
+    KsScratch& sc = g_ks[slot];
     if (sc.part_words >= need_part && sc.ctl) return ARC_OK;
     const size_t np = std::max(need_part, sc.part_words);
     unsigned long long* part = nullptr;
@@ -668,15 +673,15 @@ int ks_reserve(int fmt, uint32_t rows, uint32_t k) {
 }
 
 int matvec_splitk_prepare() {
-    static bool done[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (done[dev & 63]) return ARC_OK;
+    static std::atomic<bool> done[64] = {};  // concurrent first calls set the same (idempotent) attributes
+    const int slot = device_slot();
+    if (slot < 0) return set_error(ARC_E_CUDA, "matvec split-K prepare: no current device below index 64");
+    if (done[slot].load(std::memory_order_acquire)) return ARC_OK;
     cudaError_t e = set_attr_ks<12>();
     if (e == cudaSuccess) e = set_attr_ks<14>();
     if (e == cudaSuccess) e = set_attr_ks<ARC_TYPE_EXEC148>();
     if (e != cudaSuccess) return set_cuda_error(e, "matvec split-K prepare");
-    done[dev & 63] = true;
+    done[slot].store(true, std::memory_order_release);
     return ARC_OK;
 }
 
@@ -724,12 +729,12 @@ int matvec_kwindow_launch(int fmt, const void* w, uint32_t rows, uint32_t k, uin
     KMaps maps;
     st = ks_encode_maps(fmt, w, rows, k, pl, &maps);
     if (st != ARC_OK) return st;
-    int dev = 0;
-    cudaGetDevice(&dev);
+    const int slot = device_slot();
+    if (slot < 0) return set_error(ARC_E_CUDA, "matvec split-K: no current device below index 64");
     {
         std::lock_guard<std::mutex> lock(g_ks_mutex);
-        pl.q.part = g_ks[dev & 63].part;
-        pl.q.ctl = g_ks[dev & 63].ctl;
+        pl.q.part = g_ks[slot].part;
+        pl.q.ctl = g_ks[slot].ctl;
     }
     MvParams p{};
     p.w0 = static_cast<const uint8_t*>(w);
